@@ -1,0 +1,129 @@
+// Shared helpers for the duo mixer kernels (sm_100a only).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <string>
+
+#include "../../include/duo_mixer.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
+#error "duo mixer kernels are written for sm_100a only"
+#endif
+
+namespace duo {
+
+// ---------------------------------------------------------------------------------------------------------------
+// host-side error plumbing: every C entry point returns a duo status and records a message for duo_last_error()
+
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+
+#define DUO_CHECK_ARG(cond, msg)                                    \
+  do {                                                              \
+    if (!(cond)) return ::duo::fail(DUO_EINVAL, std::string(msg));  \
+  } while (0)
+
+#define DUO_CUDA_TRY(expr)                                                                                \
+  do {                                                                                                    \
+    cudaError_t _e = (expr);                                                                              \
+    if (_e != cudaSuccess)                                                                                \
+      return ::duo::fail(DUO_ECUDA, std::string(#expr) + ": " + cudaGetErrorString(_e));                 \
+  } while (0)
+
+#define DUO_LAUNCH_CHECK(what)                                                                             \
+  do {                                                                                                    \
+    cudaError_t _e = cudaGetLastError();                                                                  \
+    if (_e != cudaSuccess) return ::duo::fail(DUO_ECUDA, std::string(what) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+#define DUO_TRY(expr)              \
+  do {                             \
+    int _s = (expr);               \
+    if (_s != DUO_OK) return _s;   \
+  } while (0)
+
+inline cudaStream_t as_stream(duo_stream s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool valid_act(int dt) { return dt == DUO_F32 || dt == DUO_BF16; }
+
+inline int cdiv(long a, long b) { return (int)((a + b - 1) / b); }
+
+// number of SMs of the current device (cached per process; one device per process in this library's model)
+int sm_count();
+
+// ---------------------------------------------------------------------------------------------------------------
+// device helpers
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// load 8 consecutive values of T as floats (16-byte aligned for bf16, 32 for f32)
+__device__ __forceinline__ void load8(const float* p, float* o) {
+  float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* o) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float2 f = __bfloat1622float2(h[i]);
+    o[2 * i] = f.x; o[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; i++) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// block-wide sum for blockDim.x a multiple of 32, <= 1024; `red` needs 32 floats of shared memory
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+  return warp_sum(t);
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float siluf_(float x) { return x / (1.f + expf(-x)); }
+// torch's softplus (beta 1, threshold 20) and the reference WGSL's (kernels_qwen35.js:11)
+__device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+// int8 -> f32 for four packed bytes without the I2F pipe: bias each byte to unsigned, place it in the mantissa of
+// 2^23, subtract 2^23 + 128.  Exact for every int8 value.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float* o) {
+  uint32_t u = w ^ 0x80808080u;
+  const float bias = 8388736.f;  // 2^23 + 128
+  o[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - bias;
+  o[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - bias;
+  o[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - bias;
+  o[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - bias;
+}
+
+}  // namespace duo

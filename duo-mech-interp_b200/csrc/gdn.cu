@@ -1,0 +1,250 @@
+// Gated DeltaNet token mixer, part 1: the fused short-conv prologue and the recurrent (token-by-token) scan.
+//
+// Reference: engine/kernels_qwen35.js:129-247 (`conv`, `convState`, `delta`) and, for the arithmetic of its PyTorch
+// path, transformers' Qwen3_5GatedDeltaNet (causal conv1d + SiLU, l2norm of q/k, beta = sigmoid(b),
+// g = -exp(A_log) softplus(a + dt_bias), the delta rule, gated RMSNorm).
+#include <cooperative_groups.h>
+
+#include "kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace duo {
+
+// ---------------------------------------------------------------------------------------------------------------
+// conv prologue.  Block = (128-channel group = one q, k or v head, row, 32-token tile).  Thread c owns channel c of
+// the group: causal depthwise conv (KS = 4) over its inputs with the row's carried state, SiLU, into shared memory;
+// then one warp per token l2-normalises q / k heads (eps 1e-6).  v-head blocks also compute beta and g for their
+// tokens.  The block of tile 0 is the only reader of the old conv state and writes the new one after reading it.
+
+constexpr int CONV_TT = 32, CONV_KS = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(128) gdn_conv_kernel(GdnConvArgs a) {
+  __shared__ float tile[CONV_TT][128 + 4];
+  const int cgp = blockIdx.x, rr = blockIdx.y, t0 = blockIdx.z * CONV_TT;
+  const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
+  const int c = threadIdx.x;
+  const int ch = cgp * 128 + c;
+  const int R = a.row_base + rr;
+  const long m0 = (long)rr * a.t;
+  const T* y = static_cast<const T*>(a.y);
+  const int tn = min(CONV_TT, a.t - t0);
+
+  float w[CONV_KS];
+#pragma unroll
+  for (int i = 0; i < CONV_KS; i++) w[i] = a.conv_w[(long)ch * CONV_KS + i];
+  float* st = a.conv_state + ((long)R * (CONV_KS - 1)) * conv_dim + ch;  // st[j * conv_dim], j = 0 oldest
+  // inputs at tokens t0-3 .. t0-1
+  float win[CONV_KS - 1];
+#pragma unroll
+  for (int i = 0; i < CONV_KS - 1; i++) {
+    const int tt = t0 - (CONV_KS - 1) + i;
+    win[i] = tt >= 0 ? to_f(y[(m0 + tt) * a.w + ch]) : st[(long)((CONV_KS - 1) + tt) * conv_dim];
+  }
+  if (blockIdx.z == 0) {
+    // new state = last KS-1 inputs of (old state ++ this call's inputs)
+    float ns[CONV_KS - 1];
+#pragma unroll
+    for (int j = 0; j < CONV_KS - 1; j++) {
+      const int idx = a.t + j;  // index into old ++ new
+      ns[j] = idx < CONV_KS - 1 ? win[idx] : to_f(y[(m0 + idx - (CONV_KS - 1)) * a.w + ch]);
+    }
+#pragma unroll
+    for (int j = 0; j < CONV_KS - 1; j++) st[(long)j * conv_dim] = ns[j];
+  }
+  for (int i = 0; i < tn; i++) {
+    const float x = to_f(y[(m0 + t0 + i) * a.w + ch]);
+    const float acc = w[0] * win[0] + w[1] * win[1] + w[2] * win[2] + w[3] * x;
+    tile[i][c] = siluf_(acc);
+    win[0] = win[1];
+    win[1] = win[2];
+    win[2] = x;
+  }
+  __syncthreads();
+  const bool norm = cgp < 2 * a.hk;  // q and k heads are l2-normalised; v heads pass through
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  T* out = static_cast<T*>(a.qkv_out);
+  for (int i = warp; i < tn; i += 4) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) v[j] = tile[i][lane * 4 + j];
+    if (norm) {
+      float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss + 1e-6f);
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[j] *= inv;
+    }
+    T* o = out + (m0 + t0 + i) * conv_dim + cgp * 128 + lane * 4;
+#pragma unroll
+    for (int j = 0; j < 4; j++) o[j] = from_f<T>(v[j]);
+  }
+  if (!norm && c < tn) {
+    const int h = cgp - 2 * a.hk;
+    const long m = m0 + t0 + c;
+    const long base = m * a.w + conv_dim + a.hv * a.dv;
+    const float b = to_f(y[base + h]);
+    const float av = to_f(y[base + a.hv + h]);
+    a.beta_out[m * a.hv + h] = sigmoidf_(b);
+    a.g_out[m * a.hv + h] = -expf(a.a_log[h]) * softplusf_(av + a.dt_bias[h]);
+  }
+}
+
+int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
+  if (a.rows == 0 || a.t == 0) return DUO_OK;
+  if (a.dk != 128 || a.dv != 128 || a.ks != CONV_KS) return fail(DUO_EINVAL, "gdn_conv: needs dk = dv = 128, ks = 4");
+  const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
+  dim3 grid(conv_dim / 128, a.rows, cdiv(a.t, CONV_TT));
+  if (dtype == DUO_F32) gdn_conv_kernel<float><<<grid, 128, 0, st>>>(a);
+  else gdn_conv_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a);
+  DUO_LAUNCH_CHECK("gdn_conv_kernel");
+  return DUO_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// recurrent scan.  One thread-block cluster of CS CTAs per (row, value head); CTA s owns state columns
+// [s * 128 / CS, (s + 1) * 128 / CS) -- the delta rule is independent per state column -- and all 128 state rows.
+// Thread (rg, jj) keeps rows rg * RPT .. rg * RPT + RPT - 1 of column jj in registers for the whole call.
+// Per token: S *= exp(g); u = S^T k; S += k (beta (v - u))^T; o = S^T (q / sqrt(dk)), then (engine path) the gated
+// RMSNorm over the head's 128 outputs, whose sum of squares is reduced across the cluster through distributed
+// shared memory.
+
+template <typename T, int CS, bool NORM>
+__global__ void __cluster_dims__(CS, 1, 1) __launch_bounds__(128) gdn_recurrent_kernel(GdnScanArgs a) {
+  constexpr int CW = 128 / CS;   // columns per CTA
+  constexpr int RPT = 128 / CS;  // state rows per thread (CS threads share a column)
+  __shared__ float qs[128], ks[128];
+  __shared__ float red_u[CS][CW], red_o[CS][CW];
+  __shared__ float red32[32];
+  __shared__ float part[2];
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int jj = tid % CW, rg = tid / CW;
+  const int j = s * CW + jj;
+  const int kh = h / (a.h / a.hq);
+  float* S = a.state + (((long)(a.state_row0 + b) * a.h + h) * 128) * 128;
+  float st[RPT];
+#pragma unroll
+  for (int r = 0; r < RPT; r++) st[r] = S[(long)(rg * RPT + r) * 128 + j];
+  const T* qp = static_cast<const T*>(a.q);
+  const T* kp = static_cast<const T*>(a.k);
+  const T* vp = static_cast<const T*>(a.v);
+  T* op = static_cast<T*>(a.o);
+  const float qscale = rsqrtf(128.f);
+  cg::cluster_group cluster = cg::this_cluster();
+
+  for (int t = 0; t < a.t; t++) {
+    const long m = (long)b * a.t + t;
+    float qv = to_f(qp[m * a.q_stride + kh * 128 + tid]);
+    float kv = to_f(kp[m * a.k_stride + kh * 128 + tid]);
+    if (a.l2norm_qk) {
+      const float sq = block_sum(qv * qv, red32);
+      const float sk = block_sum(kv * kv, red32);
+      qv *= rsqrtf(sq + 1e-6f);
+      kv *= rsqrtf(sk + 1e-6f);
+    }
+    __syncthreads();  // previous token's readers of qs / ks / red_* are done
+    qs[tid] = qv * qscale;
+    ks[tid] = kv;
+    const float gt = a.g[m * a.h + h];
+    const float bt = a.beta[m * a.h + h];
+    __syncthreads();
+    const float dec = expf(gt);
+    float pu = 0.f;
+#pragma unroll
+    for (int r = 0; r < RPT; r++) {
+      st[r] *= dec;
+      pu = fmaf(st[r], ks[rg * RPT + r], pu);
+    }
+    red_u[rg][jj] = pu;
+    __syncthreads();
+    float u = 0.f;
+#pragma unroll
+    for (int i = 0; i < CS; i++) u += red_u[i][jj];
+    const float vj = to_f(vp[m * a.v_stride + h * 128 + j]);
+    const float d = bt * (vj - u);
+    float po = 0.f;
+#pragma unroll
+    for (int r = 0; r < RPT; r++) {
+      st[r] = fmaf(ks[rg * RPT + r], d, st[r]);
+      po = fmaf(st[r], qs[rg * RPT + r], po);
+    }
+    red_o[rg][jj] = po;
+    __syncthreads();
+    float o = 0.f;
+#pragma unroll
+    for (int i = 0; i < CS; i++) o += red_o[i][jj];
+    if (NORM) {
+      // sum of o^2 over this CTA's columns (rows rg == 0 hold each column once), then over the cluster
+      const float ss = block_sum(rg == 0 ? o * o : 0.f, red32);
+      if (tid == 0) part[t & 1] = ss;
+      cluster.sync();
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < CS; i++) tot += *cluster.map_shared_rank(&part[t & 1], i);
+      const float rms = rsqrtf(tot / 128.f + a.eps);
+      if (rg == 0) {
+        const float z = to_f(static_cast<const T*>(a.z)[m * a.z_stride + h * 128 + j]);
+        const float hs = a.head_scale ? a.head_scale[h] : 1.f;
+        op[m * a.o_stride + h * 128 + j] = from_f<T>(o * rms * a.norm_w[j] * siluf_(z) * hs);
+      }
+    } else if (rg == 0) {
+      op[m * a.o_stride + h * 128 + j] = from_f<T>(o);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RPT; r++) S[(long)(rg * RPT + r) * 128 + j] = st[r];
+  if (NORM) cluster.sync();  // peers may still read this CTA's `part`
+}
+
+template <typename T, bool NORM>
+static int run_recurrent(const GdnScanArgs& a, cudaStream_t st) {
+  const long pairs = (long)a.b * a.h;
+  // 8 column slices while the (row, head) pairs alone cannot fill the GPU, else 4 (32 state rows per thread)
+  if (pairs <= 64) gdn_recurrent_kernel<T, 8, NORM><<<dim3(8, a.h, a.b), 128, 0, st>>>(a);
+  else gdn_recurrent_kernel<T, 4, NORM><<<dim3(4, a.h, a.b), 128, 0, st>>>(a);
+  DUO_LAUNCH_CHECK("gdn_recurrent_kernel");
+  return DUO_OK;
+}
+
+int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st) {
+  if (a.b == 0 || a.t == 0) return DUO_OK;
+  if (a.dk != 128 || a.dv != 128) return fail(DUO_EINVAL, "gdn: needs dk = dv = 128");
+  if (a.hq <= 0 || a.h % a.hq) return fail(DUO_EINVAL, "gdn: value heads must be a multiple of q/k heads");
+  const bool norm = a.norm_w != nullptr;
+  if (dtype == DUO_F32) return norm ? run_recurrent<float, true>(a, st) : run_recurrent<float, false>(a, st);
+  return norm ? run_recurrent<__nv_bfloat16, true>(a, st) : run_recurrent<__nv_bfloat16, false>(a, st);
+}
+
+static int check_gdn_op(const void* q, const void* k, const void* v, int in_dtype, const float* g, const float* beta,
+                        float* state, void* o, int o_dtype, int b, int t, int h, int dk, int dv) {
+  DUO_CHECK_ARG(b >= 0 && t >= 0 && h > 0, "gdn: bad shape");
+  DUO_CHECK_ARG(dk == 128 && dv == 128, "gdn: dk and dv must be 128");
+  DUO_CHECK_ARG(valid_act(in_dtype) && o_dtype == in_dtype, "gdn: q/k/v/o dtype must be f32 or bf16 (the same)");
+  DUO_CHECK_ARG(b == 0 || t == 0 || (q && k && v && g && beta && state && o), "gdn: null pointer");
+  return DUO_OK;
+}
+
+GdnScanArgs op_scan_args(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                         float* state, void* o, int b, int t, int h, int l2norm_qk) {
+  GdnScanArgs a{};
+  a.q = q; a.k = k; a.v = v;
+  a.q_stride = a.k_stride = a.v_stride = a.o_stride = (long)h * 128;
+  a.g = g; a.beta = beta; a.state = state; a.state_row0 = 0; a.o = o;
+  a.b = b; a.t = t; a.hq = h; a.h = h; a.dk = 128; a.dv = 128;
+  a.l2norm_qk = l2norm_qk;
+  return a;
+}
+
+}  // namespace duo
+
+using namespace duo;
+
+extern "C" int duo_gdn_recurrent_fwd(const void* q, const void* k, const void* v, int in_dtype, const float* g,
+                                     const float* beta, float* state, void* o, int o_dtype, int b, int t, int h,
+                                     int dk, int dv, int l2norm_qk, duo_stream stream) {
+  DUO_TRY(check_gdn_op(q, k, v, in_dtype, g, beta, state, o, o_dtype, b, t, h, dk, dv));
+  return launch_gdn_recurrent(op_scan_args(q, k, v, g, beta, state, o, b, t, h, l2norm_qk), in_dtype,
+                              as_stream(stream));
+}

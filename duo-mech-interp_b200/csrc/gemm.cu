@@ -1,0 +1,409 @@
+// Projections of the forward: the bf16 tensor-core GEMM (tcgen05 + TMA + TMEM) and the f32 CUDA-core GEMM on int8
+// weights used by the f32 engine.  Both compute acc[m, n] = sum_k A[m, k] W[n, k] and hand it to one of the
+// epilogues of GemmEpi (plain store, residual add with the optional steering vector, SwiGLU with neuron pushes).
+//
+// The reference computes these products with `matvec` / `matmul` (engine/kernels.js:55-151) in f32 on int8 weights
+// dequantised per 128-group; model.js:382-396 picks between them by row count.
+#include <algorithm>
+#include <mutex>
+
+#include "kernels.cuh"
+#include "tc.cuh"
+
+namespace duo {
+
+__device__ unsigned g_tc_fault;
+
+// ---------------------------------------------------------------------------------------------------------------
+// epilogue helpers shared by both GEMMs
+
+__device__ __forceinline__ float push_apply(const PushTable& pt, int r, int n, float v) {
+  for (int i = 0; i < pt.count; i++) {
+    const int pn = pt.neuron[i];
+    if (pn == DUO_ALL_NEURONS || pn == n) {
+      const float val = pt.vals[(long)i * pt.rows + r];
+      v = pt.mode[i] == DUO_PUSH_MUL ? v * val : v + val;
+    }
+  }
+  return v;
+}
+
+// 32 consecutive accumulator columns n0 .. n0 + 31 of output row m (already scaled), for STORE / ADD
+__device__ __forceinline__ void epi_row32(const GemmEpiArgs& ep, int m, int n0, int N, const float* v) {
+  const long off = (long)m * ep.ldc + n0;
+  const bool full = n0 + 32 <= N;
+  if (ep.epi == EPI_STORE) {
+    if (ep.c_dtype == DUO_BF16) {
+      __nv_bfloat16* c = static_cast<__nv_bfloat16*>(ep.c) + off;
+      if (full && (((uintptr_t)c) & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) store8(c + j, v + j);
+      } else {
+        for (int j = 0; j < 32 && n0 + j < N; j++) c[j] = __float2bfloat16_rn(v[j]);
+      }
+    } else {
+      float* c = static_cast<float*>(ep.c) + off;
+      if (full && (((uintptr_t)c) & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) store8(c + j, v + j);
+      } else {
+        for (int j = 0; j < 32 && n0 + j < N; j++) c[j] = v[j];
+      }
+    }
+  } else {  // EPI_ADD_F32
+    float* x = static_cast<float*>(ep.c) + off;
+    const float* vr = ep.vec ? ep.vec + (long)(ep.row_base + m / ep.t) * ep.ldc + n0 : nullptr;
+    if (full && (((uintptr_t)x) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 o = *reinterpret_cast<float4*>(x + j);
+        o.x += v[j]; o.y += v[j + 1]; o.z += v[j + 2]; o.w += v[j + 3];
+        if (vr) {
+          const float4 a = *reinterpret_cast<const float4*>(vr + j);
+          o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
+        }
+        *reinterpret_cast<float4*>(x + j) = o;
+      }
+    } else {
+      for (int j = 0; j < 32 && n0 + j < N; j++) x[j] += v[j] + (vr ? vr[j] : 0.f);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// tcgen05 GEMM.  CTA tile 128 x BN, K step 64 (one 128-byte swizzle row of bf16), STAGES-deep TMA ring.
+// Warp 0: TMA producer (one lane).  Warp 1: TMEM allocator and MMA issuer (one lane).  Warps 2-5: epilogue, one
+// accumulator row (TMEM lane) per thread, read 32 columns at a time.
+
+constexpr int TC_BM = 128, TC_BK = 64, TC_THREADS = 192;
+
+template <int BN> struct TcCfg {
+  static constexpr int A_BYTES = TC_BM * TC_BK * 2;
+  static constexpr int B_BYTES = BN * TC_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, int M, int N,
+                   int K, GemmEpiArgs ep, unsigned* fault) {
+  using C = TcCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tmem_full = empty + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_n = blockIdx.x * BN, tile_m = blockIdx.y * TC_BM;
+  const int num_k = K / TC_BK;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < C::STAGES; s++) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(tmem_full, 1);
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tma_a);
+    tc::prefetch_tmap(&tma_b);
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, BN);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    for (int kb = 0; kb < num_k; kb++) {
+      const int s = kb % C::STAGES;
+      const uint32_t ph = (kb / C::STAGES) & 1;
+      if (kb >= C::STAGES && !tc::mbar_wait(&empty[s], ph ^ 1)) {
+        atomicOr(fault, 1u);
+        s_abort = 1;
+        break;
+      }
+      tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+      tc::tma_load_2d(sa + s * C::A_BYTES, &tma_a, kb * TC_BK, tile_m, &full[s]);
+      tc::tma_load_2d(sb + s * C::B_BYTES, &tma_b, kb * TC_BK, tile_n, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = tc::idesc_bf16_f32(TC_BM, BN);
+    bool ok = true;
+    for (int kb = 0; kb < num_k; kb++) {
+      const int s = kb % C::STAGES;
+      const uint32_t ph = (kb / C::STAGES) & 1;
+      if (!tc::mbar_wait(&full[s], ph)) {
+        atomicOr(fault, 2u);
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      const uint32_t a0 = tc::smem_u32(sa + s * C::A_BYTES), b0 = tc::smem_u32(sb + s * C::B_BYTES);
+#pragma unroll
+      for (int k = 0; k < TC_BK / 16; k++) {
+        tc::mma_bf16(tmem, tc::desc_kmajor_sw128(a0 + k * 32), tc::desc_kmajor_sw128(b0 + k * 32), idesc,
+                     (kb | k) != 0);
+      }
+      tc::mma_commit(&empty[s]);
+    }
+    if (ok) tc::mma_commit(tmem_full);
+    else s_abort = 1;
+  } else if (warp >= 2) {
+    const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31 belong to this warp
+    const int m = tile_m + quad * 32 + lane;
+    const bool ok = tc::mbar_wait(tmem_full, 0);
+    if (!ok) {
+      if (lane == 0) atomicOr(fault, 4u);
+    } else {
+      tc::fence_after_sync();
+      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+      if (EPI == EPI_SWIGLU) {
+        // columns [0, 128) are gate rows j0 .. j0+127 and [128, 256) the matching up rows (BN == 256)
+        const int j0 = tile_n / 2;
+        const int inter = N / 2;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+          float g[32], u[32];
+          tc::tmem_ld32(trow + c0, g);
+          tc::tmem_ld32(trow + BN / 2 + c0, u);
+          if (m < M) {
+            const int r = ep.row_base + m / ep.t;
+            float a[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              const float gs = ep.colscale ? g[j] * ep.colscale[tile_n + c0 + j] : g[j];
+              const float us = ep.colscale ? u[j] * ep.colscale[tile_n + BN / 2 + c0 + j] : u[j];
+              a[j] = siluf_(gs) * us;
+            }
+            if (ep.push.count) {
+              for (int j = 0; j < 32; j++) a[j] = push_apply(ep.push, r, j0 + c0 + j, a[j]);
+            }
+            __nv_bfloat16* out = static_cast<__nv_bfloat16*>(ep.c) + (long)m * ep.ldc + j0 + c0;
+            if (j0 + c0 + 32 <= inter) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) store8(out + j, a + j);
+            } else {
+              for (int j = 0; j < 32 && j0 + c0 + j < inter; j++) out[j] = __float2bfloat16_rn(a[j]);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          float v[32];
+          tc::tmem_ld32(trow + c0, v);
+          if (m < M && tile_n + c0 < N) {
+            if (ep.colscale) {
+#pragma unroll
+              for (int j = 0; j < 32; j++) v[j] *= (tile_n + c0 + j < N) ? ep.colscale[tile_n + c0 + j] : 0.f;
+            }
+            epi_row32(ep, m, tile_n + c0, N, v);
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, BN);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// host side
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+int make_tmap_bf16(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_rows, int box_cols) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16)
+    return fail(DUO_EINVAL, "tensor map: base must be 16-byte aligned and rows a multiple of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return DUO_OK;
+}
+
+unsigned* tc_fault_ptr() {
+  static unsigned* ptr = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tc_fault) == cudaSuccess) ptr = static_cast<unsigned*>(p);
+  });
+  return ptr;
+}
+
+int tc_fault_read_clear(unsigned* out) {
+  unsigned v = 0, zero = 0;
+  DUO_CUDA_TRY(cudaDeviceSynchronize());
+  DUO_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tc_fault, sizeof(v)));
+  DUO_CUDA_TRY(cudaMemcpyToSymbol(g_tc_fault, &zero, sizeof(zero)));
+  *out = v;
+  return DUO_OK;
+}
+
+template <int BN, int EPI>
+static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, int k, const GemmEpiArgs& ep,
+                  cudaStream_t st) {
+  using C = TcCfg<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    DUO_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_set = true;
+  }
+  unsigned* fault = tc_fault_ptr();
+  if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
+  dim3 grid(cdiv(n, BN), cdiv(m, TC_BM));
+  gemm_tc_kernel<BN, EPI><<<grid, TC_THREADS, C::SMEM, st>>>(ta, tb, m, n, k, ep, fault);
+  DUO_LAUNCH_CHECK("gemm_tc_kernel");
+  return DUO_OK;
+}
+
+int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, const GemmEpiArgs& ep, cudaStream_t st) {
+  if (m == 0 || n == 0) return DUO_OK;
+  DUO_CHECK_ARG(k % TC_BK == 0, "gemm_tc: k must be a multiple of 64");
+  // choose the widest N tile that still gives every SM work; SwiGLU needs 256 (gate/up interleaved per 128)
+  int bn = 256;
+  if (ep.epi != EPI_SWIGLU) {
+    const long tiles_m = cdiv(m, TC_BM);
+    if (tiles_m * cdiv(n, 256) < sm_count()) bn = 128;
+    if (tiles_m * cdiv(n, 128) < sm_count()) bn = 64;
+  } else {
+    DUO_CHECK_ARG(n % 256 == 0, "gemm_tc: SwiGLU epilogue needs n a multiple of 256");
+  }
+  CUtensorMap ta, tb;
+  DUO_TRY(make_tmap_bf16(&ta, a, m, k, k, TC_BM, TC_BK));
+  DUO_TRY(make_tmap_bf16(&tb, b, n, k, k, bn, TC_BK));
+  if (ep.epi == EPI_SWIGLU) return run_tc<256, EPI_SWIGLU>(ta, tb, m, n, k, ep, st);
+  if (ep.epi == EPI_ADD_F32) {
+    if (bn == 256) return run_tc<256, EPI_ADD_F32>(ta, tb, m, n, k, ep, st);
+    if (bn == 128) return run_tc<128, EPI_ADD_F32>(ta, tb, m, n, k, ep, st);
+    return run_tc<64, EPI_ADD_F32>(ta, tb, m, n, k, ep, st);
+  }
+  if (bn == 256) return run_tc<256, EPI_STORE>(ta, tb, m, n, k, ep, st);
+  if (bn == 128) return run_tc<128, EPI_STORE>(ta, tb, m, n, k, ep, st);
+  return run_tc<64, EPI_STORE>(ta, tb, m, n, k, ep, st);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// f32 CUDA-core GEMM on int8 weights (the f32 engine; the reference's precision).  64 x 64 tiles, K step 32,
+// 256 threads with 4 x 4 outputs each; weights dequantised (f32(q) * scale) while staging into shared memory.
+
+__global__ void __launch_bounds__(256) gemm_f32_q8_kernel(const float* __restrict__ A, int M, int K,
+                                                           const int8_t* __restrict__ W, const float* __restrict__ S,
+                                                           int group, int N, GemmEpiArgs ep) {
+  __shared__ float As[32][64 + 4];
+  __shared__ float Ws[32][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  const int groups = K / group;
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    for (int e = threadIdx.x; e < 64 * 32; e += 256) {
+      const int r = e >> 5, kk = e & 31;
+      const int gm = m0 + r, gn = n0 + r;
+      As[kk][r] = gm < M ? A[(long)gm * K + k0 + kk] : 0.f;
+      Ws[kk][r] = gn < N ? (float)W[(long)gn * K + k0 + kk] * S[(long)gn * groups + (k0 + kk) / group] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < 32; kk++) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) { a[i] = As[kk][ty * 4 + i]; b[i] = Ws[kk][tx * 4 + i]; }
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= N) continue;
+      float v = acc[i][j] * (ep.colscale ? ep.colscale[n] : 1.f);
+      const long off = (long)m * ep.ldc + n;
+      if (ep.epi == EPI_STORE) {
+        if (ep.c_dtype == DUO_F32) static_cast<float*>(ep.c)[off] = v;
+        else static_cast<__nv_bfloat16*>(ep.c)[off] = __float2bfloat16_rn(v);
+      } else {
+        float* x = static_cast<float*>(ep.c);
+        if (ep.vec) v += ep.vec[(long)(ep.row_base + m / ep.t) * ep.ldc + n];
+        x[off] += v;
+      }
+    }
+  }
+}
+
+int launch_gemm_f32_q8(const float* a, int m, int k, const int8_t* q, const float* s, int group, int n,
+                       const GemmEpiArgs& ep, cudaStream_t st) {
+  if (m == 0 || n == 0) return DUO_OK;
+  DUO_CHECK_ARG(k % 32 == 0, "gemm_f32: k must be a multiple of 32");
+  DUO_CHECK_ARG(ep.epi == EPI_STORE || ep.epi == EPI_ADD_F32, "gemm_f32: store or add epilogue only");
+  gemm_f32_q8_kernel<<<dim3(cdiv(n, 64), cdiv(m, 64)), 256, 0, st>>>(a, m, k, q, s, group, n, ep);
+  DUO_LAUNCH_CHECK("gemm_f32_q8_kernel");
+  return DUO_OK;
+}
+
+}  // namespace duo
+
+using namespace duo;
+
+extern "C" int duo_gemm_bf16(const void* a, int m, int k, const void* b, int n, const float* col_scale, void* c,
+                             int c_dtype, int ldc, int accumulate, duo_stream stream) {
+  DUO_CHECK_ARG(m >= 0 && n >= 0 && k > 0, "gemm_bf16: bad shape");
+  DUO_CHECK_ARG(k % 64 == 0, "gemm_bf16: k must be a multiple of 64");
+  DUO_CHECK_ARG(m == 0 || n == 0 || (a && b && c), "gemm_bf16: null pointer");
+  DUO_CHECK_ARG(valid_act(c_dtype), "gemm_bf16: c dtype must be f32 or bf16");
+  DUO_CHECK_ARG(ldc >= n, "gemm_bf16: ldc < n");
+  DUO_CHECK_ARG(!accumulate || c_dtype == DUO_F32, "gemm_bf16: accumulate needs an f32 C");
+  GemmEpiArgs ep;
+  ep.epi = accumulate ? EPI_ADD_F32 : EPI_STORE;
+  ep.c = c;
+  ep.c_dtype = c_dtype;
+  ep.ldc = ldc;
+  ep.colscale = col_scale;
+  return launch_gemm_tc(a, m, k, b, n, ep, as_stream(stream));
+}
+
+extern "C" int duo_fault_status(unsigned* out) {
+  DUO_CHECK_ARG(out, "fault_status: null pointer");
+  return tc_fault_read_clear(out);
+}

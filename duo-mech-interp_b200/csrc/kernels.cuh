@@ -1,0 +1,133 @@
+// Host-side launchers shared between the kernel files and the engine.  All are stream-ordered and return a duo
+// status; none allocates memory.
+#pragma once
+#include "common.cuh"
+
+namespace duo {
+
+// Push records of one layer (device arrays): neuron (DUO_ALL_NEURONS for all), mode (DUO_PUSH_ADD / MUL) and one
+// value per engine row, vals[i * rows + r].
+struct PushTable {
+  const int32_t* neuron;
+  const int32_t* mode;
+  const float* vals;
+  int count;
+  int rows;
+};
+
+// Epilogues of the tensor-core GEMM.
+enum GemmEpi {
+  EPI_STORE = 0,   // C[m, n] = acc * colscale[n]                   (bf16 or f32 C)
+  EPI_ADD_F32 = 1, // X[m, n] += acc * colscale[n] (+ vec[row(m), n])  (f32 residual stream)
+  EPI_SWIGLU = 2   // gate/up interleaved per 128 columns: A[m, j] = silu(g) * u, then pushes   (bf16 A)
+};
+
+struct GemmEpiArgs {
+  int epi = EPI_STORE;
+  void* c = nullptr;            // output (STORE: C; ADD: X f32; SWIGLU: A)
+  int c_dtype = DUO_BF16;
+  int ldc = 0;                  // leading dim of the output in elements
+  const float* colscale = nullptr;
+  const float* vec = nullptr;   // ADD: optional per-row vector table [rows_total, n]
+  int t = 1, row_base = 0;      // row(m) = row_base + m / t
+  PushTable push{};             // SWIGLU
+};
+
+int launch_gemv(const void* x, int x_dtype, int m, int k, const int8_t* q, const float* s, int group, int n, void* y,
+                int y_dtype, int accumulate, cudaStream_t st);
+int launch_gather(const int32_t* ids, int t, const int8_t* q, const float* s, int group, int k, int vocab, float* y,
+                  cudaStream_t st);
+int launch_dequant(const int8_t* q, const float* s, int n, int k, int group, void* out, int out_dtype,
+                   cudaStream_t st);
+
+// bf16 tensor-core GEMM: acc[m, n] = A[m, k] . B[n, k]^T, then the epilogue
+int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, const GemmEpiArgs& ep, cudaStream_t st);
+// f32 CUDA-core GEMM on int8 weights (the f32 engine): acc = A[m, k] . dequant(W)[n, k]^T, then the epilogue
+int launch_gemm_f32_q8(const float* a, int m, int k, const int8_t* q, const float* s, int group, int n,
+                       const GemmEpiArgs& ep, cudaStream_t st);
+
+int launch_rmsnorm(const float* x, int m, int d, const float* w, float eps, int offset, void* y, int y_dtype,
+                   cudaStream_t st);
+int launch_swiglu_push(const void* gu, int m, int inter, int t, int row_base, const PushTable& pt, void* a, int dtype,
+                       cudaStream_t st);
+int launch_vec_add(float* x, int m, int h, int t, int row_base, const float* vec, cudaStream_t st);
+int launch_argmax(const float* logits, int m, int v, int32_t* out, cudaStream_t st);
+int launch_finish_rows(const float* x, int h, int t, int row_base, int rows, float* last, int32_t* len,
+                       cudaStream_t st);
+int launch_feed_tokens(const int32_t* am, int rows, int32_t* ids, int32_t* log, int n_steps, int step,
+                       cudaStream_t st);
+
+// ---- Gated DeltaNet
+struct GdnConvArgs {
+  const void* y;          // fused projection [M, w] = [qkv (conv_dim) | z (vd) | b (hv) | a (hv)]
+  int w;                  // its row width
+  const float* conv_w;    // [conv_dim, ks]
+  float* conv_state;      // [rows_total, ks - 1, conv_dim]
+  const float* a_log;
+  const float* dt_bias;
+  void* qkv_out;          // [M, conv_dim]: l2-normalised q, k (q not yet scaled) and v
+  float* g_out;           // [M, hv]
+  float* beta_out;        // [M, hv]
+  int hk, hv, dk, dv, ks;
+  int rows, t, row_base;
+};
+int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st);
+
+struct GdnScanArgs {
+  const void* q; const void* k; const void* v;
+  long q_stride, k_stride, v_stride;  // elements between consecutive tokens
+  const float* g; const float* beta;  // [M, h]
+  float* state;                       // [b_total, h, dk, dv]; this call uses rows state_row0 ..
+  int state_row0;
+  void* o; long o_stride;
+  int b, t, hq, h, dk, dv;            // hq = heads of q/k (h / hq value heads share one q/k head)
+  int l2norm_qk;
+  // optional fused gated RMSNorm + head scale (the engine path): o = o * rms * w * silu(z) * hs[h]
+  const void* z; long z_stride;
+  const float* norm_w; const float* head_scale; float eps;
+};
+int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st);
+int launch_gdn_chunk(const GdnScanArgs& a, int dtype, cudaStream_t st);
+
+// ---- gated attention
+struct AttnPrepArgs {
+  const void* y;              // fused projection [M, w] = [q+gate (nh * 2hd) | k | v]
+  int w;
+  const float* q_norm; const float* k_norm;
+  const float* inv_freq;      // [rot / 2]
+  const int32_t* len;         // per engine row: tokens already in the cache
+  void* q_out;                // [M, nh, hd]
+  void* kc; void* vc;         // [rows_total, max_len, nkv, hd]
+  int nh, nkv, hd, rot, max_len, rows, t, row_base;
+  float eps;
+};
+int launch_attn_prep(const AttnPrepArgs& a, int dtype, cudaStream_t st);
+
+struct AttnArgs {
+  const void* q;              // [b, t, nh, hd]
+  const void* kc; const void* vc;  // [b_total, max_len, nkv, hd], rows cache_row0 ..
+  int cache_row0;
+  const int32_t* start;       // per cache row: position of this call's first query (NULL: from len - t)
+  const int32_t* len;         // alternative: per cache row tokens held after the prep (start = len - t)
+  const void* gate; long gate_stride;  // optional sigmoid gate: head h of token tok at gate + tok * gate_stride
+  long gate_hstride;                   //   + h * gate_hstride
+
+  void* o;                    // [b, t, nh, hd]
+  int b, t, nh, nkv, hd, max_len;
+  float scale;
+  float* work;                // split-K scratch for decode (may be NULL: no split)
+  long work_floats;
+};
+int launch_attention(const AttnArgs& a, int dtype, cudaStream_t st);
+long attn_work_floats(int b, int nh, int max_len);
+
+// int8 -> bf16 copy of a weight matrix for the tensor-core GEMM: dst row of src row n is n, or (interleave > 0) the
+// gate/up interleaved order [gate 128 | up 128]* with `interleave` = rows of each half.  apply_scale = 0 writes
+// bf16(q) exactly (the per-row scale then goes to the GEMM's column scale).
+int launch_pack_bf16(const int8_t* q, const float* s, int n, int k, int group, int interleave, int apply_scale,
+                     __nv_bfloat16* out, float* colscale_out, cudaStream_t st);
+
+GdnScanArgs op_scan_args(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                         float* state, void* o, int b, int t, int h, int l2norm_qk);
+
+}  // namespace duo

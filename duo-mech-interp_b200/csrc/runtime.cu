@@ -1,0 +1,36 @@
+// Error plumbing and device queries shared by every C entry point.
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace duo {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+int sm_count() {
+  static int cached = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      cached = n;
+    else
+      cached = 148;
+  }
+  return cached;
+}
+
+}  // namespace duo
+
+extern "C" const char* duo_last_error(void) { return duo::g_last_error.c_str(); }
+
+extern "C" int duo_abi_version(void) { return 1; }

@@ -1,0 +1,166 @@
+"""`Model`: the host-side mirror of the reference engine's Model class (engine/model.js:26-509).
+
+Same operations and argument meaning: alloc(rows, maxLen, maxT), reset(r), setVectors(rows), setHeadScales,
+_forward(ids, rowBase, rows, T, opts) with opts = {pushes: {layer: [{n, mode, vals}]}, vec: layer}, prefill(r, ids,
+opts) chunked by maxT, step(ids, opts), logitsRow(r), logitsAll(), argmaxAll().  Names are snake_case; errors raise
+(the reference throws, model.js:52, 406, 418).  All compute runs in libduo_mixer.so; this file only moves arguments.
+"""
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import lib as L
+from .config import Config
+from .weights import Weights
+
+
+class Model:
+    def __init__(self, cfg: Config, weights: Weights, stream=None):
+        self.cfg = cfg
+        self.weights = weights
+        self.stream = stream
+        c = cfg
+        full = (C.c_uint8 * c.num_hidden_layers)(*[1 if c.is_full(l) else 0 for l in range(c.num_hidden_layers)])
+        self._c = L.duo_config(
+            hidden=c.hidden_size, inter=c.intermediate_size, vocab=c.vocab_size, layers=c.num_hidden_layers,
+            nh=c.num_attention_heads, nkv=c.num_key_value_heads, hd=c.head_dim, rot=c.rot, theta=c.rope_theta,
+            eps=c.rms_norm_eps, hk=c.linear_num_key_heads, hv=c.linear_num_value_heads, dk=c.linear_key_head_dim,
+            dv=c.linear_value_head_dim, ks=c.linear_conv_kernel_dim, full_attention_host=C.cast(full, C.c_void_p),
+            group=c.group, act_dtype=L.DUO_F32 if c.act_dtype == "f32" else L.DUO_BF16)
+        h = C.c_void_p()
+        L.call("duo_engine_create", C.byref(self._c), C.byref(h))
+        self._h = h
+        view = weights.c_view()
+        L.call("duo_engine_load", self._h, C.byref(view), self._s())
+        torch.cuda.synchronize()
+        self.rows = 0
+        self._pushes = {}
+        self._ids_pinned = None
+
+    def _s(self):
+        return L.stream_ptr(self.stream)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            L.lib().duo_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- state (model.js:308-376)
+    def alloc(self, rows=3, max_len=1024, max_t=128, max_tokens=None):
+        """rows independent sequences, max_len cache positions per row, max_t tokens per prefill chunk;
+        max_tokens bounds rows * T of one forward call (default max(max_t, rows), as model.js:313 sizes it)."""
+        self.max_t = max_t
+        self.max_len = max_len
+        self.max_tokens = max_tokens or max(max_t, rows)
+        L.call("duo_engine_alloc", self._h, rows, max_len, self.max_tokens)
+        self.rows = rows
+        self._pushes = {}
+        self._ids_pinned = torch.empty(self.max_tokens, dtype=torch.int32, pin_memory=True)
+        return self
+
+    def reset(self, r):
+        L.call("duo_engine_reset", self._h, r, self._s())
+
+    def set_vectors(self, rows):
+        """One vector (len hidden) per row, None for zero (model.js:372-376)."""
+        H = self.cfg.hidden_size
+        buf = np.zeros((self.rows, H), dtype=np.float32)
+        for r, v in enumerate(rows):
+            if v is not None:
+                buf[r] = np.asarray(v.detach().cpu() if torch.is_tensor(v) else v, dtype=np.float32)
+        L.call("duo_engine_set_vectors", self._h, buf.ctypes.data_as(C.c_void_p), self.rows, self._s())
+        torch.cuda.current_stream().synchronize() if self.stream is None else self.stream.synchronize()
+
+    def set_head_scales(self, scales):
+        """{layer: [hv scales]} for linear-attention layers; missing layers get ones (model.js:362-369)."""
+        for l in range(self.cfg.num_hidden_layers):
+            if self.cfg.is_full(l):
+                continue
+            s = (scales or {}).get(l)
+            arr = None if s is None else np.ascontiguousarray(np.asarray(s, dtype=np.float32))
+            L.call("duo_engine_set_head_scales", self._h, l, None if arr is None else arr.ctypes.data_as(C.c_void_p),
+                   self._s())
+
+    def _set_pushes(self, pushes):
+        pushes = pushes or {}
+        for l in set(self._pushes) | set(int(k) for k in pushes):
+            recs = pushes.get(l, pushes.get(str(l), []))
+            key = tuple((r.get("n"), r.get("mode", "add"), tuple(np.asarray(r["vals"], dtype=np.float32).tolist()))
+                        for r in recs)
+            if self._pushes.get(l) == key:
+                continue
+            n = len(recs)
+            neu = np.array([L.DUO_ALL_NEURONS if r.get("n") is None else int(r["n"]) for r in recs], dtype=np.int32)
+            mode = np.array([L.DUO_PUSH_MUL if r.get("mode") == "mul" else L.DUO_PUSH_ADD for r in recs], dtype=np.int32)
+            vals = np.zeros((max(n, 1), self.rows), dtype=np.float32)
+            for i, r in enumerate(recs):
+                v = np.asarray(r["vals"], dtype=np.float32).reshape(-1)
+                vals[i, :] = 1.0 if r.get("mode") == "mul" else 0.0  # rows without a value are untouched
+                vals[i, : min(len(v), self.rows)] = v[: self.rows]
+            L.call("duo_engine_set_pushes", self._h, l, n, neu.ctypes.data_as(C.c_void_p),
+                   mode.ctypes.data_as(C.c_void_p), vals.ctypes.data_as(C.c_void_p), self._s())
+            self._pushes[l] = key
+
+    # ---- forward (model.js:404-508)
+    def forward(self, ids, row_base, rows, T, opts=None):
+        """_forward: rows consecutive sequences from row_base, T new tokens each (ids token-major, len rows * T)."""
+        opts = opts or {}
+        self._set_pushes(opts.get("pushes"))
+        vec = opts.get("vec")
+        vec = -1 if vec is None else int(vec)
+        if torch.is_tensor(ids) and ids.is_cuda:
+            ids = ids.to(torch.int32).contiguous()
+            L.call("duo_engine_forward_device", self._h, L.ptr(ids), row_base, rows, T, vec, self._s())
+            return
+        n = rows * T
+        if n > self._ids_pinned.numel():
+            raise ValueError(f"rows * T = {n} exceeds max_tokens {self._ids_pinned.numel()}")
+        host = self._ids_pinned[:n]
+        host.copy_(torch.as_tensor(np.asarray(ids, dtype=np.int32).reshape(-1)))
+        L.call("duo_engine_forward", self._h, L.ptr(host), row_base, rows, T, vec, self._s())
+
+    def prefill(self, r, ids, opts=None):
+        """Prefill row r with ids from its current length, in chunks of max_t tokens (model.js:486-491)."""
+        ids = list(ids) if not torch.is_tensor(ids) else ids
+        for i in range(0, len(ids), self.max_t):
+            chunk = ids[i:i + self.max_t]
+            self.forward(chunk, r, 1, len(chunk), opts)
+
+    def step(self, ids, opts=None):
+        """Decode one token for every row (ids[r] for row r) (model.js:508)."""
+        self.forward(ids, 0, self.rows, 1, opts)
+
+    def row_len(self, r):
+        return L.check(L.lib().duo_engine_row_len(self._h, r))
+
+    # ---- heads (model.js:472-505)
+    def logits(self, row0=0, n=None):
+        n = self.rows - row0 if n is None else n
+        out = torch.empty(n, self.cfg.vocab_size, dtype=torch.float32, device="cuda")
+        L.call("duo_engine_logits", self._h, row0, n, L.ptr(out), self._s())
+        return out
+
+    def logits_row(self, r):
+        return self.logits(r, 1)[0]
+
+    def logits_all(self):
+        return self.logits(0, self.rows)
+
+    def argmax_all(self, device_out=False):
+        out = torch.empty(self.rows, dtype=torch.int32, device="cuda")
+        L.call("duo_engine_argmax", self._h, 0, self.rows, L.ptr(out), self._s())
+        return out if device_out else out.tolist()
+
+    def generate(self, n_steps, vec=None):
+        """Greedy decode of every row for n_steps on the device (the reference's argmaxAll + step loop,
+        analysis.js:127-142); returns the tokens [rows, n_steps] (int32, CUDA)."""
+        out = torch.empty(self.rows, max(n_steps, 1), dtype=torch.int32, device="cuda")
+        L.call("duo_engine_generate", self._h, n_steps, -1 if vec is None else int(vec), L.ptr(out), self._s())
+        return out[:, :n_steps]

@@ -1,0 +1,179 @@
+/* duo_mixer.h -- C ABI of the B200 (sm_100a) token-mixing engine for Qwen3.5-shaped decoders.
+ *
+ * This is the drop-in boundary for the hot path of scasella/duo-mech-interp's engine: the Gated DeltaNet and gated
+ * attention token mixers, the int8-dequant projections around them and the residual steering-vector add.  In the
+ * reference those run as WGSL kernels behind `Model` (engine/model.js:26-509) and are dispatched through
+ * `GPU.run(name, wgsl, bindings, workgroups, uniforms)` (engine/gpu.js:109-129).  Each entry point below names the
+ * reference function or kernel it replaces.
+ *
+ * Conventions
+ *   - Every call returns a duo status: DUO_OK (0) or a negative code.  No exception or abort crosses the ABI; the
+ *     message of the last failure on the calling host thread is returned by duo_last_error().  (The reference
+ *     throws JS exceptions on shape limits, model.js:52, 406, 418; gpu.js:127.)
+ *   - Pointers named `*_host` are host memory; every other data pointer is device memory of the current CUDA device.
+ *   - `duo_stream` is a cudaStream_t (NULL = legacy default stream).  Calls are stream-ordered and asynchronous
+ *     unless documented otherwise.
+ *   - dtype codes: DUO_F32, DUO_BF16 for activations; weights are int8 + f32 scales ("q8", engine/kernels.js:1-5).
+ *   - An engine handle is not thread-safe; use one per stream / process.  Multi-GPU = one handle per process.
+ */
+#ifndef DUO_MIXER_H
+#define DUO_MIXER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* duo_stream;
+typedef struct duo_engine duo_engine;
+
+enum duo_status_code {
+  DUO_OK = 0,
+  DUO_EINVAL = -1,  /* invalid argument or shape */
+  DUO_ECUDA = -2,   /* a CUDA runtime / driver call or a kernel launch failed */
+  DUO_ESTATE = -3,  /* call out of order (no weights, no state, row past its cache, ...) */
+  DUO_ENOMEM = -4   /* device allocation failed */
+};
+
+enum duo_dtype { DUO_F32 = 0, DUO_BF16 = 1, DUO_F16 = 2, DUO_I8 = 3, DUO_I32 = 4 };
+enum duo_push_mode { DUO_PUSH_ADD = 0, DUO_PUSH_MUL = 1 };
+#define DUO_ALL_NEURONS (-1)
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* duo_last_error(void);
+/* ABI version of this library (bumped on any signature change). */
+int duo_abi_version(void);
+
+/* ============================================================================================================
+ * Op-level entry points (the per-kernel sweeps and the parity tests call these; the engine uses the same kernels)
+ * ============================================================================================================ */
+
+/* W[n, k] (f32 / bf16 / f16, row-major) -> q[n, k] int8 + s[n, k / group] f32.  scale = absmax / 127 (1 for an
+ * all-zero group), q = round-half-even(v / scale) with IEEE division.  group = 128 is the reference format; group = k
+ * gives one scale per output row.  Replaces the `quantize(src)` kernel, engine/kernels.js:16-47 (and its dispatch,
+ * model.js:213-216).  Bit-exact contract. */
+int duo_q8_quantize(const void* w, int w_dtype, int n, int k, int group, int8_t* q, float* s, duo_stream stream);
+
+/* out[n, k] = f32(q) * scale, written as f32 or bf16 (kernels.js:7-11 unpack, :74-75 dequant). */
+int duo_q8_dequantize(const int8_t* q, const float* s, int n, int k, int group, void* out, int out_dtype,
+                      duo_stream stream);
+
+/* y[m, n] (+)= x[m, k] . dequant(W)[n, k]^T for m <= 8, streaming the int8 weights once (decode).  x and y are f32 or
+ * bf16; accumulate != 0 adds into y.  Replaces `matvec(M, add)`, engine/kernels.js:55-94 (dispatched by
+ * model.js:382-392). */
+int duo_q8_gemv(const void* x, int x_dtype, int m, int k, const int8_t* q, const float* s, int group, int n, void* y,
+                int y_dtype, int accumulate, duo_stream stream);
+
+/* y[t, :] = dequant(E)[ids[t], :] (f32).  Replaces `gather`, engine/kernels.js:205-221. */
+int duo_q8_gather(const int32_t* ids, int t, const int8_t* q, const float* s, int group, int k, int vocab, float* y,
+                  duo_stream stream);
+
+/* Dense bf16 tensor-core GEMM (tcgen05, accumulators in TMEM):  C[m, n] (+)= (A[m, k] . B[n, k]^T) * col_scale[n].
+ * A and B are row-major bf16 with k a multiple of 64; col_scale may be NULL; C is f32 or bf16 with leading dim ldc.
+ * The prefill path of `matmul(add)`, engine/kernels.js:97-151, runs on this kernel. */
+int duo_gemm_bf16(const void* a, int m, int k, const void* b, int n, const float* col_scale, void* c, int c_dtype,
+                  int ldc, int accumulate, duo_stream stream);
+
+/* y[m, :] = x[m, :] * rsqrt(mean(x^2) + eps) * (1 + w) (offset != 0) or * w.  x f32, y f32 / bf16.
+ * Replaces `rmsnorm(offset)`, engine/kernels.js:226-246. */
+int duo_rmsnorm(const float* x, int m, int d, const float* w, float eps, int offset, void* y, int y_dtype,
+                duo_stream stream);
+
+/* Gated DeltaNet scan computed token by token (the recurrent form; t = 1 is one decode step) over b rows x t tokens
+ * x h heads:  q, k [b, t, h, dk], v [b, t, h, dv] (f32 or bf16, token-major), g (log decay), beta [b, t, h] f32,
+ * state [b, h, dk, dv] f32 read as the initial state and overwritten with the final one, o [b, t, h, dv].
+ * l2norm_qk != 0 l2-normalises q and k first (eps 1e-6); q is scaled by 1/sqrt(dk) inside.  dk = dv = 128.
+ * Replaces the recurrence of `delta`, engine/kernels_qwen35.js:209-236. */
+int duo_gdn_recurrent_fwd(const void* q, const void* k, const void* v, int in_dtype, const float* g,
+                          const float* beta, float* state, void* o, int o_dtype, int b, int t, int h, int dk, int dv,
+                          int l2norm_qk, duo_stream stream);
+
+/* Causal GQA softmax attention of b rows over their caches.  q [b, t, nh, hd] holds the t new queries of each row,
+ * which sit at cache positions start[r] .. start[r] + t - 1; kc, vc [b, max_len, nkv, hd] hold keys / values
+ * 0 .. start[r] + t - 1.  o[b, t, nh, hd] = softmax(q k^T * scale) v, times sigmoid(gate[b, t, nh, hd]) when gate is
+ * not NULL (gate_stride = elements between consecutive tokens' gate rows).  q, kc, vc, gate, o share `dtype`.
+ * Replaces `attention`, engine/kernels_qwen35.js:73-123. */
+int duo_attention(const void* q, const void* kc, const void* vc, const int32_t* start, const void* gate,
+                  int gate_stride, void* o, int dtype, int b, int t, int nh, int nkv, int hd, int max_len, float scale,
+                  duo_stream stream);
+
+/* ============================================================================================================
+ * Engine: mirrors engine/model.js `Model` (alloc, reset, setVectors, setHeadScales, _forward, _logits, argmaxAll)
+ * ============================================================================================================ */
+
+typedef struct duo_config {
+  int hidden, inter, vocab, layers;
+  int nh, nkv, hd, rot;   /* full attention: q heads, kv heads, head dim, rotary dims (partial RoPE) */
+  float theta, eps;
+  int hk, hv, dk, dv, ks; /* linear attention: key heads, value heads, head dims, conv kernel */
+  const uint8_t* full_attention_host; /* [layers], 1 = full attention layer, 0 = Gated DeltaNet (copied) */
+  int group;              /* int8 group size along the input dim: 128 (reference), or 0 for one scale per row */
+  int act_dtype;          /* DUO_F32 (the reference's f32 engine) or DUO_BF16 (tensor-core path) */
+} duo_config;
+
+typedef struct duo_q8_view { const int8_t* q; const float* s; } duo_q8_view;
+
+/* One layer's weights in the reference's fused layouts (model.js:70-116).  Device pointers, owned by the caller. */
+typedef struct duo_layer_view {
+  const float* in_norm;   /* [hidden], applied as (1 + w) */
+  const float* post_norm; /* [hidden] */
+  duo_q8_view proj;       /* linear: [qkv | z | b | a] x hidden;  full: [q+gate | k | v] x hidden */
+  duo_q8_view out;        /* hidden x (hv * dv) or hidden x (nh * hd) */
+  duo_q8_view gu;         /* [gate | up] (2 * inter) x hidden */
+  duo_q8_view down;       /* hidden x inter */
+  const float* conv;      /* linear: [conv_dim, ks] */
+  const float* a_log;     /* linear: [hv] */
+  const float* dt_bias;   /* linear: [hv] */
+  const float* gnorm;     /* linear: [dv] gated-norm weight (not offset) */
+  const float* q_norm;    /* full: [hd] */
+  const float* k_norm;    /* full: [hd] */
+} duo_layer_view;
+
+typedef struct duo_weights_view {
+  duo_q8_view embed;      /* vocab x hidden, tied with the LM head */
+  const float* final_norm;
+  const duo_layer_view* layers_host; /* [layers] host array of views (copied) */
+} duo_weights_view;
+
+/* new Model(cfg) (model.js:27-58). */
+int duo_engine_create(const duo_config* cfg, duo_engine** out);
+void duo_engine_destroy(duo_engine* e);
+/* Model weights (model.js:142-151, 282-302).  Pointers are kept, not copied: the caller keeps them alive.  With
+ * act_dtype = DUO_BF16 the engine also builds its own bf16 copy of every projection for the tensor-core GEMM. */
+int duo_engine_load(duo_engine* e, const duo_weights_view* w, duo_stream stream);
+/* alloc(rows, maxLen, maxT) (model.js:308-342); max_tokens bounds rows * T of one forward call. */
+int duo_engine_alloc(duo_engine* e, int rows, int max_len, int max_tokens);
+/* reset(r) (model.js:352-360): zero row r's recurrent and conv state and its length. */
+int duo_engine_reset(duo_engine* e, int row, duo_stream stream);
+/* setVectors(rows) (model.js:372-376): vecs_host [n_rows, hidden]; rows >= n_rows get zero vectors. */
+int duo_engine_set_vectors(duo_engine* e, const float* vecs_host, int n_rows, duo_stream stream);
+/* setHeadScales (model.js:362-369) for one linear-attention layer; NULL restores all ones. */
+int duo_engine_set_head_scales(duo_engine* e, int layer, const float* scales_host, duo_stream stream);
+/* Neuron pushes of one layer at the down_proj input (model.js:412-424, kernels_qwen35.js:254-279): n records, each
+ * (neuron or DUO_ALL_NEURONS, DUO_PUSH_ADD / DUO_PUSH_MUL, one value per engine row: vals_host[n, rows]).  Records
+ * apply in order; n = 0 clears the layer.  They stay in force for every later forward until changed. */
+int duo_engine_set_pushes(duo_engine* e, int layer, int n, const int32_t* neurons_host, const int32_t* modes_host,
+                          const float* vals_host, duo_stream stream);
+/* _forward(ids, rowBase, rows, T, {vec}) (model.js:404-466): ids_host [rows * T] token-major; vec_layer = -1 for
+ * none.  Copies the ids to the device on `stream`.  Leaves each row's final hidden state in the engine. */
+int duo_engine_forward(duo_engine* e, const int32_t* ids_host, int row_base, int rows, int t, int vec_layer,
+                       duo_stream stream);
+/* Same with device-resident ids (no host traffic; capturable in a CUDA graph). */
+int duo_engine_forward_device(duo_engine* e, const int32_t* ids, int row_base, int rows, int t, int vec_layer,
+                              duo_stream stream);
+/* _logits(n, r0) (model.js:472-477): final norm + tied LM head for rows r0..r0+n-1 -> out[n, vocab] f32 (device). */
+int duo_engine_logits(duo_engine* e, int row0, int n, float* out, duo_stream stream);
+/* argmaxAll (model.js:494-500) for rows r0..r0+n-1 -> out[n] int32 (device); ties go to the lower index. */
+int duo_engine_argmax(duo_engine* e, int row0, int n, int32_t* out, duo_stream stream);
+/* Greedy decode of every row for n_steps (the reference's loop of argmaxAll + step, analysis.js:127-142), entirely on
+ * the device: tokens_out [rows, n_steps] int32 (device).  The first token is the argmax of the current state. */
+int duo_engine_generate(duo_engine* e, int n_steps, int vec_layer, int32_t* tokens_out, duo_stream stream);
+/* Tokens held so far by row r (this.len[r] in model.js), or a negative status. */
+int duo_engine_row_len(duo_engine* e, int row);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DUO_MIXER_H */

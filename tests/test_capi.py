@@ -1,0 +1,75 @@
+"""CPU tests of the C ABI: the library loads, exports every entry point include/duo_mixer.h declares, and rejects
+bad arguments with a status and a message before touching a GPU (the reference throws on shape limits,
+engine/model.js:52, 406, 418)."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "duo_mixer.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(duo_\w+)\s*\(", text)) - {"duo_config", "duo_q8_view"})
+
+
+@pytest.fixture(scope="module")
+def L():
+    from duo import lib as dl
+    return dl
+
+
+def test_library_exports_every_declared_symbol(L):
+    lib = L.lib()
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the Python binding knows every one of them
+    assert sorted(set(names) - set(L.SIGNATURES)) == []
+
+
+def test_abi_version(L):
+    assert L.lib().duo_abi_version() >= 1
+
+
+def test_bad_arguments_return_status_and_message(L):
+    lib = L.lib()
+    st = lib.duo_q8_quantize(None, L.DUO_F32, 4, 100, 128, None, None, None)  # k not a multiple of the group
+    assert st == L.DUO_EINVAL
+    assert b"multiple" in lib.duo_last_error()
+    st = lib.duo_q8_gemv(None, L.DUO_F32, 9, 128, None, None, 128, 4, None, L.DUO_F32, 0, None)
+    assert st == L.DUO_EINVAL
+    st = lib.duo_gemm_bf16(None, 4, 100, None, 4, None, None, L.DUO_F32, 4, 0, None)
+    assert st == L.DUO_EINVAL and b"64" in lib.duo_last_error()
+    st = lib.duo_gdn_recurrent_fwd(None, None, None, L.DUO_F32, None, None, None, None, L.DUO_F32, 1, 1, 1, 64, 128,
+                                   1, None)
+    assert st == L.DUO_EINVAL and b"128" in lib.duo_last_error()
+    st = lib.duo_attention(None, None, None, None, None, 0, None, 7, 1, 1, 8, 2, 256, 16, 1.0, None)
+    assert st == L.DUO_EINVAL
+
+
+def test_engine_rejects_bad_config_and_null_handle(L):
+    lib = L.lib()
+    full = (C.c_uint8 * 4)(0, 0, 0, 1)
+    cfg = L.duo_config(hidden=1024, inter=3584, vocab=1000, layers=4, nh=8, nkv=2, hd=128, rot=64, theta=1e7,
+                       eps=1e-6, hk=16, hv=16, dk=128, dv=128, ks=4, full_attention_host=C.cast(full, C.c_void_p),
+                       group=128, act_dtype=L.DUO_BF16)
+    h = C.c_void_p()
+    assert lib.duo_engine_create(C.byref(cfg), C.byref(h)) == L.DUO_EINVAL  # hd must be 256
+    assert b"hd" in lib.duo_last_error()
+    cfg.hd, cfg.dk = 256, 64
+    assert lib.duo_engine_create(C.byref(cfg), C.byref(h)) == L.DUO_EINVAL
+    assert lib.duo_engine_alloc(None, 3, 64, 64) == L.DUO_EINVAL
+    assert lib.duo_engine_forward(None, None, 0, 1, 1, -1, None) == L.DUO_EINVAL
+    assert lib.duo_engine_row_len(None, 0) == L.DUO_EINVAL
+
+
+def test_python_errors_raise(L):
+    with pytest.raises(L.DuoError):
+        L.call("duo_q8_quantize", None, L.DUO_F32, 4, 100, 128, None, None, None)

@@ -1,0 +1,192 @@
+"""GPU parity of each kernel against the CPU oracle, through the C ABI.
+
+Tolerances: bit-exact for the int8 format (quantise, dequantise, gather); f32 paths 1e-4 max relative error
+(north_star's fp32-accumulation bound) or tighter; bf16 paths 2e-2 (north_star's bf16 bound)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_max
+from oracle import mixer, q8 as oq8
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops(cuda):
+    from duo import ops as o
+    return o
+
+
+def _seed(s):
+    return torch.Generator(device="cpu").manual_seed(s)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# int8 format (engine/kernels.js:16-47, 205-221): bit-exact
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,k,group", [(37, 256, 128), (5, 1024, 1024), (300, 384, 128), (1, 128, 128)])
+def test_q8_quantize_bit_exact(ops, dtype, n, k, group):
+    w = torch.randn(n, k, generator=_seed(n * 7 + k)) * 0.05
+    w[0, :min(k, 128)] = 0.0                            # an all-zero group -> scale 1
+    if k >= 256:
+        w[-1, 128:256] = torch.arange(128) * 0.5 - 32.0  # exact halves under scale 0.5/127*... edge values
+    w = w.to(dtype)
+    q, s = ops.q8_quantize(w.cuda(), group)
+    rq, rs = oq8.quantize(w.float().numpy(), group)
+    assert np.array_equal(q.cpu().numpy(), rq)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+
+
+def test_q8_dequant_and_gather_exact(ops):
+    w = torch.randn(500, 256, generator=_seed(3)) * 0.02
+    q, s = ops.q8_quantize(w.cuda(), 128)
+    d = ops.q8_dequantize(q, s, torch.float32)
+    ref = oq8.dequantize(q.cpu().numpy(), s.cpu().numpy(), 128)
+    assert np.array_equal(d.cpu().numpy(), ref)
+    db = ops.q8_dequantize(q, s, torch.bfloat16)
+    assert torch.equal(db.cpu(), torch.from_numpy(ref).to(torch.bfloat16))
+    ids = torch.tensor([0, 499, 17, 17, 250], dtype=torch.int32)
+    g = ops.q8_gather(ids.cuda(), q, s)
+    assert np.array_equal(g.cpu().numpy(), oq8.gather(ids.numpy(), q.cpu().numpy(), s.cpu().numpy(), 128))
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# decode GEMV (engine/kernels.js:55-94)
+
+
+@pytest.mark.parametrize("m", [1, 3, 8])
+@pytest.mark.parametrize("k,group", [(1024, 128), (3584, 128), (2048, 2048)])
+def test_q8_gemv(ops, m, k, group):
+    n = 1000
+    w = torch.randn(n, k, generator=_seed(k + m)) * 0.02
+    x = torch.randn(m, k, generator=_seed(k - m))
+    q, s = ops.q8_quantize(w.cuda(), group)
+    ref = oq8.matvec(x.numpy(), q.cpu().numpy(), s.cpu().numpy(), group)
+    y = ops.q8_gemv(x.cuda(), q, s)
+    assert rel_max(y, ref) < 1e-5
+    # accumulate into an existing f32 output (the residual add)
+    y0 = torch.randn(m, n, generator=_seed(5))
+    y2 = ops.q8_gemv(x.cuda(), q, s, y=y0.clone().cuda(), accumulate=True)
+    assert rel_max(y2, ref + y0.numpy()) < 1e-5
+    # bf16 activations in and out
+    yb = ops.q8_gemv(x.to(torch.bfloat16).cuda(), q, s, out_dtype=torch.bfloat16)
+    refb = oq8.matvec(x.to(torch.bfloat16).float().numpy(), q.cpu().numpy(), s.cpu().numpy(), group)
+    assert rel_max(yb.float(), refb) < 1e-2
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# tcgen05 GEMM vs a torch fp32 matmul of the same bf16 operands
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (200, 300, 1024), (1024, 1024, 3584), (40, 7168, 1024),
+                                   (3000, 512, 2048)])
+def test_gemm_bf16(ops, m, n, k):
+    a = (torch.randn(m, k, generator=_seed(m)) ).to(torch.bfloat16)
+    b = (torch.randn(n, k, generator=_seed(n)) * 0.05).to(torch.bfloat16)
+    ref = a.float() @ b.float().T
+    c = ops.gemm_bf16(a.cuda(), b.cuda(), out_dtype=torch.float32)
+    assert rel_max(c, ref) < 1e-5
+    cb = ops.gemm_bf16(a.cuda(), b.cuda(), out_dtype=torch.bfloat16)
+    assert rel_max(cb.float(), ref) < 8e-3
+    cs = torch.rand(n, generator=_seed(1)) + 0.5
+    x0 = torch.randn(m, n, generator=_seed(2))
+    acc = ops.gemm_bf16(a.cuda(), b.cuda(), col_scale=cs.cuda(), out=x0.clone().cuda(), accumulate=True)
+    assert rel_max(acc, x0 + ref * cs) < 1e-5
+    assert ops.fault_status() == 0
+
+
+def test_rmsnorm(ops):
+    x = torch.randn(7, 1024, generator=_seed(9)) * 3
+    w = torch.randn(1024, generator=_seed(10)) * 0.1
+    y = ops.rmsnorm(x.cuda(), w.cuda(), 1e-6)
+    assert rel_max(y, mixer.rmsnorm(x, w, 1e-6)) < 1e-6
+    yb = ops.rmsnorm(x.cuda(), w.cuda(), 1e-6, out_dtype=torch.bfloat16)
+    assert rel_max(yb.float(), mixer.rmsnorm(x, w, 1e-6)) < 8e-3
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Gated DeltaNet scan (kernels_qwen35.js:183-247; transformers torch_recurrent_gated_delta_rule)
+
+
+def _gdn_inputs(b, t, h, seed, normed):
+    g = _seed(seed)
+    q = torch.randn(b, t, h, 128, generator=g)
+    k = torch.randn(b, t, h, 128, generator=g)
+    if normed:
+        q, k = mixer.l2norm(q), mixer.l2norm(k)
+    v = torch.randn(b, t, h, 128, generator=g)
+    beta = torch.sigmoid(torch.randn(b, t, h, generator=g))
+    gg = -torch.nn.functional.softplus(torch.randn(b, t, h, generator=g))
+    s0 = torch.randn(b, h, 128, 128, generator=g) * 0.05
+    return q, k, v, gg, beta, s0
+
+
+@pytest.mark.parametrize("b,t,h", [(1, 1, 16), (2, 37, 4), (8, 3, 16), (40, 1, 16)])
+def test_gdn_recurrent_f32(ops, b, t, h):
+    q, k, v, g, beta, s0 = _gdn_inputs(b, t, h, b * 100 + t, False)
+    ro, rs = mixer.recurrent_gated_delta_rule(q.double(), k.double(), v.double(), g.double(), beta.double(),
+                                              state=s0.double())
+    st = s0.clone().cuda()
+    o = ops.gdn_recurrent(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), st, l2norm_qk=True)
+    assert rel_max(o, ro) < 1e-4
+    assert rel_max(st, rs) < 1e-4
+
+
+def test_gdn_recurrent_steps_equal_one_call(ops):
+    q, k, v, g, beta, s0 = _gdn_inputs(2, 6, 4, 77, True)
+    st1 = s0.clone().cuda()
+    o1 = ops.gdn_recurrent(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), st1, l2norm_qk=False)
+    st2 = s0.clone().cuda()
+    outs = []
+    for i in range(6):
+        sl = lambda x: x[:, i:i + 1].contiguous().cuda()
+        outs.append(ops.gdn_recurrent(sl(q), sl(k), sl(v), sl(g), sl(beta), st2, l2norm_qk=False))
+    assert rel_max(torch.cat(outs, 1), o1) < 1e-6
+    assert rel_max(st2, st1) < 1e-6
+
+
+def test_gdn_recurrent_bf16(ops):
+    q, k, v, g, beta, s0 = _gdn_inputs(2, 40, 16, 5, True)
+    qb, kb, vb = (x.to(torch.bfloat16) for x in (q, k, v))
+    ro, rs = mixer.recurrent_gated_delta_rule(qb.double(), kb.double(), vb.double(), g.double(), beta.double(),
+                                              state=s0.double(), l2norm_qk=False)
+    st = s0.clone().cuda()
+    o = ops.gdn_recurrent(qb.cuda(), kb.cuda(), vb.cuda(), g.cuda(), beta.cuda(), st, l2norm_qk=False)
+    assert rel_max(o.float(), ro) < 2e-2
+    assert rel_max(st, rs) < 1e-3
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# attention (kernels_qwen35.js:73-123; transformers eager attention with repeat_kv, sigmoid gate)
+
+
+def _attn_ref(q, kc, vc, start, gate):
+    b, t, nh, hd = q.shape
+    out = torch.zeros(b, t, nh, hd, dtype=torch.float64)
+    for r in range(b):
+        n_keys = [int(start[r]) + i + 1 for i in range(t)]
+        out[r] = mixer.cached_attention(q[r].double(), kc[r].double(), vc[r].double(), n_keys, 1 / math.sqrt(hd))
+    if gate is not None:
+        out = out * torch.sigmoid(gate.double())
+    return out
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2)])
+@pytest.mark.parametrize("b,t,starts,max_len", [(2, 70, [0, 30], 128), (3, 1, [0, 5, 900], 1024),
+                                                (2, 1, [4095, 3000], 4096), (1, 33, [100], 256)])
+def test_attention(ops, dtype, tol, b, t, starts, max_len):
+    g = _seed(b * 1000 + t)
+    nh, nkv, hd = 8, 2, 256
+    q = torch.randn(b, t, nh, hd, generator=g).to(dtype)
+    kc = torch.randn(b, max_len, nkv, hd, generator=g).to(dtype)
+    vc = torch.randn(b, max_len, nkv, hd, generator=g).to(dtype)
+    gate = torch.randn(b, t, nh, hd, generator=g).to(dtype)
+    start = torch.tensor(starts, dtype=torch.int32)
+    ref = _attn_ref(q.float(), kc.float(), vc.float(), start, gate.float())
+    o = ops.attention(q.cuda(), kc.cuda(), vc.cuda(), start.cuda(), gate=gate.cuda())
+    assert rel_max(o.float(), ref) < tol
