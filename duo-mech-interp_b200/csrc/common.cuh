@@ -31,11 +31,15 @@ int fail(int code, const std::string& msg);
       return ::duo::fail(DUO_ECUDA, std::string(#expr) + ": " + cudaGetErrorString(_e));                 \
   } while (0)
 
+// after every kernel launch: count it (duo_launch_count) and turn a launch error into a status
 #define DUO_LAUNCH_CHECK(what)                                                                             \
   do {                                                                                                    \
+    ::duo::count_launch();                                                                                \
     cudaError_t _e = cudaGetLastError();                                                                  \
     if (_e != cudaSuccess) return ::duo::fail(DUO_ECUDA, std::string(what) + ": " + cudaGetErrorString(_e)); \
   } while (0)
+
+void count_launch();
 
 #define DUO_TRY(expr)              \
   do {                             \

@@ -174,8 +174,9 @@ int launch_finish_rows(const float* x, int h, int t, int row_base, int rows, flo
                        cudaStream_t st) {
   if (rows == 0) return DUO_OK;
   copy_last_kernel<<<rows, 256, 0, st>>>(x, h, t, row_base, last);
+  DUO_LAUNCH_CHECK("copy_last_kernel");
   advance_len_kernel<<<cdiv(rows, 256), 256, 0, st>>>(len, row_base, rows, t);
-  DUO_LAUNCH_CHECK("finish_rows");
+  DUO_LAUNCH_CHECK("advance_len_kernel");
   return DUO_OK;
 }
 

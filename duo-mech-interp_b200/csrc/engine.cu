@@ -75,10 +75,40 @@ struct duo_engine {
   std::vector<int> len;
   std::vector<LayerState> ls;
   std::vector<void*> state_owned;
+  // residual capture (model.js `resid`): copy of x after layer `cap_layer` of each forward into cap_out[M, hidden]
+  int cap_layer = -1;
+  float* cap_out = nullptr;
+  // live profiling: per kind, a pool of (start, stop) event pairs recorded around launches on the stream
+  unsigned prof_mask = 0;
+  struct ProfKind {
+    std::vector<cudaEvent_t> ev;  // 2 per recorded launch
+    size_t used = 0;
+  } prof[DUO_PROF_KINDS];
 
   ~duo_engine() {
     free_state();
     for (void* p : owned) cudaFree(p);
+    for (auto& k : prof)
+      for (cudaEvent_t ev : k.ev) cudaEventDestroy(ev);
+  }
+  // index of a started span, or -1 when this kind is not profiled
+  long prof_begin(int kind, cudaStream_t st) {
+    if (!(prof_mask & (1u << kind))) return -1;
+    ProfKind& k = prof[kind];
+    if (k.used + 2 > k.ev.size()) {
+      for (int i = 0; i < 256; i++) {
+        cudaEvent_t ev;
+        if (cudaEventCreate(&ev) != cudaSuccess) return -1;
+        k.ev.push_back(ev);
+      }
+    }
+    const long i = (long)k.used;
+    k.used += 2;
+    cudaEventRecord(k.ev[i], st);
+    return i;
+  }
+  void prof_end(int kind, long i, cudaStream_t st) {
+    if (i >= 0) cudaEventRecord(prof[kind].ev[i + 1], st);
   }
   void free_state() {
     for (void* p : state_owned) cudaFree(p);
@@ -100,6 +130,15 @@ struct duo_engine {
 };
 
 namespace {
+
+// DUO_TRY with the launch timed under profiling class `kind`
+#define PROF_TRY(kind, expr)                  \
+  do {                                        \
+    const long _pi = e->prof_begin(kind, st); \
+    const int _ps = (expr);                   \
+    e->prof_end(kind, _pi, st);               \
+    if (_ps != DUO_OK) return _ps;            \
+  } while (0)
 
 int check_engine(duo_engine* e, bool need_weights, bool need_state) {
   DUO_CHECK_ARG(e, "null engine");
@@ -145,13 +184,13 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
   const int M = rows * T;
   const int H = c.hidden;
   const int act = e->act;
-  DUO_TRY(launch_gather(ids_dev, M, e->w.embed.q, e->w.embed.s, e->gsize(H), H, c.vocab, e->x, st));
+  PROF_TRY(DUO_PROF_GATHER, launch_gather(ids_dev, M, e->w.embed.q, e->w.embed.s, e->gsize(H), H, c.vocab, e->x, st));
   for (int l = 0; l < c.layers; l++) {
     const duo_layer_view& L = e->lw[l];
     LayerState& S = e->ls[l];
     const bool full = e->is_full(l);
     const int wproj = full ? e->w_full : e->w_lin;
-    DUO_TRY(launch_rmsnorm(e->x, M, H, L.in_norm, c.eps, 1, e->xn, act, st));
+    PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->x, M, H, L.in_norm, c.eps, 1, e->xn, act, st));
     const void* xin = e->xn;
     {
       GemmEpiArgs ep;
@@ -159,7 +198,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.c = e->y;
       ep.c_dtype = act;
       ep.ldc = wproj;
-      DUO_TRY(project(e, xin, M, H, L.proj, e->p_proj[l], wproj, ep, st));
+      PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, xin, M, H, L.proj, e->p_proj[l], wproj, ep, st));
     }
     int out_k;
     if (!full) {
@@ -168,7 +207,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ca.dt_bias = L.dt_bias; ca.qkv_out = e->qkv; ca.g_out = e->g; ca.beta_out = e->beta;
       ca.hk = c.hk; ca.hv = c.hv; ca.dk = c.dk; ca.dv = c.dv; ca.ks = c.ks;
       ca.rows = rows; ca.t = T; ca.row_base = row_base;
-      DUO_TRY(launch_gdn_conv(ca, act, st));
+      PROF_TRY(DUO_PROF_GDN_CONV, launch_gdn_conv(ca, act, st));
       GdnScanArgs sa{};
       const size_t es = e->act_size;
       sa.q = e->qkv;
@@ -182,7 +221,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       sa.z = static_cast<const char*>(e->y) + (size_t)e->conv_dim * es;
       sa.z_stride = wproj;
       sa.norm_w = L.gnorm; sa.head_scale = S.head_scale; sa.eps = c.eps;
-      DUO_TRY(launch_gdn_recurrent(sa, act, st));
+      PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_recurrent(sa, act, st));
       out_k = e->vd;
     } else {
       AttnPrepArgs pa{};
@@ -190,7 +229,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       pa.len = e->len_dev; pa.q_out = e->q; pa.kc = S.kc; pa.vc = S.vc;
       pa.nh = c.nh; pa.nkv = c.nkv; pa.hd = c.hd; pa.rot = c.rot; pa.max_len = e->max_len;
       pa.rows = rows; pa.t = T; pa.row_base = row_base; pa.eps = c.eps;
-      DUO_TRY(launch_attn_prep(pa, act, st));
+      PROF_TRY(DUO_PROF_ATTN_PREP, launch_attn_prep(pa, act, st));
       AttnArgs aa{};
       aa.q = e->q; aa.kc = S.kc; aa.vc = S.vc;
       aa.cache_row0 = row_base;
@@ -202,7 +241,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       aa.b = rows; aa.t = T; aa.nh = c.nh; aa.nkv = c.nkv; aa.hd = c.hd; aa.max_len = e->max_len;
       aa.scale = 1.f / std::sqrt((float)c.hd);
       aa.work = e->attn_work; aa.work_floats = e->attn_work_floats_n;
-      DUO_TRY(launch_attention(aa, act, st));
+      PROF_TRY(DUO_PROF_ATTN, launch_attention(aa, act, st));
       out_k = c.nh * c.hd;
     }
     {
@@ -211,9 +250,9 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.c = e->x;
       ep.c_dtype = DUO_F32;
       ep.ldc = H;
-      DUO_TRY(project(e, e->o, M, out_k, L.out, e->p_out[l], H, ep, st));
+      PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->o, M, out_k, L.out, e->p_out[l], H, ep, st));
     }
-    DUO_TRY(launch_rmsnorm(e->x, M, H, L.post_norm, c.eps, 1, e->xn, act, st));
+    PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->x, M, H, L.post_norm, c.eps, 1, e->xn, act, st));
     PushTable pt{S.push_neuron, S.push_mode, S.push_vals, S.push_count, e->rows};
     if (M > kGemvMax && act == DUO_BF16) {
       GemmEpiArgs ep;
@@ -225,15 +264,15 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.t = T;
       ep.row_base = row_base;
       ep.push = pt;
-      DUO_TRY(launch_gemm_tc(e->xn, M, H, e->p_gu[l].w, 2 * c.inter, ep, st));
+      PROF_TRY(DUO_PROF_GEMM, launch_gemm_tc(e->xn, M, H, e->p_gu[l].w, 2 * c.inter, ep, st));
     } else {
       GemmEpiArgs ep;
       ep.epi = EPI_STORE;
       ep.c = e->y;
       ep.c_dtype = act;
       ep.ldc = 2 * c.inter;
-      DUO_TRY(project(e, e->xn, M, H, L.gu, Pack{}, 2 * c.inter, ep, st));
-      DUO_TRY(launch_swiglu_push(e->y, M, c.inter, T, row_base, pt, e->a, act, st));
+      PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->xn, M, H, L.gu, Pack{}, 2 * c.inter, ep, st));
+      PROF_TRY(DUO_PROF_SWIGLU, launch_swiglu_push(e->y, M, c.inter, T, row_base, pt, e->a, act, st));
     }
     {
       GemmEpiArgs ep;
@@ -244,23 +283,26 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.vec = (vec_layer == l) ? e->vec : nullptr;
       ep.t = T;
       ep.row_base = row_base;
-      DUO_TRY(project(e, e->a, M, c.inter, L.down, e->p_down[l], H, ep, st));
+      PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->a, M, c.inter, L.down, e->p_down[l], H, ep, st));
     }
+    if (l == e->cap_layer && e->cap_out)
+      DUO_CUDA_TRY(cudaMemcpyAsync(e->cap_out, e->x, (size_t)M * H * 4, cudaMemcpyDeviceToDevice, st));
   }
-  DUO_TRY(launch_finish_rows(e->x, H, T, row_base, rows, e->last, e->len_dev, st));
+  PROF_TRY(DUO_PROF_OTHER, launch_finish_rows(e->x, H, T, row_base, rows, e->last, e->len_dev, st));
   return DUO_OK;
 }
 
 int logits_impl(duo_engine* e, int row0, int n, float* out, cudaStream_t st) {
   const duo_config& c = e->cfg;
   const int H = c.hidden;
-  DUO_TRY(launch_rmsnorm(e->last + (size_t)row0 * H, n, H, e->w.final_norm, c.eps, 1, e->xn_last, e->act, st));
+  PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->last + (size_t)row0 * H, n, H, e->w.final_norm, c.eps, 1, e->xn_last, e->act, st));
   GemmEpiArgs ep;
   ep.epi = EPI_STORE;
   ep.c = out;
   ep.c_dtype = DUO_F32;
   ep.ldc = c.vocab;
-  return project(e, e->xn_last, n, H, e->w.embed, e->p_embed, c.vocab, ep, st);
+  PROF_TRY(n <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->xn_last, n, H, e->w.embed, e->p_embed, c.vocab, ep, st));
+  return DUO_OK;
 }
 
 int check_rows(duo_engine* e, int row_base, int rows, int T) {
@@ -422,6 +464,29 @@ extern "C" int duo_engine_alloc(duo_engine* e, int rows, int max_len, int max_to
   return DUO_OK;
 }
 
+extern "C" int duo_engine_reset_all(duo_engine* e, duo_stream stream) {
+  DUO_TRY(check_engine(e, false, true));
+  const duo_config& c = e->cfg;
+  cudaStream_t st = as_stream(stream);
+  for (int l = 0; l < c.layers; l++) {
+    if (e->is_full(l)) continue;
+    DUO_CUDA_TRY(cudaMemsetAsync(e->ls[l].conv, 0, (size_t)e->rows * (c.ks - 1) * e->conv_dim * 4, st));
+    DUO_CUDA_TRY(cudaMemsetAsync(e->ls[l].S, 0, (size_t)e->rows * c.hv * c.dk * c.dv * 4, st));
+  }
+  DUO_CUDA_TRY(cudaMemsetAsync(e->len_dev, 0, (size_t)e->rows * 4, st));
+  for (int& v : e->len) v = 0;
+  return DUO_OK;
+}
+
+extern "C" int duo_engine_capture_resid(duo_engine* e, int layer, float* out) {
+  DUO_CHECK_ARG(e, "null engine");
+  DUO_CHECK_ARG(layer >= -1 && layer < e->cfg.layers, "capture_resid: layer out of range");
+  DUO_CHECK_ARG(layer == -1 || out, "capture_resid: null output");
+  e->cap_layer = layer;
+  e->cap_out = layer >= 0 ? out : nullptr;
+  return DUO_OK;
+}
+
 extern "C" int duo_engine_reset(duo_engine* e, int row, duo_stream stream) {
   DUO_TRY(check_engine(e, false, true));
   DUO_CHECK_ARG(row >= 0 && row < e->rows, "engine_reset: row out of range");
@@ -519,8 +584,8 @@ extern "C" int duo_engine_argmax(duo_engine* e, int row0, int n, int32_t* out, d
 namespace {
 int generate_step(duo_engine* e, int vec_layer, int32_t* tokens_out, int n_steps, int step, cudaStream_t st) {
   DUO_TRY(logits_impl(e, 0, e->rows, e->logits, st));
-  DUO_TRY(launch_argmax(e->logits, e->rows, e->cfg.vocab, e->amax, st));
-  DUO_TRY(launch_feed_tokens(e->amax, e->rows, e->ids, tokens_out, n_steps, step, st));
+  PROF_TRY(DUO_PROF_OTHER, launch_argmax(e->logits, e->rows, e->cfg.vocab, e->amax, st));
+  PROF_TRY(DUO_PROF_OTHER, launch_feed_tokens(e->amax, e->rows, e->ids, tokens_out, n_steps, step, st));
   return forward_impl(e, e->ids, 0, e->rows, 1, vec_layer, st);
 }
 }  // namespace
@@ -544,4 +609,29 @@ extern "C" int duo_engine_row_len(duo_engine* e, int row) {
   DUO_TRY(check_engine(e, false, true));
   DUO_CHECK_ARG(row >= 0 && row < e->rows, "row_len: row out of range");
   return e->len[row];
+}
+
+extern "C" int duo_engine_profile(duo_engine* e, unsigned mask) {
+  DUO_CHECK_ARG(e, "null engine");
+  for (auto& k : e->prof) k.used = 0;
+  e->prof_mask = mask;
+  return DUO_OK;
+}
+
+extern "C" int duo_engine_profile_read(duo_engine* e, double* ms_out, long long* launches_out) {
+  DUO_CHECK_ARG(e && ms_out && launches_out, "profile_read: null pointer");
+  DUO_CUDA_TRY(cudaDeviceSynchronize());
+  for (int kind = 0; kind < DUO_PROF_KINDS; kind++) {
+    auto& k = e->prof[kind];
+    double ms = 0;
+    for (size_t i = 0; i + 1 < k.used; i += 2) {
+      float t = 0.f;
+      DUO_CUDA_TRY(cudaEventElapsedTime(&t, k.ev[i], k.ev[i + 1]));
+      ms += t;
+    }
+    ms_out[kind] = ms;
+    launches_out[kind] = (long long)(k.used / 2);
+    k.used = 0;
+  }
+  return DUO_OK;
 }

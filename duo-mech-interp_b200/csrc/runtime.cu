@@ -1,4 +1,5 @@
 // Error plumbing and device queries shared by every C entry point.
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -14,6 +15,10 @@ int fail(int code, const std::string& msg) {
   set_error(msg);
   return code;
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int sm_count() {
   static int cached = 0;
@@ -34,3 +39,5 @@ int sm_count() {
 extern "C" const char* duo_last_error(void) { return duo::g_last_error.c_str(); }
 
 extern "C" int duo_abi_version(void) { return 1; }
+
+extern "C" unsigned long long duo_launch_count(void) { return duo::g_launches.load(std::memory_order_relaxed); }

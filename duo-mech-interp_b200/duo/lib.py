@@ -64,7 +64,15 @@ SIGNATURES = {
     "duo_engine_argmax": (_i, [_vp, _i, _i, _vp, _vp]),
     "duo_engine_generate": (_i, [_vp, _i, _i, _vp, _vp]),
     "duo_engine_row_len": (_i, [_vp, _i]),
+    "duo_launch_count": (C.c_ulonglong, []),
+    "duo_engine_reset_all": (_i, [_vp, _vp]),
+    "duo_engine_capture_resid": (_i, [_vp, _i, _vp]),
+    "duo_engine_profile": (_i, [_vp, _u]),
+    "duo_engine_profile_read": (_i, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_longlong)]),
 }
+
+# profiling classes of duo_engine_profile (enum duo_prof_kind)
+PROF_KINDS = ["gather", "rmsnorm", "gemv", "gemm", "gdn_conv", "gdn_scan", "attn_prep", "attn", "swiglu", "other"]
 
 
 class DuoError(RuntimeError):

@@ -68,6 +68,20 @@ class Model:
     def reset(self, r):
         L.call("duo_engine_reset", self._h, r, self._s())
 
+    def reset_all(self):
+        L.call("duo_engine_reset_all", self._h, self._s())
+
+    def capture_resid(self, layer=None):
+        """The reference's `resid` option for one layer: later forwards copy the residual stream after `layer` into
+        the returned [max_tokens, hidden] f32 tensor (rows of the last call first).  None turns it off."""
+        if layer is None:
+            L.call("duo_engine_capture_resid", self._h, -1, None)
+            self._resid = None
+            return None
+        self._resid = torch.empty(self.max_tokens, self.cfg.hidden_size, dtype=torch.float32, device="cuda")
+        L.call("duo_engine_capture_resid", self._h, int(layer), L.ptr(self._resid))
+        return self._resid
+
     def set_vectors(self, rows):
         """One vector (len hidden) per row, None for zero (model.js:372-376)."""
         H = self.cfg.hidden_size
@@ -121,7 +135,7 @@ class Model:
             return
         n = rows * T
         if n > self._ids_pinned.numel():
-            raise ValueError(f"rows * T = {n} exceeds max_tokens {self._ids_pinned.numel()}")
+            raise L.DuoError(L.DUO_EINVAL, f"forward: rows * T = {n} exceeds max_tokens {self._ids_pinned.numel()}")
         host = self._ids_pinned[:n]
         host.copy_(torch.as_tensor(np.asarray(ids, dtype=np.int32).reshape(-1)))
         L.call("duo_engine_forward", self._h, L.ptr(host), row_base, rows, T, vec, self._s())
@@ -139,6 +153,23 @@ class Model:
 
     def row_len(self, r):
         return L.check(L.lib().duo_engine_row_len(self._h, r))
+
+    # ---- live profiling (CUDA events around each launch of the selected kernel classes)
+    def profile(self, kinds=None):
+        """Start timing the given classes (names of lib.PROF_KINDS; None = all, [] = off)."""
+        kinds = L.PROF_KINDS if kinds is None else kinds
+        mask = 0
+        for k in kinds:
+            mask |= 1 << L.PROF_KINDS.index(k)
+        L.call("duo_engine_profile", self._h, mask)
+
+    def profile_read(self):
+        """{class: (milliseconds, launches)} since the last read; synchronises the device."""
+        n = len(L.PROF_KINDS)
+        ms = (C.c_double * n)()
+        cnt = (C.c_longlong * n)()
+        L.call("duo_engine_profile_read", self._h, ms, cnt)
+        return {k: (ms[i], cnt[i]) for i, k in enumerate(L.PROF_KINDS) if cnt[i]}
 
     # ---- heads (model.js:472-505)
     def logits(self, row0=0, n=None):

@@ -45,6 +45,12 @@ enum duo_push_mode { DUO_PUSH_ADD = 0, DUO_PUSH_MUL = 1 };
 const char* duo_last_error(void);
 /* ABI version of this library (bumped on any signature change). */
 int duo_abi_version(void);
+/* Number of kernels this library has launched in this process (every entry point counts its launches). */
+unsigned long long duo_launch_count(void);
+/* Synchronise the device and read-and-clear the fault word of the tensor-core kernels: non-zero means a bounded
+ * wait inside a kernel gave up (the kernel unwound instead of hanging).  The reference's analogue is its
+ * device-lost check, engine/gpu.js:38, 151. */
+int duo_fault_status(unsigned* out);
 
 /* ============================================================================================================
  * Op-level entry points (the per-kernel sweeps and the parity tests call these; the engine uses the same kernels)
@@ -147,6 +153,11 @@ int duo_engine_load(duo_engine* e, const duo_weights_view* w, duo_stream stream)
 int duo_engine_alloc(duo_engine* e, int rows, int max_len, int max_tokens);
 /* reset(r) (model.js:352-360): zero row r's recurrent and conv state and its length. */
 int duo_engine_reset(duo_engine* e, int row, duo_stream stream);
+/* reset(r) for every row at once. */
+int duo_engine_reset_all(duo_engine* e, duo_stream stream);
+/* The `resid` hook of model.js:7-12, 461 for one layer: every later forward copies the residual stream after layer
+ * `layer` (after its MLP and vector add) into out[rows * T, hidden] (f32, device).  layer = -1 turns it off. */
+int duo_engine_capture_resid(duo_engine* e, int layer, float* out);
 /* setVectors(rows) (model.js:372-376): vecs_host [n_rows, hidden]; rows >= n_rows get zero vectors. */
 int duo_engine_set_vectors(duo_engine* e, const float* vecs_host, int n_rows, duo_stream stream);
 /* setHeadScales (model.js:362-369) for one linear-attention layer; NULL restores all ones. */
@@ -172,6 +183,16 @@ int duo_engine_argmax(duo_engine* e, int row0, int n, int32_t* out, duo_stream s
 int duo_engine_generate(duo_engine* e, int n_steps, int vec_layer, int32_t* tokens_out, duo_stream stream);
 /* Tokens held so far by row r (this.len[r] in model.js), or a negative status. */
 int duo_engine_row_len(duo_engine* e, int row);
+
+/* Live per-kernel-class timing with CUDA events on the launching stream (the reference only times whole steps,
+ * tests/profile.html:19-45).  mask = OR of (1 << DUO_PROF_*) classes to time, 0 = off.  Reading synchronises the
+ * device, writes the summed milliseconds and launch counts per class (arrays of DUO_PROF_KINDS) and clears them. */
+enum duo_prof_kind {
+  DUO_PROF_GATHER = 0, DUO_PROF_RMSNORM, DUO_PROF_GEMV, DUO_PROF_GEMM, DUO_PROF_GDN_CONV, DUO_PROF_GDN_SCAN,
+  DUO_PROF_ATTN_PREP, DUO_PROF_ATTN, DUO_PROF_SWIGLU, DUO_PROF_OTHER, DUO_PROF_KINDS
+};
+int duo_engine_profile(duo_engine* e, unsigned mask);
+int duo_engine_profile_read(duo_engine* e, double* ms_out, long long* launches_out);
 
 #ifdef __cplusplus
 }

@@ -90,13 +90,13 @@ def test_gemm_bf16(ops, m, n, k):
     b = (torch.randn(n, k, generator=_seed(n)) * 0.05).to(torch.bfloat16)
     ref = a.float() @ b.float().T
     c = ops.gemm_bf16(a.cuda(), b.cuda(), out_dtype=torch.float32)
-    assert rel_max(c, ref) < 1e-5
+    assert rel_max(c, ref) < 1e-5 * max(1.0, k / 1024)  # f32 summation order over k terms
     cb = ops.gemm_bf16(a.cuda(), b.cuda(), out_dtype=torch.bfloat16)
     assert rel_max(cb.float(), ref) < 8e-3
     cs = torch.rand(n, generator=_seed(1)) + 0.5
     x0 = torch.randn(m, n, generator=_seed(2))
     acc = ops.gemm_bf16(a.cuda(), b.cuda(), col_scale=cs.cuda(), out=x0.clone().cuda(), accumulate=True)
-    assert rel_max(acc, x0 + ref * cs) < 1e-5
+    assert rel_max(acc, x0 + ref * cs) < 1e-5 * max(1.0, k / 1024)
     assert ops.fault_status() == 0
 
 
