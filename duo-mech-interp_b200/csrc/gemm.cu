@@ -28,48 +28,6 @@ __device__ __forceinline__ float push_apply(const PushTable& pt, int r, int n, f
   return v;
 }
 
-// 32 consecutive accumulator columns n0 .. n0 + 31 of output row m (already scaled), for STORE / ADD
-__device__ __forceinline__ void epi_row32(const GemmEpiArgs& ep, int m, int n0, int N, const float* v) {
-  const long off = (long)m * ep.ldc + n0;
-  const bool full = n0 + 32 <= N;
-  if (ep.epi == EPI_STORE) {
-    if (ep.c_dtype == DUO_BF16) {
-      __nv_bfloat16* c = static_cast<__nv_bfloat16*>(ep.c) + off;
-      if (full && (((uintptr_t)c) & 15) == 0) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) store8(c + j, v + j);
-      } else {
-        for (int j = 0; j < 32 && n0 + j < N; j++) c[j] = __float2bfloat16_rn(v[j]);
-      }
-    } else {
-      float* c = static_cast<float*>(ep.c) + off;
-      if (full && (((uintptr_t)c) & 15) == 0) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) store8(c + j, v + j);
-      } else {
-        for (int j = 0; j < 32 && n0 + j < N; j++) c[j] = v[j];
-      }
-    }
-  } else {  // EPI_ADD_F32
-    float* x = static_cast<float*>(ep.c) + off;
-    const float* vr = ep.vec ? ep.vec + (long)(ep.row_base + m / ep.t) * ep.ldc + n0 : nullptr;
-    if (full && (((uintptr_t)x) & 15) == 0) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float4 o = *reinterpret_cast<float4*>(x + j);
-        o.x += v[j]; o.y += v[j + 1]; o.z += v[j + 2]; o.w += v[j + 3];
-        if (vr) {
-          const float4 a = *reinterpret_cast<const float4*>(vr + j);
-          o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
-        }
-        *reinterpret_cast<float4*>(x + j) = o;
-      }
-    } else {
-      for (int j = 0; j < 32 && n0 + j < N; j++) x[j] += v[j] + (vr ? vr[j] : 0.f);
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------------------------------------------
 // tcgen05 GEMM.  CTA tile 128 x BN, K step 64 (one 128-byte swizzle row of bf16), STAGES-deep TMA ring.
 // Warp 0: TMA producer (one lane).  Warp 1: TMEM allocator and MMA issuer (one lane).  Warps 2-5: epilogue, one
@@ -98,14 +56,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* tmem_full = empty + C::STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
-  __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_n = blockIdx.x * BN, tile_m = blockIdx.y * TC_BM;
   const int num_k = K / TC_BK;
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
     for (int s = 0; s < C::STAGES; s++) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
@@ -127,7 +83,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t ph = (kb / C::STAGES) & 1;
       if (kb >= C::STAGES && !tc::mbar_wait(&empty[s], ph ^ 1)) {
         atomicOr(fault, 1u);
-        s_abort = 1;
         break;
       }
       tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
@@ -155,57 +110,96 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::mma_commit(&empty[s]);
     }
     if (ok) tc::mma_commit(tmem_full);
-    else s_abort = 1;
   } else if (warp >= 2) {
+    // Epilogue in two passes.  (1) Each warp moves its 32 accumulator rows TMEM -> registers -> (scaled, and for
+    // SwiGLU combined) f32 rows of a shared-memory tile that reuses the pipeline buffers, idle once every MMA has
+    // completed.  (2) The four warps sweep the tile row by row with consecutive lanes on consecutive columns, so every
+    // global load / store of the output (and the residual read-modify-write) is coalesced.
+    constexpr int NC = (EPI == EPI_SWIGLU) ? BN / 2 : BN;  // output columns of this tile
+    constexpr int P = NC + 4;                               // row pitch: rows start 4 banks apart
+    float* stile = reinterpret_cast<float*>(smem);
     const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31 belong to this warp
-    const int m = tile_m + quad * 32 + lane;
+    const int row = quad * 32 + lane;
     const bool ok = tc::mbar_wait(tmem_full, 0);
     if (!ok) {
       if (lane == 0) atomicOr(fault, 4u);
     } else {
       tc::fence_after_sync();
       const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-      if (EPI == EPI_SWIGLU) {
-        // columns [0, 128) are gate rows j0 .. j0+127 and [128, 256) the matching up rows (BN == 256)
-        const int j0 = tile_n / 2;
-        const int inter = N / 2;
+      float* srow = stile + row * P;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
-          float g[32], u[32];
-          tc::tmem_ld32(trow + c0, g);
+      for (int c0 = 0; c0 < NC; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(trow + c0, v);
+        if (EPI == EPI_SWIGLU) {
+          // columns [0, BN/2) are gate rows j0 .. and [BN/2, BN) the matching up rows
+          float u[32];
           tc::tmem_ld32(trow + BN / 2 + c0, u);
-          if (m < M) {
-            const int r = ep.row_base + m / ep.t;
-            float a[32];
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-              const float gs = ep.colscale ? g[j] * ep.colscale[tile_n + c0 + j] : g[j];
-              const float us = ep.colscale ? u[j] * ep.colscale[tile_n + BN / 2 + c0 + j] : u[j];
-              a[j] = siluf_(gs) * us;
-            }
-            if (ep.push.count) {
-              for (int j = 0; j < 32; j++) a[j] = push_apply(ep.push, r, j0 + c0 + j, a[j]);
-            }
-            __nv_bfloat16* out = static_cast<__nv_bfloat16*>(ep.c) + (long)m * ep.ldc + j0 + c0;
-            if (j0 + c0 + 32 <= inter) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) store8(out + j, a + j);
-            } else {
-              for (int j = 0; j < 32 && j0 + c0 + j < inter; j++) out[j] = __float2bfloat16_rn(a[j]);
-            }
+          for (int j = 0; j < 32; j++) {
+            const float gs = ep.colscale ? v[j] * ep.colscale[tile_n + c0 + j] : v[j];
+            const float us = ep.colscale ? u[j] * ep.colscale[tile_n + BN / 2 + c0 + j] : u[j];
+            v[j] = siluf_(gs) * us;
           }
-        }
-      } else {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          float v[32];
-          tc::tmem_ld32(trow + c0, v);
-          if (m < M && tile_n + c0 < N) {
-            if (ep.colscale) {
+        } else if (ep.colscale) {
 #pragma unroll
-              for (int j = 0; j < 32; j++) v[j] *= (tile_n + c0 + j < N) ? ep.colscale[tile_n + c0 + j] : 0.f;
+          for (int j = 0; j < 32; j++) v[j] *= (tile_n + c0 + j < N) ? ep.colscale[tile_n + c0 + j] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(srow + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+    if (ok) {
+      const int ew = warp - 2;
+      const int n0 = (EPI == EPI_SWIGLU) ? tile_n / 2 : tile_n;  // first output column of the tile
+      const int ncols = (EPI == EPI_SWIGLU) ? N / 2 : N;          // output width
+      const bool al = ((reinterpret_cast<uintptr_t>(ep.c) & 15) == 0) && (ep.ldc % 4 == 0);
+      for (int rr = ew; rr < TC_BM; rr += 4) {
+        const int m = tile_m + rr;
+        if (m >= M) break;
+        const int r = ep.row_base + m / ep.t;
+        const float* srow = stile + rr * P;
+        for (int c = lane * 4; c < NC; c += 128) {
+          const int n = n0 + c;
+          if (n >= ncols) break;
+          float4 v = *reinterpret_cast<const float4*>(srow + c);
+          float x[4] = {v.x, v.y, v.z, v.w};
+          const long off = (long)m * ep.ldc + n;
+          const bool vec4 = al && n + 4 <= ncols;
+          if (EPI == EPI_SWIGLU && ep.push.count) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) x[i] = push_apply(ep.push, r, n + i, x[i]);
+          }
+          if (EPI == EPI_ADD_F32) {
+            float* X = static_cast<float*>(ep.c) + off;
+            const float* vr = ep.vec ? ep.vec + (long)r * ep.ldc + n : nullptr;
+            if (vec4) {
+              float4 o = *reinterpret_cast<float4*>(X);
+              o.x += x[0]; o.y += x[1]; o.z += x[2]; o.w += x[3];
+              if (vr) {
+                const float4 a = *reinterpret_cast<const float4*>(vr);
+                o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
+              }
+              *reinterpret_cast<float4*>(X) = o;
+            } else {
+              for (int i = 0; i < 4 && n + i < ncols; i++) X[i] += x[i] + (vr ? vr[i] : 0.f);
             }
-            epi_row32(ep, m, tile_n + c0, N, v);
+          } else if (ep.c_dtype == DUO_BF16) {
+            __nv_bfloat16* C = static_cast<__nv_bfloat16*>(ep.c) + off;
+            if (vec4) {
+              __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+              uint2 u;
+              u.x = *reinterpret_cast<uint32_t*>(&lo);
+              u.y = *reinterpret_cast<uint32_t*>(&hi);
+              *reinterpret_cast<uint2*>(C) = u;
+            } else {
+              for (int i = 0; i < 4 && n + i < ncols; i++) C[i] = __float2bfloat16_rn(x[i]);
+            }
+          } else {
+            float* C = static_cast<float*>(ep.c) + off;
+            if (vec4) *reinterpret_cast<float4*>(C) = make_float4(x[0], x[1], x[2], x[3]);
+            else for (int i = 0; i < 4 && n + i < ncols; i++) C[i] = x[i];
           }
         }
       }
