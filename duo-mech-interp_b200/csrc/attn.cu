@@ -5,6 +5,7 @@
 // inv_freq = theta^(-2j/rot), softmax(q k^T / sqrt(hd)) v with repeat_kv, output times sigmoid(gate)).
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "kernels.cuh"
 
@@ -300,6 +301,10 @@ long attn_work_floats(int b, int nh, int max_len) {
 
 template <typename T>
 static int run_attention(const AttnArgs& a, cudaStream_t st) {
+  if (std::is_same<T, __nv_bfloat16>::value && a.t > 1) {
+    const int rep = a.nh / a.nkv;
+    if (rep == 1 || rep == 2 || rep == 4) return launch_attn_prefill_mma(a, st);  // tensor cores
+  }
   if (a.t == 1) {
     int ns, sl;
     decode_plan(a, &ns, &sl);

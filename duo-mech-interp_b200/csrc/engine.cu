@@ -221,7 +221,9 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       sa.z = static_cast<const char*>(e->y) + (size_t)e->conv_dim * es;
       sa.z_stride = wproj;
       sa.norm_w = L.gnorm; sa.head_scale = S.head_scale; sa.eps = c.eps;
-      PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_recurrent(sa, act, st));
+      // prefill of the bf16 engine: chunked tensor-core scan; decode and the f32 engine: the recurrent form
+      if (act == DUO_BF16 && T > 16) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
+      else PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_recurrent(sa, act, st));
       out_k = e->vd;
     } else {
       AttnPrepArgs pa{};

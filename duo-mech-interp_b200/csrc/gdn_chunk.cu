@@ -1,0 +1,427 @@
+// Gated DeltaNet token mixer, part 2: the chunked (WY / UT-transform) scan for prefill.
+//
+// Chunk form of the gated delta rule, as published with the PyTorch path the reference runs (transformers
+// torch_chunk_gated_delta_rule, chunk 64).  Per chunk of C = 64 tokens with cumulative log-decay G (inclusive cumsum
+// of g inside the chunk):
+//   L[i, j] = beta_i (k_i . k_j) exp(G_i - G_j) for j < i,   T = (I + L)^-1            (unit lower triangular)
+//   U = T diag(beta) V,   W = T diag(beta e^G) K
+//   V' = U - W S,   O = diag(e^G) Q S + tril(Q K^T * exp(G_i - G_j)) V'
+//   S <- e^{G_63} S + (diag(e^{G_63 - G}) K)^T V'
+// One CTA (8 warps) owns one (row, value head) and walks its chunks in order.  The 64 x 64 and 64 x 128 products and
+// the 128 x 128 state update run on the tensor cores (bf16 operands, f32 accumulation); the state lives in registers
+// as f32 accumulators for the whole sequence and is rounded to bf16 only as an operand copy.  T is formed in f32 by
+// blocked forward substitution (16 x 16 diagonal blocks, then the off-diagonal blocks by distance).  The gated
+// RMSNorm of the engine path is fused into the output.
+#include "kernels.cuh"
+#include "mma.cuh"
+
+namespace duo {
+
+namespace {
+
+constexpr int CK = 64;         // chunk length
+constexpr int PD = 128 + 8;    // pitch (elements) of the 128-wide bf16 tiles
+constexpr int PC = 64 + 8;     // pitch of the 64-wide bf16 tiles
+constexpr int PF = 64 + 1;     // pitch of the f32 64 x 64 tiles
+
+struct ChunkSmem {
+  __nv_bfloat16 q[CK * PD], k[CK * PD], v[CK * PD];  // chunk inputs (q scaled by 1/sqrt(dk))
+  __nv_bfloat16 w[CK * PD];                          // W
+  __nv_bfloat16 vn[CK * PD];                         // V'
+  __nv_bfloat16 vd[CK * PD];                         // diag(e^{G_63 - G}) V'
+  __nv_bfloat16 s[128 * PD];                         // bf16 copy of the state [dk][dv]
+  __nv_bfloat16 aq[CK * PC];                         // tril(Q K^T) * decay
+  __nv_bfloat16 t1[CK * PC], t2[CK * PC];            // T diag(beta), T diag(beta e^G)
+  float a[CK * PF];                                  // L (strictly lower), f32
+  float t[CK * PF];                                  // T = (I + L)^-1, f32
+  float x[3 * 16 * 17];                              // off-diagonal solve scratch
+  float gcum[CK], eg[CK], egl[CK], beta[CK];
+  float rowss[2][CK];                                // gated-norm partial sums (two column halves)
+};
+
+template <typename T> __device__ __forceinline__ void ld4f(const T* p, float* o);
+template <> __device__ __forceinline__ void ld4f<float>(const float* p, float* o) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+}
+template <> __device__ __forceinline__ void ld4f<__nv_bfloat16>(const __nv_bfloat16* p, float* o) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+}
+
+__device__ __forceinline__ void st4bf(__nv_bfloat16* p, const float* v) {
+  uint2 u;
+  u.x = wm::pack_bf16(v[0], v[1]);
+  u.y = wm::pack_bf16(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+}  // namespace
+
+template <typename TI, bool NORM>
+__global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  ChunkSmem& sm = *reinterpret_cast<ChunkSmem*>(smem_raw);
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q4 = lane & 3;
+  const int kh = h / (a.h / a.hq);
+  const TI* qp = static_cast<const TI*>(a.q);
+  const TI* kp = static_cast<const TI*>(a.k);
+  const TI* vp = static_cast<const TI*>(a.v);
+  float* Sg = a.state + (((long)(a.state_row0 + b) * a.h + h) * 128) * 128;
+  const float qscale = rsqrtf(128.f);
+
+  // state: warp w owns dk rows 16w .. 16w + 15, all 128 dv columns (16 n-tiles of 8)
+  float S[16][4];
+  {
+    const int r0 = warp * 16 + g;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const int c = 8 * j + 2 * q4;
+      const float2 lo = *reinterpret_cast<const float2*>(Sg + (long)r0 * 128 + c);
+      const float2 hi = *reinterpret_cast<const float2*>(Sg + (long)(r0 + 8) * 128 + c);
+      S[j][0] = lo.x; S[j][1] = lo.y; S[j][2] = hi.x; S[j][3] = hi.y;
+      *reinterpret_cast<uint32_t*>(sm.s + r0 * PD + c) = wm::pack_bf16(lo.x, lo.y);
+      *reinterpret_cast<uint32_t*>(sm.s + (r0 + 8) * PD + c) = wm::pack_bf16(hi.x, hi.y);
+    }
+  }
+
+  const int nchunks = (a.t + CK - 1) / CK;
+  for (int c = 0; c < nchunks; c++) {
+    const int t0 = c * CK;
+    __syncthreads();  // previous chunk's readers are done with every tile
+    // ---- load the chunk: one warp per token row, 4 values per lane; padded tokens are zero (g = beta = 0)
+    for (int r = warp; r < CK; r += 8) {
+      const int t = t0 + r;
+      float qv[4] = {0, 0, 0, 0}, kv[4] = {0, 0, 0, 0}, vv[4] = {0, 0, 0, 0};
+      if (t < a.t) {
+        const long m = (long)b * a.t + t;
+        ld4f(qp + m * a.q_stride + kh * 128 + lane * 4, qv);
+        ld4f(kp + m * a.k_stride + kh * 128 + lane * 4, kv);
+        ld4f(vp + m * a.v_stride + h * 128 + lane * 4, vv);
+        if (a.l2norm_qk) {
+          const float sq = warp_sum(qv[0] * qv[0] + qv[1] * qv[1] + qv[2] * qv[2] + qv[3] * qv[3]);
+          const float sk = warp_sum(kv[0] * kv[0] + kv[1] * kv[1] + kv[2] * kv[2] + kv[3] * kv[3]);
+          const float iq = rsqrtf(sq + 1e-6f), ik = rsqrtf(sk + 1e-6f);
+#pragma unroll
+          for (int i = 0; i < 4; i++) { qv[i] *= iq; kv[i] *= ik; }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) qv[i] *= qscale;
+      }
+      st4bf(sm.q + r * PD + lane * 4, qv);
+      st4bf(sm.k + r * PD + lane * 4, kv);
+      st4bf(sm.v + r * PD + lane * 4, vv);
+    }
+    if (tid < CK) {
+      const int t = t0 + tid;
+      const long m = (long)b * a.t + t;
+      sm.gcum[tid] = t < a.t ? a.g[m * a.h + h] : 0.f;
+      sm.beta[tid] = t < a.t ? a.beta[m * a.h + h] : 0.f;
+    }
+    __syncthreads();
+    // ---- cumulative decay (warp 0) while the other warps start on Q K^T and K K^T
+    if (warp == 0) {
+      const float g0 = sm.gcum[2 * lane], g1 = sm.gcum[2 * lane + 1];
+      float s = g0 + g1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += n;
+      }
+      const float excl = s - g0 - g1;
+      const float G0 = excl + g0, G1 = excl + g0 + g1;
+      const float Gl = __shfl_sync(0xffffffffu, G1, 31);
+      sm.gcum[2 * lane] = G0;
+      sm.gcum[2 * lane + 1] = G1;
+      sm.eg[2 * lane] = expf(G0);
+      sm.eg[2 * lane + 1] = expf(G1);
+      sm.egl[2 * lane] = expf(Gl - G0);
+      sm.egl[2 * lane + 1] = expf(Gl - G1);
+    }
+    // Q K^T and K K^T, 64 x 64 each: warp tile 16 rows x 32 columns
+    float qk[4][4], kk[4][4];
+    {
+      const int wr = (warp & 3) * 16, wc = (warp >> 2) * 32;
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) qk[j][e] = kk[j][e] = 0.f;
+#pragma unroll
+      for (int k0 = 0; k0 < 128; k0 += 16) {
+        uint32_t aq[4], ak[4], bf[2][4];
+        wm::lda(aq, sm.q, PD, wr, k0);
+        wm::lda(ak, sm.k, PD, wr, k0);
+        wm::ldb_nk(bf[0], sm.k, PD, wc, k0);
+        wm::ldb_nk(bf[1], sm.k, PD, wc + 16, k0);
+#pragma unroll
+        for (int jj = 0; jj < 2; jj++) {
+          wm::mma(qk[2 * jj], aq, bf[jj]);
+          wm::mma(qk[2 * jj + 1], aq, bf[jj] + 2);
+          wm::mma(kk[2 * jj], ak, bf[jj]);
+          wm::mma(kk[2 * jj + 1], ak, bf[jj] + 2);
+        }
+      }
+    }
+    __syncthreads();  // G ready
+    {
+      const int wr = (warp & 3) * 16, wc = (warp >> 2) * 32;
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int i = wr + g + (e >> 1) * 8, jc = wc + 8 * j + 2 * q4 + (e & 1);
+          const float dec = jc <= i ? expf(sm.gcum[i] - sm.gcum[jc]) : 0.f;
+          sm.a[i * PF + jc] = jc < i ? sm.beta[i] * kk[j][e] * dec : 0.f;
+          sm.aq[i * PC + jc] = __float2bfloat16_rn(qk[j][e] * dec);
+          sm.t[i * PF + jc] = 0.f;
+        }
+    }
+    __syncthreads();
+    // ---- T = (I + L)^-1: 16 x 16 diagonal blocks by forward substitution (warp b, lane = column) ...
+    if (warp < 4 && lane < 16) {
+      const int o = warp * 16, col = lane;
+      for (int i = 0; i < 16; i++) {
+        float v = (i == col) ? 1.f : 0.f;
+        for (int j = col; j < i; j++) v -= sm.a[(o + i) * PF + o + j] * sm.t[(o + j) * PF + o + col];
+        sm.t[(o + i) * PF + o + col] = v;
+      }
+    }
+    __syncthreads();
+    // ... then the off-diagonal blocks by distance: T[bi][bj] = -T[bi][bi] sum_{bj <= bk < bi} L[bi][bk] T[bk][bj]
+    for (int d = 1; d < 4; d++) {
+      const int nb = 4 - d;
+      for (int e = tid; e < nb * 256; e += 256) {
+        const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15, bi = bj + d;
+        float x = 0.f;
+        for (int bk = bj; bk < bi; bk++)
+#pragma unroll 4
+          for (int kk2 = 0; kk2 < 16; kk2++)
+            x += sm.a[(bi * 16 + r) * PF + bk * 16 + kk2] * sm.t[(bk * 16 + kk2) * PF + bj * 16 + cc];
+        sm.x[bj * 272 + r * 17 + cc] = x;
+      }
+      __syncthreads();
+      for (int e = tid; e < nb * 256; e += 256) {
+        const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15, bi = bj + d;
+        float y = 0.f;
+#pragma unroll 4
+        for (int kk2 = 0; kk2 <= r; kk2++) y += sm.t[(bi * 16 + r) * PF + bi * 16 + kk2] * sm.x[bj * 272 + kk2 * 17 + cc];
+        sm.t[(bi * 16 + r) * PF + bj * 16 + cc] = -y;
+      }
+      __syncthreads();
+    }
+    // T1 = T diag(beta), T2 = T diag(beta e^G) in bf16
+    for (int e = tid; e < CK * CK; e += 256) {
+      const int i = e >> 6, j = e & 63;
+      const float tv = sm.t[i * PF + j];
+      sm.t1[i * PC + j] = __float2bfloat16_rn(tv * sm.beta[j]);
+      sm.t2[i * PC + j] = __float2bfloat16_rn(tv * sm.beta[j] * sm.eg[j]);
+    }
+    __syncthreads();
+    // ---- U = T1 V and W = T2 K (64 x 128, K = 64): warp tile 16 rows x 64 columns
+    const int wr = (warp & 3) * 16, wc = (warp >> 2) * 64;
+    float U[8][4], Wt[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) U[j][e] = Wt[j][e] = 0.f;
+#pragma unroll
+    for (int k0 = 0; k0 < CK; k0 += 16) {
+      uint32_t a1[4], a2[4];
+      wm::lda(a1, sm.t1, PC, wr, k0);
+      wm::lda(a2, sm.t2, PC, wr, k0);
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        uint32_t bv[4], bk[4];
+        wm::ldb_kn(bv, sm.v, PD, wc + 16 * jj, k0);
+        wm::ldb_kn(bk, sm.k, PD, wc + 16 * jj, k0);
+        wm::mma(U[2 * jj], a1, bv);
+        wm::mma(U[2 * jj + 1], a1, bv + 2);
+        wm::mma(Wt[2 * jj], a2, bk);
+        wm::mma(Wt[2 * jj + 1], a2, bk + 2);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int cc = wc + 8 * j + 2 * q4;
+      *reinterpret_cast<uint32_t*>(sm.w + (wr + g) * PD + cc) = wm::pack_bf16(Wt[j][0], Wt[j][1]);
+      *reinterpret_cast<uint32_t*>(sm.w + (wr + g + 8) * PD + cc) = wm::pack_bf16(Wt[j][2], Wt[j][3]);
+    }
+    __syncthreads();
+    // ---- W S and Q S (64 x 128, K = 128); V' = U - W S; O = diag(e^G) Q S
+    float O[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) { Wt[j][e] = 0.f; O[j][e] = 0.f; }
+#pragma unroll
+    for (int k0 = 0; k0 < 128; k0 += 16) {
+      uint32_t aw[4], aq2[4];
+      wm::lda(aw, sm.w, PD, wr, k0);
+      wm::lda(aq2, sm.q, PD, wr, k0);
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        uint32_t bs[4];
+        wm::ldb_kn(bs, sm.s, PD, wc + 16 * jj, k0);
+        wm::mma(Wt[2 * jj], aw, bs);
+        wm::mma(Wt[2 * jj + 1], aw, bs + 2);
+        wm::mma(O[2 * jj], aq2, bs);
+        wm::mma(O[2 * jj + 1], aq2, bs + 2);
+      }
+    }
+    {
+      const float e0 = sm.eg[wr + g], e1 = sm.eg[wr + g + 8];
+      const float l0 = sm.egl[wr + g], l1 = sm.egl[wr + g + 8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int cc = wc + 8 * j + 2 * q4;
+        const float v0 = U[j][0] - Wt[j][0], v1 = U[j][1] - Wt[j][1];
+        const float v2 = U[j][2] - Wt[j][2], v3 = U[j][3] - Wt[j][3];
+        *reinterpret_cast<uint32_t*>(sm.vn + (wr + g) * PD + cc) = wm::pack_bf16(v0, v1);
+        *reinterpret_cast<uint32_t*>(sm.vn + (wr + g + 8) * PD + cc) = wm::pack_bf16(v2, v3);
+        *reinterpret_cast<uint32_t*>(sm.vd + (wr + g) * PD + cc) = wm::pack_bf16(v0 * l0, v1 * l0);
+        *reinterpret_cast<uint32_t*>(sm.vd + (wr + g + 8) * PD + cc) = wm::pack_bf16(v2 * l1, v3 * l1);
+        O[j][0] *= e0; O[j][1] *= e0; O[j][2] *= e1; O[j][3] *= e1;
+      }
+    }
+    __syncthreads();
+    // ---- O += tril(QK^T decay) V' (K = 64)
+#pragma unroll
+    for (int k0 = 0; k0 < CK; k0 += 16) {
+      uint32_t aa[4];
+      wm::lda(aa, sm.aq, PC, wr, k0);
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        uint32_t bv[4];
+        wm::ldb_kn(bv, sm.vn, PD, wc + 16 * jj, k0);
+        wm::mma(O[2 * jj], aa, bv);
+        wm::mma(O[2 * jj + 1], aa, bv + 2);
+      }
+    }
+    // ---- state update S = e^{G_63} S + K^T diag(e^{G_63 - G}) V' (128 x 128, K = 64); rows 16w ..
+    {
+      const float el = sm.eg[CK - 1];
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) S[j][e] *= el;
+#pragma unroll
+      for (int k0 = 0; k0 < CK; k0 += 16) {
+        uint32_t ak[4];
+        wm::lda_t(ak, sm.k, PD, warp * 16, k0);
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) {
+          uint32_t bv[4];
+          wm::ldb_kn(bv, sm.vd, PD, 16 * jj, k0);
+          wm::mma(S[2 * jj], ak, bv);
+          wm::mma(S[2 * jj + 1], ak, bv + 2);
+        }
+      }
+    }
+    // ---- output rows (optionally the gated RMSNorm over the 128 columns of the head)
+    if (NORM) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        s0 += O[j][0] * O[j][0] + O[j][1] * O[j][1];
+        s1 += O[j][2] * O[j][2] + O[j][3] * O[j][3];
+      }
+      s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+      s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+      if (q4 == 0) {
+        sm.rowss[warp >> 2][wr + g] = s0;
+        sm.rowss[warp >> 2][wr + g + 8] = s1;
+      }
+    }
+    __syncthreads();  // every warp is past its reads of sm.s; row sums are in
+    // write the new bf16 state copy for the next chunk
+    {
+      const int r0 = warp * 16 + g;
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int cc = 8 * j + 2 * q4;
+        *reinterpret_cast<uint32_t*>(sm.s + r0 * PD + cc) = wm::pack_bf16(S[j][0], S[j][1]);
+        *reinterpret_cast<uint32_t*>(sm.s + (r0 + 8) * PD + cc) = wm::pack_bf16(S[j][2], S[j][3]);
+      }
+    }
+    {
+      TI* op = static_cast<TI*>(a.o);
+      const TI* zp = static_cast<const TI*>(a.z);
+      const float hs = (NORM && a.head_scale) ? a.head_scale[h] : 1.f;
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+        const int i = wr + g + half * 8;
+        const int t = t0 + i;
+        if (t >= a.t) continue;
+        const long m = (long)b * a.t + t;
+        float rms = 1.f;
+        if (NORM) rms = rsqrtf((sm.rowss[0][i] + sm.rowss[1][i]) / 128.f + a.eps);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const int cc = wc + 8 * j + 2 * q4;
+          float o0 = O[j][half * 2], o1 = O[j][half * 2 + 1];
+          if (NORM) {
+            const float z0 = to_f(zp[m * a.z_stride + h * 128 + cc]), z1 = to_f(zp[m * a.z_stride + h * 128 + cc + 1]);
+            o0 = o0 * rms * a.norm_w[cc] * siluf_(z0) * hs;
+            o1 = o1 * rms * a.norm_w[cc + 1] * siluf_(z1) * hs;
+          }
+          op[m * a.o_stride + h * 128 + cc] = from_f<TI>(o0);
+          op[m * a.o_stride + h * 128 + cc + 1] = from_f<TI>(o1);
+        }
+      }
+    }
+  }
+  // final state (f32)
+  {
+    const int r0 = warp * 16 + g;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const int cc = 8 * j + 2 * q4;
+      *reinterpret_cast<float2*>(Sg + (long)r0 * 128 + cc) = make_float2(S[j][0], S[j][1]);
+      *reinterpret_cast<float2*>(Sg + (long)(r0 + 8) * 128 + cc) = make_float2(S[j][2], S[j][3]);
+    }
+  }
+}
+
+template <typename TI, bool NORM>
+static int run_chunk(const GdnScanArgs& a, cudaStream_t st) {
+  static bool attr = false;
+  const int smem = (int)sizeof(ChunkSmem);
+  if (!attr) {
+    DUO_CUDA_TRY(cudaFuncSetAttribute(gdn_chunk_kernel<TI, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  gdn_chunk_kernel<TI, NORM><<<dim3(a.h, a.b), 256, smem, st>>>(a);
+  DUO_LAUNCH_CHECK("gdn_chunk_kernel");
+  return DUO_OK;
+}
+
+int launch_gdn_chunk(const GdnScanArgs& a, int dtype, cudaStream_t st) {
+  if (a.b == 0 || a.t == 0) return DUO_OK;
+  if (a.dk != 128 || a.dv != 128) return fail(DUO_EINVAL, "gdn_chunk: needs dk = dv = 128");
+  if (a.hq <= 0 || a.h % a.hq) return fail(DUO_EINVAL, "gdn_chunk: value heads must be a multiple of q/k heads");
+  if ((a.q_stride | a.k_stride | a.v_stride) % 4)
+    return fail(DUO_EINVAL, "gdn_chunk: q/k/v token strides must be multiples of 4 elements");
+  const bool norm = a.norm_w != nullptr;
+  if (dtype == DUO_F32) return norm ? run_chunk<float, true>(a, st) : run_chunk<float, false>(a, st);
+  return norm ? run_chunk<__nv_bfloat16, true>(a, st) : run_chunk<__nv_bfloat16, false>(a, st);
+}
+
+}  // namespace duo
+
+using namespace duo;
+
+extern "C" int duo_gdn_chunk_fwd(const void* q, const void* k, const void* v, int in_dtype, const float* g,
+                                 const float* beta, float* state, void* o, int o_dtype, int b, int t, int h, int dk,
+                                 int dv, int l2norm_qk, duo_stream stream) {
+  DUO_CHECK_ARG(b >= 0 && t >= 0 && h > 0, "gdn_chunk: bad shape");
+  DUO_CHECK_ARG(dk == 128 && dv == 128, "gdn_chunk: dk and dv must be 128");
+  DUO_CHECK_ARG(valid_act(in_dtype) && o_dtype == in_dtype, "gdn_chunk: q/k/v/o dtype must be f32 or bf16 (the same)");
+  DUO_CHECK_ARG(b == 0 || t == 0 || (q && k && v && g && beta && state && o), "gdn_chunk: null pointer");
+  return launch_gdn_chunk(op_scan_args(q, k, v, g, beta, state, o, b, t, h, l2norm_qk), in_dtype, as_stream(stream));
+}

@@ -120,6 +120,7 @@ struct AttnArgs {
 };
 int launch_attention(const AttnArgs& a, int dtype, cudaStream_t st);
 long attn_work_floats(int b, int nh, int max_len);
+int launch_attn_prefill_mma(const AttnArgs& a, cudaStream_t st);  // bf16, t > 1, hd 256
 
 // int8 -> bf16 copy of a weight matrix for the tensor-core GEMM: dst row of src row n is n, or (interleave > 0) the
 // gate/up interleaved order [gate 128 | up 128]* with `interleave` = rows of each half.  apply_scale = 0 writes

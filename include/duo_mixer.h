@@ -96,6 +96,14 @@ int duo_gdn_recurrent_fwd(const void* q, const void* k, const void* v, int in_dt
                           const float* beta, float* state, void* o, int o_dtype, int b, int t, int h, int dk, int dv,
                           int l2norm_qk, duo_stream stream);
 
+/* Same contract as duo_gdn_recurrent_fwd, computed in the chunked WY / UT form (chunk 64) on the tensor cores: bf16
+ * operands, f32 accumulation, f32 state.  f32 inputs are rounded to bf16 on load.  This is the prefill form of the
+ * reference's PyTorch path (transformers torch_chunk_gated_delta_rule); the reference's own WGSL engine runs prefill
+ * token by token in `delta` (engine/kernels_qwen35.js:183-247). */
+int duo_gdn_chunk_fwd(const void* q, const void* k, const void* v, int in_dtype, const float* g, const float* beta,
+                      float* state, void* o, int o_dtype, int b, int t, int h, int dk, int dv, int l2norm_qk,
+                      duo_stream stream);
+
 /* Causal GQA softmax attention of b rows over their caches.  q [b, t, nh, hd] holds the t new queries of each row,
  * which sit at cache positions start[r] .. start[r] + t - 1; kc, vc [b, max_len, nkv, hd] hold keys / values
  * 0 .. start[r] + t - 1.  o[b, t, nh, hd] = softmax(q k^T * scale) v, times sigmoid(gate[b, t, nh, hd]) when gate is

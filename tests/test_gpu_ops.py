@@ -161,6 +161,30 @@ def test_gdn_recurrent_bf16(ops):
     assert rel_max(st, rs) < 1e-3
 
 
+@pytest.mark.parametrize("b,t,h,l2", [(1, 64, 2, False), (2, 100, 4, True), (1, 300, 16, False), (3, 17, 2, True),
+                                      (2, 1024, 16, False)])
+def test_gdn_chunk_bf16(ops, b, t, h, l2):
+    """Chunked tensor-core scan vs the oracle's chunk rule (f64) on the same bf16-rounded inputs; bf16 bound 2e-2."""
+    q, k, v, g, beta, s0 = _gdn_inputs(b, t, h, 1000 + t, not l2)
+    qb, kb, vb = (x.to(torch.bfloat16) for x in (q, k, v))
+    ro, rs = mixer.chunk_gated_delta_rule(qb.double(), kb.double(), vb.double(), g.double(), beta.double(),
+                                          state=s0.double(), l2norm_qk=l2)
+    st = s0.clone().cuda()
+    o = ops.gdn_chunk(qb.cuda(), kb.cuda(), vb.cuda(), g.cuda(), beta.cuda(), st, l2norm_qk=l2)
+    assert rel_max(o.float(), ro) < 2e-2
+    assert rel_max(st, rs) < 2e-2
+
+
+def test_gdn_chunk_matches_recurrent_kernel(ops):
+    """The two GPU forms of the scan agree (f32 inputs; the chunk kernel rounds its operands to bf16)."""
+    q, k, v, g, beta, s0 = _gdn_inputs(2, 200, 16, 4242, True)
+    st1, st2 = s0.clone().cuda(), s0.clone().cuda()
+    o1 = ops.gdn_recurrent(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), st1, l2norm_qk=False)
+    o2 = ops.gdn_chunk(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), st2, l2norm_qk=False)
+    assert rel_max(o2, o1) < 2e-2
+    assert rel_max(st2, st1) < 2e-2
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # attention (kernels_qwen35.js:73-123; transformers eager attention with repeat_kv, sigmoid gate)
 
@@ -177,11 +201,13 @@ def _attn_ref(q, kc, vc, start, gate):
 
 
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2)])
-@pytest.mark.parametrize("b,t,starts,max_len", [(2, 70, [0, 30], 128), (3, 1, [0, 5, 900], 1024),
-                                                (2, 1, [4095, 3000], 4096), (1, 33, [100], 256)])
-def test_attention(ops, dtype, tol, b, t, starts, max_len):
+@pytest.mark.parametrize("b,t,starts,max_len,nh,nkv", [(2, 70, [0, 30], 128, 8, 2), (3, 1, [0, 5, 900], 1024, 8, 2),
+                                                        (2, 1, [4095, 3000], 4096, 8, 2), (1, 33, [100], 256, 8, 2),
+                                                        (1, 300, [0], 512, 8, 2), (2, 129, [7, 0], 200, 4, 2),
+                                                        (1, 65, [3], 128, 2, 2)])
+def test_attention(ops, dtype, tol, b, t, starts, max_len, nh, nkv):
     g = _seed(b * 1000 + t)
-    nh, nkv, hd = 8, 2, 256
+    hd = 256
     q = torch.randn(b, t, nh, hd, generator=g).to(dtype)
     kc = torch.randn(b, max_len, nkv, hd, generator=g).to(dtype)
     vc = torch.randn(b, max_len, nkv, hd, generator=g).to(dtype)
