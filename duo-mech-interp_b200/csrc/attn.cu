@@ -294,6 +294,13 @@ static void decode_plan(const AttnArgs& a, int* nsplit, int* split_len) {
   *split_len = cdiv(a.max_len, ns);
 }
 
+long attn_decode_scratch_floats(int b, int nh, int nkv, int max_len) {
+  const long blocks = (long)std::max(1, b) * nkv;
+  int ns = (int)std::max<long>(1, (2L * sm_count() + blocks - 1) / blocks);
+  ns = std::min(ns, std::max(1, cdiv(max_len, 256)));
+  return ns > 1 ? (long)b * nh * ns * (AP_HD + 2) : 0;
+}
+
 long attn_work_floats(int b, int nh, int max_len) {
   const int ns_max = std::max(1, cdiv(max_len, 256));
   return (long)b * nh * std::min<long>(ns_max, 2L * sm_count()) * (AP_HD + 2);

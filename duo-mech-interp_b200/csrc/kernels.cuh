@@ -120,6 +120,8 @@ struct AttnArgs {
 };
 int launch_attention(const AttnArgs& a, int dtype, cudaStream_t st);
 long attn_work_floats(int b, int nh, int max_len);
+// split-K scratch (floats) the decode planner fills when the workspace does not limit it; 0 = no split
+long attn_decode_scratch_floats(int b, int nh, int nkv, int max_len);
 int launch_attn_prefill_mma(const AttnArgs& a, cudaStream_t st);  // bf16, t > 1, hd 256
 
 // int8 -> bf16 copy of a weight matrix for the tensor-core GEMM: dst row of src row n is n, or (interleave > 0) the

@@ -50,6 +50,7 @@ SIGNATURES = {
     "duo_gdn_recurrent_fwd": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "duo_gdn_chunk_fwd": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "duo_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
+    "duo_attention_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
     "duo_fault_status": (_i, [C.POINTER(_u)]),
     "duo_engine_create": (_i, [C.POINTER(duo_config), C.POINTER(_vp)]),
     "duo_engine_destroy": (None, [_vp]),

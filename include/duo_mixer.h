@@ -113,6 +113,18 @@ int duo_attention(const void* q, const void* kc, const void* vc, const int32_t* 
                   int gate_stride, void* o, int dtype, int b, int t, int nh, int nkv, int hd, int max_len, float scale,
                   duo_stream stream);
 
+/* duo_attention for callers that cannot allocate device memory (a serving stack whose pooled allocator owns all of
+ * it, or a decode loop where cudaMalloc and the synchronisation it implies are not allowed).  No counterpart in the
+ * reference.  Same arguments, kernels and split plan as duo_attention, but the split-K decode scratch is a fixed
+ * file-scope device array of 262,144 floats (1 MiB, held on every GPU that loads the library) instead of a
+ * library-allocated workspace: nothing is allocated.  A decode call (t == 1) needing more than that
+ * (b * nh * splits * (hd + 2) floats) fails with DUO_EINVAL before any launch.  The first call on a device looks up
+ * the array's address and should come before any stream capture.  Calls share the array: calls that overlap on the
+ * GPU race (order them on one stream); nothing in it needs clearing between calls. */
+int duo_attention_noalloc(const void* q, const void* kc, const void* vc, const int32_t* start, const void* gate,
+                          int gate_stride, void* o, int dtype, int b, int t, int nh, int nkv, int hd, int max_len,
+                          float scale, duo_stream stream);
+
 /* ============================================================================================================
  * Engine: mirrors engine/model.js `Model` (alloc, reset, setVectors, setHeadScales, _forward, _logits, argmaxAll)
  * ============================================================================================================ */
