@@ -55,10 +55,11 @@ int launch_attn_prep(const AttnPrepArgs& a, int dtype, cudaStream_t st) {
   if (a.hd % 32 || a.hd > 1024 || a.rot > a.hd || a.rot % 2) return fail(DUO_EINVAL, "attn_prep: bad head dims");
   dim3 grid(m, a.nh + a.nkv);
   const size_t sm = a.hd * sizeof(float);
-  if (dtype == DUO_F32) attn_prep_kernel<float><<<grid, a.hd, sm, st>>>(a);
-  else attn_prep_kernel<__nv_bfloat16><<<grid, a.hd, sm, st>>>(a);
-  DUO_LAUNCH_CHECK("attn_prep_kernel");
-  return DUO_OK;
+  return with_act(dtype, [&](auto tag) -> int {
+    attn_prep_kernel<decltype(tag)><<<grid, a.hd, sm, st>>>(a);
+    DUO_LAUNCH_CHECK("attn_prep_kernel");
+    return DUO_OK;
+  });
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -308,9 +309,10 @@ long attn_work_floats(int b, int nh, int max_len) {
 
 template <typename T>
 static int run_attention(const AttnArgs& a, cudaStream_t st) {
-  if (std::is_same<T, __nv_bfloat16>::value && a.t > 1) {
+  if (!std::is_same<T, float>::value && a.t > 1) {
     const int rep = a.nh / a.nkv;
-    if (rep == 1 || rep == 2 || rep == 4) return launch_attn_prefill_mma(a, st);  // tensor cores
+    if (rep == 1 || rep == 2 || rep == 4)  // tensor cores
+      return launch_attn_prefill_mma(a, std::is_same<T, __half>::value ? DUO_F16 : DUO_BF16, st);
   }
   if (a.t == 1) {
     int ns, sl;
@@ -338,7 +340,7 @@ int launch_attention(const AttnArgs& a, int dtype, cudaStream_t st) {
   if (a.b == 0 || a.t == 0) return DUO_OK;
   if (a.hd != AP_HD) return fail(DUO_EINVAL, "attention: head dim must be 256");
   if (a.nkv <= 0 || a.nh % a.nkv || a.nh / a.nkv > AD_REP) return fail(DUO_EINVAL, "attention: nh / nkv must be 1..4");
-  return dtype == DUO_F32 ? run_attention<float>(a, st) : run_attention<__nv_bfloat16>(a, st);
+  return with_act(dtype, [&](auto tag) -> int { return run_attention<decltype(tag)>(a, st); });
 }
 
 // library-owned split-K workspace for the op-level entry point (grown on demand)
@@ -354,7 +356,7 @@ extern "C" int duo_attention(const void* q, const void* kc, const void* vc, cons
                              int gate_stride, void* o, int dtype, int b, int t, int nh, int nkv, int hd, int max_len,
                              float scale, duo_stream stream) {
   DUO_CHECK_ARG(b >= 0 && t >= 0 && nh > 0 && nkv > 0 && max_len > 0, "attention: bad shape");
-  DUO_CHECK_ARG(valid_act(dtype), "attention: dtype must be f32 or bf16");
+  DUO_CHECK_ARG(valid_act(dtype), "attention: dtype must be f32, bf16 or f16");
   DUO_CHECK_ARG(b == 0 || t == 0 || (q && kc && vc && start && o), "attention: null pointer");
   AttnArgs a{};
   a.q = q; a.kc = kc; a.vc = vc; a.cache_row0 = 0; a.start = start; a.len = nullptr;

@@ -2,7 +2,7 @@
 //
 // One CTA = (row, kv head, tile of 128 / rep queries); its 128 query rows are the rep q heads of that kv head over the
 // same query positions, so every K / V tile is loaded once for all of them.  8 warps x 16 rows; head dim 256.
-// Per 64-key tile: S = Q K^T (bf16 mma, f32 accumulate), causal mask, online softmax in f32 (base 2), O += P V with
+// Per 64-key tile: S = Q K^T (bf16 or f16 mma, f32 accumulate), causal mask, online softmax in f32 (base 2), O += P V with
 // P taken straight from the S accumulators.  K / V tiles are double-buffered with cp.async.  The output is divided by
 // the softmax sum and multiplied by sigmoid(gate) on the way out (transformers Qwen3_5Attention: attention, then
 // `attn_output * sigmoid(gate)`; the reference's WGSL does the same per (token, head), kernels_qwen35.js:73-123).
@@ -25,13 +25,13 @@ template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.as
 
 }  // namespace
 
-template <int REP>
+template <int REP, typename T16>
 __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
   constexpr int QT = 128 / REP;  // query positions per CTA
   extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* Ks = Qs + 128 * PQ;
-  __nv_bfloat16* Vs = Ks + 2 * BKEY * PQ;
+  T16* Qs = reinterpret_cast<T16*>(smem);
+  T16* Ks = Qs + 128 * PQ;
+  T16* Vs = Ks + 2 * BKEY * PQ;
   const int qt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q4 = lane & 3;
@@ -41,16 +41,16 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
   const int nq = min(QT, a.t - tq0);
   const int n_keys = p0 + tq0 + nq;
   const int ntiles = (n_keys + BKEY - 1) / BKEY;
-  const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(a.q);
-  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(a.kc);
-  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(a.vc);
+  const T16* q = static_cast<const T16*>(a.q);
+  const T16* kc = static_cast<const T16*>(a.kc);
+  const T16* vc = static_cast<const T16*>(a.vc);
 
   // Q tile: row r = head (kvh * REP + r / QT) at query position tq0 + r % QT; 32 chunks of 16 bytes per row
   for (int e = tid; e < 128 * 32; e += 256) {
     const int r = e >> 5, c = (e & 31) * 8;
     const int qi = r % QT, hq = kvh * REP + r / QT;
     const bool ok = qi < nq;
-    const __nv_bfloat16* src = ok ? q + (((long)b * a.t + tq0 + qi) * a.nh + hq) * HD + c : q;
+    const T16* src = ok ? q + (((long)b * a.t + tq0 + qi) * a.nh + hq) * HD + c : q;
     cp_async16(Qs + r * PQ + c, src, ok);
   }
   auto load_kv = [&](int kt, int buf) {
@@ -83,8 +83,8 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
     cp_commit();
     cp_wait<1>();
     __syncthreads();
-    const __nv_bfloat16* Kb = Ks + buf * BKEY * PQ;
-    const __nv_bfloat16* Vb = Vs + buf * BKEY * PQ;
+    const T16* Kb = Ks + buf * BKEY * PQ;
+    const T16* Vb = Vs + buf * BKEY * PQ;
     // S = Q K^T: 16 x 64 per warp
     float S[8][4];
 #pragma unroll
@@ -99,8 +99,8 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
       for (int jj = 0; jj < 4; jj++) {
         uint32_t bk[4];
         wm::ldb_nk(bk, Kb, PQ, 16 * jj, k0);
-        wm::mma(S[2 * jj], aq, bk);
-        wm::mma(S[2 * jj + 1], aq, bk + 2);
+        wm::Ops<T16>::mma(S[2 * jj], aq, bk);
+        wm::Ops<T16>::mma(S[2 * jj + 1], aq, bk + 2);
       }
     }
     // causal mask + online softmax (rows g and g + 8 of the warp; a row's 64 scores sit on 4 lanes)
@@ -132,8 +132,8 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
       const float e3 = S[j][3] == -INFINITY ? 0.f : exp2f(S[j][3] - mn1);
       ps0 += e0 + e1;
       ps1 += e2 + e3;
-      pf[j >> 1][(j & 1) * 2] = wm::pack_bf16(e0, e1);
-      pf[j >> 1][(j & 1) * 2 + 1] = wm::pack_bf16(e2, e3);
+      pf[j >> 1][(j & 1) * 2] = wm::Ops<T16>::pack(e0, e1);
+      pf[j >> 1][(j & 1) * 2 + 1] = wm::Ops<T16>::pack(e2, e3);
     }
     ps0 += __shfl_xor_sync(0xffffffffu, ps0, 1);
     ps0 += __shfl_xor_sync(0xffffffffu, ps0, 2);
@@ -155,8 +155,8 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
       for (int nn = 0; nn < 16; nn++) {
         uint32_t bv[4];
         wm::ldb_kn(bv, Vb, PQ, 16 * nn, 16 * kk);
-        wm::mma(O[2 * nn], pf[kk], bv);
-        wm::mma(O[2 * nn + 1], pf[kk], bv + 2);
+        wm::Ops<T16>::mma(O[2 * nn], pf[kk], bv);
+        wm::Ops<T16>::mma(O[2 * nn + 1], pf[kk], bv + 2);
       }
     }
     __syncthreads();  // this buffer is refilled by the next iteration's prefetch
@@ -164,8 +164,8 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
   cp_wait<0>();
 
   // epilogue: normalise, gate, store
-  __nv_bfloat16* op = static_cast<__nv_bfloat16*>(a.o);
-  const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(a.gate);
+  T16* op = static_cast<T16*>(a.o);
+  const T16* gp = static_cast<const T16*>(a.gate);
   const int hq = kvh * REP + wr / QT;
 #pragma unroll
   for (int half = 0; half < 2; half++) {
@@ -173,42 +173,42 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
     if (qi >= nq) continue;
     const float inv = 1.f / (half ? l1 : l0);
     const long tok = (long)b * a.t + tq0 + qi;
-    __nv_bfloat16* orow = op + (tok * a.nh + hq) * HD;
-    const __nv_bfloat16* grow = gp ? gp + tok * a.gate_stride + (long)hq * a.gate_hstride : nullptr;
+    T16* orow = op + (tok * a.nh + hq) * HD;
+    const T16* grow = gp ? gp + tok * a.gate_stride + (long)hq * a.gate_hstride : nullptr;
 #pragma unroll
     for (int j = 0; j < 32; j++) {
       const int d = 8 * j + 2 * q4;
       float v0 = O[j][half * 2] * inv, v1 = O[j][half * 2 + 1] * inv;
       if (grow) {
-        v0 *= sigmoidf_(__bfloat162float(grow[d]));
-        v1 *= sigmoidf_(__bfloat162float(grow[d + 1]));
+        v0 *= sigmoidf_(to_f(grow[d]));
+        v1 *= sigmoidf_(to_f(grow[d + 1]));
       }
-      *reinterpret_cast<uint32_t*>(orow + d) = wm::pack_bf16(v0, v1);
+      *reinterpret_cast<uint32_t*>(orow + d) = wm::Ops<T16>::pack(v0, v1);
     }
   }
 }
 
-template <int REP>
+template <int REP, typename T16>
 static int run_prefill_mma(const AttnArgs& a, cudaStream_t st) {
   constexpr int smem = (128 + 4 * BKEY) * PQ * 2;
   static bool attr = false;
   if (!attr) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_mma_kernel<REP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    DUO_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_mma_kernel<REP, T16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  attn_prefill_mma_kernel<REP><<<dim3(cdiv(a.t, 128 / REP), a.nkv, a.b), 256, smem, st>>>(a);
+  attn_prefill_mma_kernel<REP, T16><<<dim3(cdiv(a.t, 128 / REP), a.nkv, a.b), 256, smem, st>>>(a);
   DUO_LAUNCH_CHECK("attn_prefill_mma_kernel");
   return DUO_OK;
 }
 
-int launch_attn_prefill_mma(const AttnArgs& a, cudaStream_t st) {
+int launch_attn_prefill_mma(const AttnArgs& a, int dtype, cudaStream_t st) {
   if (a.hd != HD) return fail(DUO_EINVAL, "attention prefill: head dim must be 256");
-  switch (a.nh / a.nkv) {
-    case 1: return run_prefill_mma<1>(a, st);
-    case 2: return run_prefill_mma<2>(a, st);
-    case 4: return run_prefill_mma<4>(a, st);
-    default: return fail(DUO_EINVAL, "attention prefill: nh / nkv must be 1, 2 or 4");
-  }
+  const int rep = a.nh / a.nkv;
+  if (rep != 1 && rep != 2 && rep != 4) return fail(DUO_EINVAL, "attention prefill: nh / nkv must be 1, 2 or 4");
+  if (dtype == DUO_F16) return rep == 1 ? run_prefill_mma<1, __half>(a, st) : rep == 2 ? run_prefill_mma<2, __half>(a, st)
+                                                                                    : run_prefill_mma<4, __half>(a, st);
+  return rep == 1 ? run_prefill_mma<1, __nv_bfloat16>(a, st) : rep == 2 ? run_prefill_mma<2, __nv_bfloat16>(a, st)
+                                                                       : run_prefill_mma<4, __nv_bfloat16>(a, st);
 }
 
 }  // namespace duo

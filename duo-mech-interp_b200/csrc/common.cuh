@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 #include <string>
 
@@ -49,9 +50,21 @@ void count_launch();
 
 inline cudaStream_t as_stream(duo_stream s) { return reinterpret_cast<cudaStream_t>(s); }
 
-inline bool valid_act(int dt) { return dt == DUO_F32 || dt == DUO_BF16; }
+inline bool valid_act(int dt) { return dt == DUO_F32 || dt == DUO_BF16 || dt == DUO_F16; }
+inline size_t act_bytes(int dt) { return dt == DUO_F32 ? 4 : 2; }
 
 inline int cdiv(long a, long b) { return (int)((a + b - 1) / b); }
+
+// Run f(tag) with tag a value of the C++ type of activation dtype `dt` (float, __nv_bfloat16 or __half):
+//   with_act(dt, [&](auto tag) { using T = decltype(tag); ... });
+template <typename F> int with_act(int dt, F&& f) {
+  switch (dt) {
+    case DUO_F32: return f(float{});
+    case DUO_BF16: return f(__nv_bfloat16{});
+    case DUO_F16: return f(__half{});
+    default: return fail(DUO_EINVAL, "unsupported activation dtype " + std::to_string(dt));
+  }
+}
 
 // number of SMs of the current device (cached per process; one device per process in this library's model)
 int sm_count();
@@ -61,10 +74,12 @@ int sm_count();
 
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 
 template <typename T> __device__ __forceinline__ T from_f(float v);
 template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
 // load 8 consecutive values of T as floats (16-byte aligned for bf16, 32 for f32)
 __device__ __forceinline__ void load8(const float* p, float* o) {
@@ -79,6 +94,22 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* o) {
     float2 f = __bfloat1622float2(h[i]);
     o[2 * i] = f.x; o[2 * i + 1] = f.y;
   }
+}
+__device__ __forceinline__ void load8(const __half* p, float* o) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float2 f = __half22float2(h[i]);
+    o[2 * i] = f.x; o[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(__half* p, const float* v) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
 }
 __device__ __forceinline__ void store8(float* p, const float* v) {
   *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);

@@ -38,12 +38,12 @@ int launch_rmsnorm(const float* x, int m, int d, const float* w, float eps, int 
                    cudaStream_t st) {
   if (m == 0) return DUO_OK;
   const int threads = std::min(256, std::max(32, ((d / 8 + 31) / 32) * 32));
-  if (y_dtype == DUO_F32)
-    rmsnorm_kernel<float><<<m, threads, 0, st>>>(x, d, w, eps, offset, static_cast<float*>(y));
-  else
-    rmsnorm_kernel<__nv_bfloat16><<<m, threads, 0, st>>>(x, d, w, eps, offset, static_cast<__nv_bfloat16*>(y));
-  DUO_LAUNCH_CHECK("rmsnorm_kernel");
-  return DUO_OK;
+  return with_act(y_dtype, [&](auto yt) -> int {
+    using TY = decltype(yt);
+    rmsnorm_kernel<TY><<<m, threads, 0, st>>>(x, d, w, eps, offset, static_cast<TY*>(y));
+    DUO_LAUNCH_CHECK("rmsnorm_kernel");
+    return DUO_OK;
+  });
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -79,14 +79,12 @@ int launch_swiglu_push(const void* gu, int m, int inter, int t, int row_base, co
                        int dtype, cudaStream_t st) {
   if (m == 0) return DUO_OK;
   dim3 grid(cdiv(inter / 8, 256), m);
-  if (dtype == DUO_F32)
-    swiglu_push_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(gu), inter, t, row_base, pt,
-                                                    static_cast<float*>(a));
-  else
-    swiglu_push_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(gu), inter, t,
-                                                            row_base, pt, static_cast<__nv_bfloat16*>(a));
-  DUO_LAUNCH_CHECK("swiglu_push_kernel");
-  return DUO_OK;
+  return with_act(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    swiglu_push_kernel<T><<<grid, 256, 0, st>>>(static_cast<const T*>(gu), inter, t, row_base, pt, static_cast<T*>(a));
+    DUO_LAUNCH_CHECK("swiglu_push_kernel");
+    return DUO_OK;
+  });
 }
 
 // ---------------------------------------------------------------------------------------------------------------

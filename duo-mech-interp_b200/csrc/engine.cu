@@ -19,7 +19,7 @@ constexpr int kMaxPush = 16;  // push records per layer (the reference allows 8,
 constexpr int kGemvMax = 8;   // rows up to which projections stream int8 weights through the GEMV
 
 struct Pack {
-  __nv_bfloat16* w = nullptr;
+  void* w = nullptr;  // 16-bit (the engine's activation dtype) copy of the int8 matrix
   float* colscale = nullptr;  // per output column when the int8 scale is per row, else null
 };
 
@@ -162,20 +162,20 @@ int project(duo_engine* e, const void* xin, int m, int k, const duo_q8_view& wq,
   if (e->act == DUO_F32) return launch_gemm_f32_q8(static_cast<const float*>(xin), m, k, wq.q, wq.s, grp, n, ep, st);
   GemmEpiArgs ep2 = ep;
   ep2.colscale = pk.colscale;
-  return launch_gemm_tc(xin, m, k, pk.w, n, ep2, st);
+  return launch_gemm_tc(xin, m, k, pk.w, n, e->act, ep2, st);
 }
 
 int build_pack(duo_engine* e, const duo_q8_view& v, int n, int k, int interleave, Pack* out, cudaStream_t st) {
   void* w = nullptr;
   DUO_TRY(e->dalloc(&w, (size_t)n * k * 2, false));
-  out->w = static_cast<__nv_bfloat16*>(w);
+  out->w = w;
   const bool per_row = e->group == 0;
   if (per_row) {
     void* cs = nullptr;
     DUO_TRY(e->dalloc(&cs, (size_t)n * 4, false));
     out->colscale = static_cast<float*>(cs);
   }
-  return launch_pack_bf16(v.q, v.s, n, k, e->gsize(k), interleave, per_row ? 0 : 1, out->w, out->colscale, st);
+  return launch_pack16(v.q, v.s, n, k, e->gsize(k), interleave, per_row ? 0 : 1, e->act, out->w, out->colscale, st);
 }
 
 int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, int T, int vec_layer,
@@ -222,7 +222,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       sa.z_stride = wproj;
       sa.norm_w = L.gnorm; sa.head_scale = S.head_scale; sa.eps = c.eps;
       // prefill of the bf16 engine: chunked tensor-core scan; decode and the f32 engine: the recurrent form
-      if (act == DUO_BF16 && T > 16) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
+      if (act != DUO_F32 && T > 16) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
       else PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_recurrent(sa, act, st));
       out_k = e->vd;
     } else {
@@ -256,17 +256,17 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
     }
     PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->x, M, H, L.post_norm, c.eps, 1, e->xn, act, st));
     PushTable pt{S.push_neuron, S.push_mode, S.push_vals, S.push_count, e->rows};
-    if (M > kGemvMax && act == DUO_BF16) {
+    if (M > kGemvMax && act != DUO_F32) {
       GemmEpiArgs ep;
       ep.epi = EPI_SWIGLU;
       ep.c = e->a;
-      ep.c_dtype = DUO_BF16;
+      ep.c_dtype = act;
       ep.ldc = c.inter;
       ep.colscale = e->p_gu[l].colscale;
       ep.t = T;
       ep.row_base = row_base;
       ep.push = pt;
-      PROF_TRY(DUO_PROF_GEMM, launch_gemm_tc(e->xn, M, H, e->p_gu[l].w, 2 * c.inter, ep, st));
+      PROF_TRY(DUO_PROF_GEMM, launch_gemm_tc(e->xn, M, H, e->p_gu[l].w, 2 * c.inter, act, ep, st));
     } else {
       GemmEpiArgs ep;
       ep.epi = EPI_STORE;
@@ -335,7 +335,7 @@ extern "C" int duo_engine_create(const duo_config* cfg, duo_engine** out) {
   DUO_CHECK_ARG(c.hk > 0 && c.hv % c.hk == 0, "engine_create: hv must be a multiple of hk");
   DUO_CHECK_ARG(c.group == 0 || (c.group % 16 == 0 && c.hidden % c.group == 0 && c.inter % c.group == 0),
                 "engine_create: group must be 0 or a multiple of 16 dividing hidden and inter");
-  DUO_CHECK_ARG(valid_act(c.act_dtype), "engine_create: act_dtype must be DUO_F32 or DUO_BF16");
+  DUO_CHECK_ARG(valid_act(c.act_dtype), "engine_create: act_dtype must be DUO_F32, DUO_BF16 or DUO_F16");
   DUO_CHECK_ARG(c.full_attention_host, "engine_create: null layer type array");
   duo_engine* e = new duo_engine();
   e->cfg = c;
@@ -349,7 +349,7 @@ extern "C" int duo_engine_create(const duo_config* cfg, duo_engine** out) {
   e->wmax = std::max(std::max(e->w_lin, e->w_full), 2 * c.inter);
   e->group = c.group;
   e->act = c.act_dtype;
-  e->act_size = c.act_dtype == DUO_F32 ? 4 : 2;
+  e->act_size = act_bytes(c.act_dtype);
   // inv_freq[j] = 1 / theta^(2j / rot) in f32, the way transformers computes the default RoPE table
   std::vector<float> inv(c.rot / 2);
   for (int j = 0; j < c.rot / 2; j++) {
@@ -388,7 +388,7 @@ extern "C" int duo_engine_load(duo_engine* e, const duo_weights_view* wv, duo_st
   e->p_out.assign(c.layers, Pack{});
   e->p_gu.assign(c.layers, Pack{});
   e->p_down.assign(c.layers, Pack{});
-  if (e->act == DUO_BF16) {
+  if (e->act != DUO_F32) {
     for (int l = 0; l < c.layers; l++) {
       const duo_layer_view& L = e->lw[l];
       const bool full = e->is_full(l);

@@ -96,10 +96,11 @@ int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
   if (a.dk != 128 || a.dv != 128 || a.ks != CONV_KS) return fail(DUO_EINVAL, "gdn_conv: needs dk = dv = 128, ks = 4");
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
   dim3 grid(conv_dim / 128, a.rows, cdiv(a.t, CONV_TT));
-  if (dtype == DUO_F32) gdn_conv_kernel<float><<<grid, 128, 0, st>>>(a);
-  else gdn_conv_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a);
-  DUO_LAUNCH_CHECK("gdn_conv_kernel");
-  return DUO_OK;
+  return with_act(dtype, [&](auto tag) -> int {
+    gdn_conv_kernel<decltype(tag)><<<grid, 128, 0, st>>>(a);
+    DUO_LAUNCH_CHECK("gdn_conv_kernel");
+    return DUO_OK;
+  });
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -213,15 +214,17 @@ int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st) {
   if (a.dk != 128 || a.dv != 128) return fail(DUO_EINVAL, "gdn: needs dk = dv = 128");
   if (a.hq <= 0 || a.h % a.hq) return fail(DUO_EINVAL, "gdn: value heads must be a multiple of q/k heads");
   const bool norm = a.norm_w != nullptr;
-  if (dtype == DUO_F32) return norm ? run_recurrent<float, true>(a, st) : run_recurrent<float, false>(a, st);
-  return norm ? run_recurrent<__nv_bfloat16, true>(a, st) : run_recurrent<__nv_bfloat16, false>(a, st);
+  return with_act(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    return norm ? run_recurrent<T, true>(a, st) : run_recurrent<T, false>(a, st);
+  });
 }
 
 static int check_gdn_op(const void* q, const void* k, const void* v, int in_dtype, const float* g, const float* beta,
                         float* state, void* o, int o_dtype, int b, int t, int h, int dk, int dv) {
   DUO_CHECK_ARG(b >= 0 && t >= 0 && h > 0, "gdn: bad shape");
   DUO_CHECK_ARG(dk == 128 && dv == 128, "gdn: dk and dv must be 128");
-  DUO_CHECK_ARG(valid_act(in_dtype) && o_dtype == in_dtype, "gdn: q/k/v/o dtype must be f32 or bf16 (the same)");
+  DUO_CHECK_ARG(valid_act(in_dtype) && o_dtype == in_dtype, "gdn: q/k/v/o dtype must be f32, bf16 or f16 (the same)");
   DUO_CHECK_ARG(b == 0 || t == 0 || (q && k && v && g && beta && state && o), "gdn: null pointer");
   return DUO_OK;
 }

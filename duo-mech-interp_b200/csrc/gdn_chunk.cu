@@ -8,8 +8,9 @@
 //   V' = U - W S,   O = diag(e^G) Q S + tril(Q K^T * exp(G_i - G_j)) V'
 //   S <- e^{G_63} S + (diag(e^{G_63 - G}) K)^T V'
 // One CTA (8 warps) owns one (row, value head) and walks its chunks in order.  The 64 x 64 and 64 x 128 products and
-// the 128 x 128 state update run on the tensor cores (bf16 operands, f32 accumulation); the state lives in registers
-// as f32 accumulators for the whole sequence and is rounded to bf16 only as an operand copy.  T is formed in f32 by
+// the 128 x 128 state update run on the tensor cores (f16 operands, f32 accumulation; f16 keeps 8x more mantissa than
+// bf16 for these normalised, decay-bounded intermediates); the state lives in registers as f32 accumulators for the
+// whole sequence and is rounded to f16 only as an operand copy.  T is formed in f32 by
 // blocked forward substitution (16 x 16 diagonal blocks, then the off-diagonal blocks by distance).  The gated
 // RMSNorm of the engine path is fused into the output.
 #include "kernels.cuh"
@@ -25,13 +26,13 @@ constexpr int PC = 64 + 8;     // pitch of the 64-wide bf16 tiles
 constexpr int PF = 64 + 1;     // pitch of the f32 64 x 64 tiles
 
 struct ChunkSmem {
-  __nv_bfloat16 q[CK * PD], k[CK * PD], v[CK * PD];  // chunk inputs (q scaled by 1/sqrt(dk))
-  __nv_bfloat16 w[CK * PD];                          // W
-  __nv_bfloat16 vn[CK * PD];                         // V'
-  __nv_bfloat16 vd[CK * PD];                         // diag(e^{G_63 - G}) V'
-  __nv_bfloat16 s[128 * PD];                         // bf16 copy of the state [dk][dv]
-  __nv_bfloat16 aq[CK * PC];                         // tril(Q K^T) * decay
-  __nv_bfloat16 t1[CK * PC], t2[CK * PC];            // T diag(beta), T diag(beta e^G)
+  __half q[CK * PD], k[CK * PD], v[CK * PD];  // chunk inputs (q scaled by 1/sqrt(dk))
+  __half w[CK * PD];                          // W
+  __half vn[CK * PD];                         // V'
+  __half vd[CK * PD];                         // diag(e^{G_63 - G}) V'
+  __half s[128 * PD];                         // f16 copy of the state [dk][dv]
+  __half aq[CK * PC];                         // tril(Q K^T) * decay
+  __half t1[CK * PC], t2[CK * PC];            // T diag(beta), T diag(beta e^G)
   float a[CK * PF];                                  // L (strictly lower), f32
   float t[CK * PF];                                  // T = (I + L)^-1, f32
   float x[3 * 16 * 17];                              // off-diagonal solve scratch
@@ -50,11 +51,17 @@ template <> __device__ __forceinline__ void ld4f<__nv_bfloat16>(const __nv_bfloa
   const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
   o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
 }
+template <> __device__ __forceinline__ void ld4f<__half>(const __half* p, float* o) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+}
 
-__device__ __forceinline__ void st4bf(__nv_bfloat16* p, const float* v) {
+__device__ __forceinline__ void st4h(__half* p, const float* v) {
   uint2 u;
-  u.x = wm::pack_bf16(v[0], v[1]);
-  u.y = wm::pack_bf16(v[2], v[3]);
+  u.x = wm::pack_f16(v[0], v[1]);
+  u.y = wm::pack_f16(v[2], v[3]);
   *reinterpret_cast<uint2*>(p) = u;
 }
 
@@ -84,8 +91,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
       const float2 lo = *reinterpret_cast<const float2*>(Sg + (long)r0 * 128 + c);
       const float2 hi = *reinterpret_cast<const float2*>(Sg + (long)(r0 + 8) * 128 + c);
       S[j][0] = lo.x; S[j][1] = lo.y; S[j][2] = hi.x; S[j][3] = hi.y;
-      *reinterpret_cast<uint32_t*>(sm.s + r0 * PD + c) = wm::pack_bf16(lo.x, lo.y);
-      *reinterpret_cast<uint32_t*>(sm.s + (r0 + 8) * PD + c) = wm::pack_bf16(hi.x, hi.y);
+      *reinterpret_cast<uint32_t*>(sm.s + r0 * PD + c) = wm::pack_f16(lo.x, lo.y);
+      *reinterpret_cast<uint32_t*>(sm.s + (r0 + 8) * PD + c) = wm::pack_f16(hi.x, hi.y);
     }
   }
 
@@ -112,9 +119,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; i++) qv[i] *= qscale;
       }
-      st4bf(sm.q + r * PD + lane * 4, qv);
-      st4bf(sm.k + r * PD + lane * 4, kv);
-      st4bf(sm.v + r * PD + lane * 4, vv);
+      st4h(sm.q + r * PD + lane * 4, qv);
+      st4h(sm.k + r * PD + lane * 4, kv);
+      st4h(sm.v + r * PD + lane * 4, vv);
     }
     if (tid < CK) {
       const int t = t0 + tid;
@@ -159,10 +166,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
         wm::ldb_nk(bf[1], sm.k, PD, wc + 16, k0);
 #pragma unroll
         for (int jj = 0; jj < 2; jj++) {
-          wm::mma(qk[2 * jj], aq, bf[jj]);
-          wm::mma(qk[2 * jj + 1], aq, bf[jj] + 2);
-          wm::mma(kk[2 * jj], ak, bf[jj]);
-          wm::mma(kk[2 * jj + 1], ak, bf[jj] + 2);
+          wm::mma_f16(qk[2 * jj], aq, bf[jj]);
+          wm::mma_f16(qk[2 * jj + 1], aq, bf[jj] + 2);
+          wm::mma_f16(kk[2 * jj], ak, bf[jj]);
+          wm::mma_f16(kk[2 * jj + 1], ak, bf[jj] + 2);
         }
       }
     }
@@ -176,7 +183,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
           const int i = wr + g + (e >> 1) * 8, jc = wc + 8 * j + 2 * q4 + (e & 1);
           const float dec = jc <= i ? expf(sm.gcum[i] - sm.gcum[jc]) : 0.f;
           sm.a[i * PF + jc] = jc < i ? sm.beta[i] * kk[j][e] * dec : 0.f;
-          sm.aq[i * PC + jc] = __float2bfloat16_rn(qk[j][e] * dec);
+          sm.aq[i * PC + jc] = __float2half_rn(qk[j][e] * dec);
           sm.t[i * PF + jc] = 0.f;
         }
     }
@@ -217,8 +224,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
     for (int e = tid; e < CK * CK; e += 256) {
       const int i = e >> 6, j = e & 63;
       const float tv = sm.t[i * PF + j];
-      sm.t1[i * PC + j] = __float2bfloat16_rn(tv * sm.beta[j]);
-      sm.t2[i * PC + j] = __float2bfloat16_rn(tv * sm.beta[j] * sm.eg[j]);
+      sm.t1[i * PC + j] = __float2half_rn(tv * sm.beta[j]);
+      sm.t2[i * PC + j] = __float2half_rn(tv * sm.beta[j] * sm.eg[j]);
     }
     __syncthreads();
     // ---- U = T1 V and W = T2 K (64 x 128, K = 64): warp tile 16 rows x 64 columns
@@ -238,17 +245,17 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
         uint32_t bv[4], bk[4];
         wm::ldb_kn(bv, sm.v, PD, wc + 16 * jj, k0);
         wm::ldb_kn(bk, sm.k, PD, wc + 16 * jj, k0);
-        wm::mma(U[2 * jj], a1, bv);
-        wm::mma(U[2 * jj + 1], a1, bv + 2);
-        wm::mma(Wt[2 * jj], a2, bk);
-        wm::mma(Wt[2 * jj + 1], a2, bk + 2);
+        wm::mma_f16(U[2 * jj], a1, bv);
+        wm::mma_f16(U[2 * jj + 1], a1, bv + 2);
+        wm::mma_f16(Wt[2 * jj], a2, bk);
+        wm::mma_f16(Wt[2 * jj + 1], a2, bk + 2);
       }
     }
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       const int cc = wc + 8 * j + 2 * q4;
-      *reinterpret_cast<uint32_t*>(sm.w + (wr + g) * PD + cc) = wm::pack_bf16(Wt[j][0], Wt[j][1]);
-      *reinterpret_cast<uint32_t*>(sm.w + (wr + g + 8) * PD + cc) = wm::pack_bf16(Wt[j][2], Wt[j][3]);
+      *reinterpret_cast<uint32_t*>(sm.w + (wr + g) * PD + cc) = wm::pack_f16(Wt[j][0], Wt[j][1]);
+      *reinterpret_cast<uint32_t*>(sm.w + (wr + g + 8) * PD + cc) = wm::pack_f16(Wt[j][2], Wt[j][3]);
     }
     __syncthreads();
     // ---- W S and Q S (64 x 128, K = 128); V' = U - W S; O = diag(e^G) Q S
@@ -266,10 +273,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
       for (int jj = 0; jj < 4; jj++) {
         uint32_t bs[4];
         wm::ldb_kn(bs, sm.s, PD, wc + 16 * jj, k0);
-        wm::mma(Wt[2 * jj], aw, bs);
-        wm::mma(Wt[2 * jj + 1], aw, bs + 2);
-        wm::mma(O[2 * jj], aq2, bs);
-        wm::mma(O[2 * jj + 1], aq2, bs + 2);
+        wm::mma_f16(Wt[2 * jj], aw, bs);
+        wm::mma_f16(Wt[2 * jj + 1], aw, bs + 2);
+        wm::mma_f16(O[2 * jj], aq2, bs);
+        wm::mma_f16(O[2 * jj + 1], aq2, bs + 2);
       }
     }
     {
@@ -280,10 +287,10 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
         const int cc = wc + 8 * j + 2 * q4;
         const float v0 = U[j][0] - Wt[j][0], v1 = U[j][1] - Wt[j][1];
         const float v2 = U[j][2] - Wt[j][2], v3 = U[j][3] - Wt[j][3];
-        *reinterpret_cast<uint32_t*>(sm.vn + (wr + g) * PD + cc) = wm::pack_bf16(v0, v1);
-        *reinterpret_cast<uint32_t*>(sm.vn + (wr + g + 8) * PD + cc) = wm::pack_bf16(v2, v3);
-        *reinterpret_cast<uint32_t*>(sm.vd + (wr + g) * PD + cc) = wm::pack_bf16(v0 * l0, v1 * l0);
-        *reinterpret_cast<uint32_t*>(sm.vd + (wr + g + 8) * PD + cc) = wm::pack_bf16(v2 * l1, v3 * l1);
+        *reinterpret_cast<uint32_t*>(sm.vn + (wr + g) * PD + cc) = wm::pack_f16(v0, v1);
+        *reinterpret_cast<uint32_t*>(sm.vn + (wr + g + 8) * PD + cc) = wm::pack_f16(v2, v3);
+        *reinterpret_cast<uint32_t*>(sm.vd + (wr + g) * PD + cc) = wm::pack_f16(v0 * l0, v1 * l0);
+        *reinterpret_cast<uint32_t*>(sm.vd + (wr + g + 8) * PD + cc) = wm::pack_f16(v2 * l1, v3 * l1);
         O[j][0] *= e0; O[j][1] *= e0; O[j][2] *= e1; O[j][3] *= e1;
       }
     }
@@ -297,8 +304,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
       for (int jj = 0; jj < 4; jj++) {
         uint32_t bv[4];
         wm::ldb_kn(bv, sm.vn, PD, wc + 16 * jj, k0);
-        wm::mma(O[2 * jj], aa, bv);
-        wm::mma(O[2 * jj + 1], aa, bv + 2);
+        wm::mma_f16(O[2 * jj], aa, bv);
+        wm::mma_f16(O[2 * jj + 1], aa, bv + 2);
       }
     }
     // ---- state update S = e^{G_63} S + K^T diag(e^{G_63 - G}) V' (128 x 128, K = 64); rows 16w ..
@@ -316,8 +323,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
         for (int jj = 0; jj < 8; jj++) {
           uint32_t bv[4];
           wm::ldb_kn(bv, sm.vd, PD, 16 * jj, k0);
-          wm::mma(S[2 * jj], ak, bv);
-          wm::mma(S[2 * jj + 1], ak, bv + 2);
+          wm::mma_f16(S[2 * jj], ak, bv);
+          wm::mma_f16(S[2 * jj + 1], ak, bv + 2);
         }
       }
     }
@@ -345,8 +352,8 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
 #pragma unroll
       for (int j = 0; j < 16; j++) {
         const int cc = 8 * j + 2 * q4;
-        *reinterpret_cast<uint32_t*>(sm.s + r0 * PD + cc) = wm::pack_bf16(S[j][0], S[j][1]);
-        *reinterpret_cast<uint32_t*>(sm.s + (r0 + 8) * PD + cc) = wm::pack_bf16(S[j][2], S[j][3]);
+        *reinterpret_cast<uint32_t*>(sm.s + r0 * PD + cc) = wm::pack_f16(S[j][0], S[j][1]);
+        *reinterpret_cast<uint32_t*>(sm.s + (r0 + 8) * PD + cc) = wm::pack_f16(S[j][2], S[j][3]);
       }
     }
     {
@@ -408,8 +415,10 @@ int launch_gdn_chunk(const GdnScanArgs& a, int dtype, cudaStream_t st) {
   if ((a.q_stride | a.k_stride | a.v_stride) % 4)
     return fail(DUO_EINVAL, "gdn_chunk: q/k/v token strides must be multiples of 4 elements");
   const bool norm = a.norm_w != nullptr;
-  if (dtype == DUO_F32) return norm ? run_chunk<float, true>(a, st) : run_chunk<float, false>(a, st);
-  return norm ? run_chunk<__nv_bfloat16, true>(a, st) : run_chunk<__nv_bfloat16, false>(a, st);
+  return with_act(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    return norm ? run_chunk<T, true>(a, st) : run_chunk<T, false>(a, st);
+  });
 }
 
 }  // namespace duo
@@ -421,7 +430,8 @@ extern "C" int duo_gdn_chunk_fwd(const void* q, const void* k, const void* v, in
                                  int dv, int l2norm_qk, duo_stream stream) {
   DUO_CHECK_ARG(b >= 0 && t >= 0 && h > 0, "gdn_chunk: bad shape");
   DUO_CHECK_ARG(dk == 128 && dv == 128, "gdn_chunk: dk and dv must be 128");
-  DUO_CHECK_ARG(valid_act(in_dtype) && o_dtype == in_dtype, "gdn_chunk: q/k/v/o dtype must be f32 or bf16 (the same)");
+  DUO_CHECK_ARG(valid_act(in_dtype) && o_dtype == in_dtype,
+                "gdn_chunk: q/k/v/o dtype must be f32, bf16 or f16 (the same)");
   DUO_CHECK_ARG(b == 0 || t == 0 || (q && k && v && g && beta && state && o), "gdn_chunk: null pointer");
   return launch_gdn_chunk(op_scan_args(q, k, v, g, beta, state, o, b, t, h, l2norm_qk), in_dtype, as_stream(stream));
 }

@@ -43,7 +43,7 @@ template <int BN> struct TcCfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool F16>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, int M, int N,
                    int K, GemmEpiArgs ep, unsigned* fault) {
@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc::tma_load_2d(sb + s * C::B_BYTES, &tma_b, kb * TC_BK, tile_n, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = tc::idesc_bf16_f32(TC_BM, BN);
+    constexpr uint32_t idesc = tc::idesc_16_f32(TC_BM, BN, F16);
     bool ok = true;
     for (int kb = 0; kb < num_k; kb++) {
       const int s = kb % C::STAGES;
@@ -185,6 +185,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             } else {
               for (int i = 0; i < 4 && n + i < ncols; i++) X[i] += x[i] + (vr ? vr[i] : 0.f);
             }
+          } else if (ep.c_dtype == DUO_F16) {
+            __half* C = static_cast<__half*>(ep.c) + off;
+            if (vec4) {
+              __half2 lo = __floats2half2_rn(x[0], x[1]), hi = __floats2half2_rn(x[2], x[3]);
+              uint2 u;
+              u.x = *reinterpret_cast<uint32_t*>(&lo);
+              u.y = *reinterpret_cast<uint32_t*>(&hi);
+              *reinterpret_cast<uint2*>(C) = u;
+            } else {
+              for (int i = 0; i < 4 && n + i < ncols; i++) C[i] = __float2half_rn(x[i]);
+            }
           } else if (ep.c_dtype == DUO_BF16) {
             __nv_bfloat16* C = static_cast<__nv_bfloat16*>(ep.c) + off;
             if (vec4) {
@@ -233,7 +244,8 @@ static PFN_encodeTiled get_encode_fn() {
   return fn;
 }
 
-int make_tmap_bf16(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_rows, int box_cols) {
+int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
+                int box_cols) {
   PFN_encodeTiled enc = get_encode_fn();
   if (!enc) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16)
@@ -242,7 +254,8 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, long rows, long cols, lon
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  const CUtensorMapDataType dt = dtype == DUO_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
@@ -268,26 +281,42 @@ int tc_fault_read_clear(unsigned* out) {
   return DUO_OK;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool F16>
 static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, int k, const GemmEpiArgs& ep,
                   cudaStream_t st) {
   using C = TcCfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    DUO_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set = true;
   }
   unsigned* fault = tc_fault_ptr();
   if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
   dim3 grid(cdiv(n, BN), cdiv(m, TC_BM));
-  gemm_tc_kernel<BN, EPI><<<grid, TC_THREADS, C::SMEM, st>>>(ta, tb, m, n, k, ep, fault);
+  gemm_tc_kernel<BN, EPI, F16><<<grid, TC_THREADS, C::SMEM, st>>>(ta, tb, m, n, k, ep, fault);
   DUO_LAUNCH_CHECK("gemm_tc_kernel");
   return DUO_OK;
 }
 
-int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, const GemmEpiArgs& ep, cudaStream_t st) {
+template <bool F16>
+static int dispatch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int m, int n, int k, const GemmEpiArgs& ep,
+                       cudaStream_t st) {
+  if (ep.epi == EPI_SWIGLU) return run_tc<256, EPI_SWIGLU, F16>(ta, tb, m, n, k, ep, st);
+  if (ep.epi == EPI_ADD_F32) {
+    if (bn == 256) return run_tc<256, EPI_ADD_F32, F16>(ta, tb, m, n, k, ep, st);
+    if (bn == 128) return run_tc<128, EPI_ADD_F32, F16>(ta, tb, m, n, k, ep, st);
+    return run_tc<64, EPI_ADD_F32, F16>(ta, tb, m, n, k, ep, st);
+  }
+  if (bn == 256) return run_tc<256, EPI_STORE, F16>(ta, tb, m, n, k, ep, st);
+  if (bn == 128) return run_tc<128, EPI_STORE, F16>(ta, tb, m, n, k, ep, st);
+  return run_tc<64, EPI_STORE, F16>(ta, tb, m, n, k, ep, st);
+}
+
+int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dtype, const GemmEpiArgs& ep,
+                   cudaStream_t st) {
   if (m == 0 || n == 0) return DUO_OK;
   DUO_CHECK_ARG(k % TC_BK == 0, "gemm_tc: k must be a multiple of 64");
+  DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_tc: operands must be bf16 or f16");
   // choose the widest N tile that still gives every SM work; SwiGLU needs 256 (gate/up interleaved per 128)
   int bn = 256;
   if (ep.epi != EPI_SWIGLU) {
@@ -298,17 +327,10 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, const Gemm
     DUO_CHECK_ARG(n % 256 == 0, "gemm_tc: SwiGLU epilogue needs n a multiple of 256");
   }
   CUtensorMap ta, tb;
-  DUO_TRY(make_tmap_bf16(&ta, a, m, k, k, TC_BM, TC_BK));
-  DUO_TRY(make_tmap_bf16(&tb, b, n, k, k, bn, TC_BK));
-  if (ep.epi == EPI_SWIGLU) return run_tc<256, EPI_SWIGLU>(ta, tb, m, n, k, ep, st);
-  if (ep.epi == EPI_ADD_F32) {
-    if (bn == 256) return run_tc<256, EPI_ADD_F32>(ta, tb, m, n, k, ep, st);
-    if (bn == 128) return run_tc<128, EPI_ADD_F32>(ta, tb, m, n, k, ep, st);
-    return run_tc<64, EPI_ADD_F32>(ta, tb, m, n, k, ep, st);
-  }
-  if (bn == 256) return run_tc<256, EPI_STORE>(ta, tb, m, n, k, ep, st);
-  if (bn == 128) return run_tc<128, EPI_STORE>(ta, tb, m, n, k, ep, st);
-  return run_tc<64, EPI_STORE>(ta, tb, m, n, k, ep, st);
+  DUO_TRY(make_tmap_16(&ta, a, ab_dtype, m, k, k, TC_BM, TC_BK));
+  DUO_TRY(make_tmap_16(&tb, b, ab_dtype, n, k, k, bn, TC_BK));
+  return ab_dtype == DUO_F16 ? dispatch_tc<true>(ta, tb, bn, m, n, k, ep, st)
+                             : dispatch_tc<false>(ta, tb, bn, m, n, k, ep, st);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -394,7 +416,7 @@ extern "C" int duo_gemm_bf16(const void* a, int m, int k, const void* b, int n, 
   ep.c_dtype = c_dtype;
   ep.ldc = ldc;
   ep.colscale = col_scale;
-  return launch_gemm_tc(a, m, k, b, n, ep, as_stream(stream));
+  return launch_gemm_tc(a, m, k, b, n, DUO_BF16, ep, as_stream(stream));
 }
 
 extern "C" int duo_fault_status(unsigned* out) {

@@ -40,8 +40,10 @@ int launch_gather(const int32_t* ids, int t, const int8_t* q, const float* s, in
 int launch_dequant(const int8_t* q, const float* s, int n, int k, int group, void* out, int out_dtype,
                    cudaStream_t st);
 
-// bf16 tensor-core GEMM: acc[m, n] = A[m, k] . B[n, k]^T, then the epilogue
-int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, const GemmEpiArgs& ep, cudaStream_t st);
+// 16-bit tensor-core GEMM (A and B both bf16 or both f16, ab_dtype): acc[m, n] = A[m, k] . B[n, k]^T, then the
+// epilogue
+int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dtype, const GemmEpiArgs& ep,
+                   cudaStream_t st);
 // f32 CUDA-core GEMM on int8 weights (the f32 engine): acc = A[m, k] . dequant(W)[n, k]^T, then the epilogue
 int launch_gemm_f32_q8(const float* a, int m, int k, const int8_t* q, const float* s, int group, int n,
                        const GemmEpiArgs& ep, cudaStream_t st);
@@ -122,13 +124,13 @@ int launch_attention(const AttnArgs& a, int dtype, cudaStream_t st);
 long attn_work_floats(int b, int nh, int max_len);
 // split-K scratch (floats) the decode planner fills when the workspace does not limit it; 0 = no split
 long attn_decode_scratch_floats(int b, int nh, int nkv, int max_len);
-int launch_attn_prefill_mma(const AttnArgs& a, cudaStream_t st);  // bf16, t > 1, hd 256
+int launch_attn_prefill_mma(const AttnArgs& a, int dtype, cudaStream_t st);  // bf16 / f16, t > 1, hd 256
 
-// int8 -> bf16 copy of a weight matrix for the tensor-core GEMM: dst row of src row n is n, or (interleave > 0) the
-// gate/up interleaved order [gate 128 | up 128]* with `interleave` = rows of each half.  apply_scale = 0 writes
-// bf16(q) exactly (the per-row scale then goes to the GEMM's column scale).
-int launch_pack_bf16(const int8_t* q, const float* s, int n, int k, int group, int interleave, int apply_scale,
-                     __nv_bfloat16* out, float* colscale_out, cudaStream_t st);
+// int8 -> 16-bit (bf16 or f16) copy of a weight matrix for the tensor-core GEMM: dst row of src row n is n, or
+// (interleave > 0) the gate/up interleaved order [gate 128 | up 128]* with `interleave` = rows of each half.
+// apply_scale = 0 writes the int8 values exactly (the per-row scale then goes to the GEMM's column scale).
+int launch_pack16(const int8_t* q, const float* s, int n, int k, int group, int interleave, int apply_scale,
+                  int out_dtype, void* out, float* colscale_out, cudaStream_t st);
 
 GdnScanArgs op_scan_args(const void* q, const void* k, const void* v, const float* g, const float* beta,
                          float* state, void* o, int b, int t, int h, int l2norm_qk);

@@ -103,12 +103,7 @@ __device__ __forceinline__ uint4 ld_stream16(const int8_t* p) {
   return r;
 }
 
-template <typename TX> __device__ __forceinline__ void ld_x16(const TX* p, float* o);
-template <> __device__ __forceinline__ void ld_x16<float>(const float* p, float* o) {
-  load8(p, o);
-  load8(p + 8, o + 8);
-}
-template <> __device__ __forceinline__ void ld_x16<__nv_bfloat16>(const __nv_bfloat16* p, float* o) {
+template <typename TX> __device__ __forceinline__ void ld_x16(const TX* p, float* o) {
   load8(p, o);
   load8(p + 8, o + 8);
 }
@@ -177,12 +172,11 @@ int launch_gemv_t(const void* x, int m, int k, const int8_t* q, const float* s, 
 
 int launch_gemv(const void* x, int x_dtype, int m, int k, const int8_t* q, const float* s, int group, int n, void* y,
                 int y_dtype, int accumulate, cudaStream_t st) {
-  if (x_dtype == DUO_F32 && y_dtype == DUO_F32) return launch_gemv_t<float, float>(x, m, k, q, s, group, n, y, accumulate, st);
-  if (x_dtype == DUO_F32 && y_dtype == DUO_BF16) return launch_gemv_t<float, __nv_bfloat16>(x, m, k, q, s, group, n, y, accumulate, st);
-  if (x_dtype == DUO_BF16 && y_dtype == DUO_F32) return launch_gemv_t<__nv_bfloat16, float>(x, m, k, q, s, group, n, y, accumulate, st);
-  if (x_dtype == DUO_BF16 && y_dtype == DUO_BF16)
-    return launch_gemv_t<__nv_bfloat16, __nv_bfloat16>(x, m, k, q, s, group, n, y, accumulate, st);
-  return fail(DUO_EINVAL, "gemv: x/y dtype must be f32 or bf16");
+  return with_act(x_dtype, [&](auto xt) -> int {
+    return with_act(y_dtype, [&](auto yt) -> int {
+      return launch_gemv_t<decltype(xt), decltype(yt)>(x, m, k, q, s, group, n, y, accumulate, st);
+    });
+  });
 }
 
 int launch_gather(const int32_t* ids, int t, const int8_t* q, const float* s, int group, int k, int vocab, float* y,
@@ -198,16 +192,16 @@ int launch_dequant(const int8_t* q, const float* s, int n, int k, int group, voi
   const long total16 = (long)n * k / 16;
   if (total16 == 0) return DUO_OK;
   const int grid = (int)std::min<long>((total16 + 255) / 256, (long)sm_count() * 16);
-  if (out_dtype == DUO_F32)
-    q8_dequant_kernel<float><<<grid, 256, 0, st>>>(q, s, total16, k, group, static_cast<float*>(out));
-  else
-    q8_dequant_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(q, s, total16, k, group, static_cast<__nv_bfloat16*>(out));
-  DUO_LAUNCH_CHECK("q8_dequant_kernel");
-  return DUO_OK;
+  return with_act(out_dtype, [&](auto ot) -> int {
+    using TO = decltype(ot);
+    q8_dequant_kernel<TO><<<grid, 256, 0, st>>>(q, s, total16, k, group, static_cast<TO*>(out));
+    DUO_LAUNCH_CHECK("q8_dequant_kernel");
+    return DUO_OK;
+  });
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// bf16 pack of an int8 matrix for the tensor-core GEMM (one 128-thread block per row, 8 values per thread)
+// 16-bit (bf16 or f16) pack of an int8 matrix for the tensor-core GEMM (one 128-thread block per row, 8 values per thread)
 
 __device__ __forceinline__ int pack_dst_row(int n, int interleave) {
   if (interleave <= 0) return n;
@@ -216,13 +210,14 @@ __device__ __forceinline__ int pack_dst_row(int n, int interleave) {
   return (r / 128) * 256 + half * 128 + (r % 128);
 }
 
-__global__ void q8_pack_bf16_kernel(const int8_t* __restrict__ q, const float* __restrict__ s, int k, int group,
-                                    int interleave, int apply_scale, __nv_bfloat16* __restrict__ out,
+template <typename TO>
+__global__ void q8_pack16_kernel(const int8_t* __restrict__ q, const float* __restrict__ s, int k, int group,
+                                    int interleave, int apply_scale, TO* __restrict__ out,
                                     float* __restrict__ colscale) {
   const int n = blockIdx.x;
   const int dn = pack_dst_row(n, interleave);
   const int8_t* qr = q + (long)n * k;
-  __nv_bfloat16* orow = out + (long)dn * k;
+  TO* orow = out + (long)dn * k;
   for (int c = threadIdx.x * 8; c < k; c += blockDim.x * 8) {
     const uint2 u = *reinterpret_cast<const uint2*>(qr + c);
     float f[8];
@@ -238,13 +233,18 @@ __global__ void q8_pack_bf16_kernel(const int8_t* __restrict__ q, const float* _
   if (colscale && threadIdx.x == 0) colscale[dn] = s[(long)n * (k / group)];
 }
 
-int launch_pack_bf16(const int8_t* q, const float* s, int n, int k, int group, int interleave, int apply_scale,
-                     __nv_bfloat16* out, float* colscale_out, cudaStream_t st) {
+int launch_pack16(const int8_t* q, const float* s, int n, int k, int group, int interleave, int apply_scale,
+                  int out_dtype, void* out, float* colscale_out, cudaStream_t st) {
   if (n == 0) return DUO_OK;
   if (interleave > 0 && (interleave % 128 || n != 2 * interleave))
     return fail(DUO_EINVAL, "pack: interleave needs n = 2 * interleave, a multiple of 128");
-  q8_pack_bf16_kernel<<<n, 128, 0, st>>>(q, s, k, group, interleave, apply_scale, out, colscale_out);
-  DUO_LAUNCH_CHECK("q8_pack_bf16_kernel");
+  if (out_dtype == DUO_F16)
+    q8_pack16_kernel<__half><<<n, 128, 0, st>>>(q, s, k, group, interleave, apply_scale, static_cast<__half*>(out),
+                                                colscale_out);
+  else
+    q8_pack16_kernel<__nv_bfloat16><<<n, 128, 0, st>>>(q, s, k, group, interleave, apply_scale,
+                                                       static_cast<__nv_bfloat16*>(out), colscale_out);
+  DUO_LAUNCH_CHECK("q8_pack16_kernel");
   return DUO_OK;
 }
 

@@ -87,11 +87,12 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16 with bf16 A and B (both K-major) and an f32 accumulator.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+// Instruction descriptor for kind::f16 with A and B both bf16 (f16 = false) or both f16 (both K-major) and an f32
+// accumulator.
+__host__ __device__ constexpr uint32_t idesc_16_f32(int m, int n, bool f16) {
   return (1u << 4)                      // D format: f32
-         | (1u << 7)                    // A format: bf16
-         | (1u << 10)                   // B format: bf16
+         | ((f16 ? 0u : 1u) << 7)       // A format: f16 = 0, bf16 = 1
+         | ((f16 ? 0u : 1u) << 10)      // B format
          | ((uint32_t)(n >> 3) << 17)   // N / 8
          | ((uint32_t)(m >> 4) << 24);  // M / 16
 }
@@ -128,9 +129,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 
 }  // namespace tc
 
-// Host: build a 2D bf16 tensor map over a row-major [rows, cols] matrix (leading dim ld elements) with a
-// (box_cols x box_rows) box and 128-byte swizzle.  Out-of-range elements of a box read as zero.
-int make_tmap_bf16(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_rows, int box_cols);
+// Host: build a 2D 16-bit (DUO_BF16 / DUO_F16) tensor map over a row-major [rows, cols] matrix (leading dim ld
+// elements) with a (box_cols x box_rows) box and 128-byte swizzle.  Out-of-range elements of a box read as zero.
+int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
+                 int box_cols);
 
 // Device fault word shared by the tensor-core kernels: a bounded wait that gave up ORs a code into it.  tc_fault_ptr()
 // is its device address (kernels take it as a parameter); tc_fault_read_clear() synchronises the device, reads it

@@ -24,7 +24,8 @@ class Config:
     layer_types: Optional[List[str]] = None
     full_attention_interval: int = 4
     # engine options (not in the HF config): int8 group size along K (128 = the reference's q8 format, 0 = one
-    # scale per output row) and the activation dtype ("f32" = the reference's precision, "bf16" = tensor cores)
+    # scale per output row) and the activation dtype: "f32" = the reference's precision (CUDA cores), "bf16" or
+    # "f16" = the tensor-core path with 16-bit activations (f16 keeps 3 more mantissa bits, bf16 more range)
     group: int = 128
     act_dtype: str = "bf16"
 
@@ -34,8 +35,8 @@ class Config:
                                 for i in range(self.num_hidden_layers)]
         if len(self.layer_types) != self.num_hidden_layers:
             raise ValueError("layer_types must have num_hidden_layers entries")
-        if self.act_dtype not in ("f32", "bf16"):
-            raise ValueError("act_dtype must be 'f32' or 'bf16'")
+        if self.act_dtype not in ("f32", "bf16", "f16"):
+            raise ValueError("act_dtype must be 'f32', 'bf16' or 'f16'")
 
     # derived sizes (engine/model.js:44-54)
     @property

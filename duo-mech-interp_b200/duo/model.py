@@ -27,7 +27,7 @@ class Model:
             nh=c.num_attention_heads, nkv=c.num_key_value_heads, hd=c.head_dim, rot=c.rot, theta=c.rope_theta,
             eps=c.rms_norm_eps, hk=c.linear_num_key_heads, hv=c.linear_num_value_heads, dk=c.linear_key_head_dim,
             dv=c.linear_value_head_dim, ks=c.linear_conv_kernel_dim, full_attention_host=C.cast(full, C.c_void_p),
-            group=c.group, act_dtype=L.DUO_F32 if c.act_dtype == "f32" else L.DUO_BF16)
+            group=c.group, act_dtype={"f32": L.DUO_F32, "bf16": L.DUO_BF16, "f16": L.DUO_F16}[c.act_dtype])
         h = C.c_void_p()
         L.call("duo_engine_create", C.byref(self._c), C.byref(h))
         self._h = h

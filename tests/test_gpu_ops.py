@@ -161,12 +161,13 @@ def test_gdn_recurrent_bf16(ops):
     assert rel_max(st, rs) < 1e-3
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("b,t,h,l2", [(1, 64, 2, False), (2, 100, 4, True), (1, 300, 16, False), (3, 17, 2, True),
                                       (2, 1024, 16, False)])
-def test_gdn_chunk_bf16(ops, b, t, h, l2):
-    """Chunked tensor-core scan vs the oracle's chunk rule (f64) on the same bf16-rounded inputs; bf16 bound 2e-2."""
+def test_gdn_chunk_16bit(ops, dtype, b, t, h, l2):
+    """Chunked tensor-core scan vs the oracle's chunk rule (f64) on the same 16-bit inputs; 16-bit bound 2e-2."""
     q, k, v, g, beta, s0 = _gdn_inputs(b, t, h, 1000 + t, not l2)
-    qb, kb, vb = (x.to(torch.bfloat16) for x in (q, k, v))
+    qb, kb, vb = (x.to(dtype) for x in (q, k, v))
     ro, rs = mixer.chunk_gated_delta_rule(qb.double(), kb.double(), vb.double(), g.double(), beta.double(),
                                           state=s0.double(), l2norm_qk=l2)
     st = s0.clone().cuda()
@@ -200,7 +201,7 @@ def _attn_ref(q, kc, vc, start, gate):
     return out
 
 
-@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2)])
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2), (torch.float16, 2e-2)])
 @pytest.mark.parametrize("b,t,starts,max_len,nh,nkv", [(2, 70, [0, 30], 128, 8, 2), (3, 1, [0, 5, 900], 1024, 8, 2),
                                                         (2, 1, [4095, 3000], 4096, 8, 2), (1, 33, [100], 256, 8, 2),
                                                         (1, 300, [0], 512, 8, 2), (2, 129, [7, 0], 200, 4, 2),
