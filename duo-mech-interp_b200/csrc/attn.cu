@@ -295,11 +295,24 @@ static void decode_plan(const AttnArgs& a, int* nsplit, int* split_len) {
   *split_len = cdiv(a.max_len, ns);
 }
 
-long attn_decode_scratch_floats(int b, int nh, int nkv, int max_len) {
-  const long blocks = (long)std::max(1, b) * nkv;
-  int ns = (int)std::max<long>(1, (2L * sm_count() + blocks - 1) / blocks);
-  ns = std::min(ns, std::max(1, cdiv(max_len, 256)));
+long attn_decode_scratch_floats(int b, int nh, int nkv, int max_len, int dtype) {
+  int ns;
+  if (dtype != DUO_F32) {
+    ns = attn_decode_mma_plan(b, nkv, max_len, nullptr);
+  } else {
+    const long blocks = (long)std::max(1, b) * nkv;
+    ns = (int)std::max<long>(1, (2L * sm_count() + blocks - 1) / blocks);
+    ns = std::min(ns, std::max(1, cdiv(max_len, 256)));
+  }
   return ns > 1 ? (long)b * nh * ns * (AP_HD + 2) : 0;
+}
+
+int launch_attn_combine(const AttnArgs& a, int dtype, int nsplit, cudaStream_t st) {
+  return with_act(dtype, [&](auto tag) -> int {
+    attn_combine_kernel<decltype(tag)><<<dim3(a.nh, a.b), AP_HD, 0, st>>>(a, nsplit);
+    DUO_LAUNCH_CHECK("attn_combine_kernel");
+    return DUO_OK;
+  });
 }
 
 long attn_work_floats(int b, int nh, int max_len) {
@@ -314,6 +327,8 @@ static int run_attention(const AttnArgs& a, cudaStream_t st) {
     if (rep == 1 || rep == 2 || rep == 4)  // tensor cores
       return launch_attn_prefill_mma(a, std::is_same<T, __half>::value ? DUO_F16 : DUO_BF16, st);
   }
+  if (!std::is_same<T, float>::value && a.t == 1)  // HBM-streaming tensor-core decode
+    return launch_attn_decode_mma(a, std::is_same<T, __half>::value ? DUO_F16 : DUO_BF16, st);
   if (a.t == 1) {
     int ns, sl;
     decode_plan(a, &ns, &sl);

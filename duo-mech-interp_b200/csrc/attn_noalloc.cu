@@ -67,7 +67,7 @@ extern "C" int duo_attention_noalloc(const void* q, const void* kc, const void* 
   a.gate = gate; a.gate_stride = gate_stride; a.gate_hstride = hd; a.o = o;
   a.b = b; a.t = t; a.nh = nh; a.nkv = nkv; a.hd = hd; a.max_len = max_len; a.scale = scale;
   if (t == 1 && b > 0) {
-    const long need = attn_decode_scratch_floats(b, nh, nkv, max_len);
+    const long need = attn_decode_scratch_floats(b, nh, nkv, max_len, dtype);
     if (need > kScratchFloats)
       return fail(DUO_EINVAL, "attention_noalloc: this decode call needs " + std::to_string(need) +
                                   " floats of split-K scratch (b * nh * splits * (hd + 2)) but the static array holds " +

@@ -207,7 +207,6 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ca.dt_bias = L.dt_bias; ca.qkv_out = e->qkv; ca.g_out = e->g; ca.beta_out = e->beta;
       ca.hk = c.hk; ca.hv = c.hv; ca.dk = c.dk; ca.dv = c.dv; ca.ks = c.ks;
       ca.rows = rows; ca.t = T; ca.row_base = row_base;
-      PROF_TRY(DUO_PROF_GDN_CONV, launch_gdn_conv(ca, act, st));
       GdnScanArgs sa{};
       const size_t es = e->act_size;
       sa.q = e->qkv;
@@ -221,9 +220,15 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       sa.z = static_cast<const char*>(e->y) + (size_t)e->conv_dim * es;
       sa.z_stride = wproj;
       sa.norm_w = L.gnorm; sa.head_scale = S.head_scale; sa.eps = c.eps;
-      // prefill of the bf16 engine: chunked tensor-core scan; decode and the f32 engine: the recurrent form
-      if (act != DUO_F32 && T > 16) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
-      else PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_recurrent(sa, act, st));
+      if (T == 1 && c.hk == c.hv) {
+        // decode: one fused kernel from the projection to the gated norm
+        PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_decode(ca, sa, act, st));
+      } else {
+        PROF_TRY(DUO_PROF_GDN_CONV, launch_gdn_conv(ca, act, st));
+        // prefill of the 16-bit engines: chunked tensor-core scan; the f32 engine: the recurrent form
+        if (act != DUO_F32 && T > 16) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
+        else PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_recurrent(sa, act, st));
+      }
       out_k = e->vd;
     } else {
       AttnPrepArgs pa{};

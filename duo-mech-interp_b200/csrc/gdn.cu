@@ -220,6 +220,154 @@ int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st) {
   });
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// decode step (t = 1) of the engine, everything of a Gated DeltaNet layer between the projection and out_proj in one
+// kernel: conv1d + SiLU on this token (with the carried state, which it also shifts), l2norm of q and k, the gates,
+// the delta-rule update of the f32 state and the gated RMSNorm.  One cluster of 4 CTAs per (row, head); CTA s owns
+// state columns [32 s, 32 s + 32) and all 128 rows; thread (rg = tid / 8, cg = tid % 8) holds rows 8 rg .. 8 rg + 7 of
+// columns 32 s + 4 cg .. + 3 as 8 float4 (16-byte state traffic).  Needs hk == hv (each q/k channel belongs to one
+// head, so one CTA of one cluster owns its conv-state shift).
+
+constexpr int DEC_CS = 4;
+
+template <typename T>
+__global__ void __cluster_dims__(DEC_CS, 1, 1) __launch_bounds__(128) gdn_decode_kernel(GdnConvArgs ca,
+                                                                                       GdnScanArgs a) {
+  __shared__ float qs[128], ks[128], vs[32];
+  __shared__ float red[4][2][32];  // per warp, per reduction (u, o), per column
+  __shared__ float red32[32];
+  __shared__ float part;
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cg = tid & 7, rg = tid >> 3;
+  const int j0 = s * 32;
+  const int R = a.state_row0 + b;
+  const int conv_dim = 2 * ca.hk * 128 + ca.hv * 128;
+  const T* y = static_cast<const T*>(ca.y);
+  const long yrow = (long)b * ca.w;
+  cg::cluster_group cluster = cg::this_cluster();
+
+  // 1. issue the state loads first (the long-latency part), then the conv while they fly
+  float4* S4 = reinterpret_cast<float4*>(a.state + (((long)R * a.h + h) * 128) * 128);
+  float4 st[8];
+#pragma unroll
+  for (int r = 0; r < 8; r++) st[r] = S4[(rg * 8 + r) * 32 + s * 8 + cg];
+
+  auto conv_ch = [&](int ch, float* xin_new) {
+    const float* cs = ca.conv_state + ((long)R * 3) * conv_dim + ch;
+    const float x0 = cs[0], x1 = cs[(long)conv_dim], x2 = cs[2L * conv_dim];
+    const float x3 = to_f(y[yrow + ch]);
+    const float* w = ca.conv_w + (long)ch * 4;
+    *xin_new = x3;
+    return siluf_(w[0] * x0 + w[1] * x1 + w[2] * x2 + w[3] * x3);
+  };
+  // q and k channel `tid` of head h (hk == hv); v channels j0 .. j0 + 31 of head h
+  float qx, kx;
+  const float qv = conv_ch(h * 128 + tid, &qx);
+  const float kv = conv_ch(ca.hk * 128 + h * 128 + tid, &kx);
+  float vx = 0.f, vv = 0.f;
+  if (tid < 32) vv = conv_ch(2 * ca.hk * 128 + h * 128 + j0 + tid, &vx);
+  const float sq = block_sum(qv * qv, red32);
+  const float sk = block_sum(kv * kv, red32);
+  qs[tid] = qv * rsqrtf(sq + 1e-6f) * rsqrtf(128.f);
+  ks[tid] = kv * rsqrtf(sk + 1e-6f);
+  if (tid < 32) vs[tid] = vv;
+  const long gb = yrow + conv_dim + ca.hv * 128;
+  const float beta = sigmoidf_(to_f(y[gb + h]));
+  const float gdec = expf(-expf(ca.a_log[h]) * softplusf_(to_f(y[gb + ca.hv + h]) + ca.dt_bias[h]));
+  __syncthreads();
+
+  // 2. u = S^T k after the decay; then delta, S += k delta^T, o = S^T q
+  float u4[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int r = 0; r < 8; r++) {
+    const float kr = ks[rg * 8 + r];
+    st[r].x *= gdec; st[r].y *= gdec; st[r].z *= gdec; st[r].w *= gdec;
+    u4[0] = fmaf(st[r].x, kr, u4[0]); u4[1] = fmaf(st[r].y, kr, u4[1]);
+    u4[2] = fmaf(st[r].z, kr, u4[2]); u4[3] = fmaf(st[r].w, kr, u4[3]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    u4[i] += __shfl_xor_sync(0xffffffffu, u4[i], 8);
+    u4[i] += __shfl_xor_sync(0xffffffffu, u4[i], 16);
+  }
+  if (lane < 8) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) red[warp][0][cg * 4 + i] = u4[i];
+  }
+  __syncthreads();
+  float d4[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int c = cg * 4 + i;
+    const float u = red[0][0][c] + red[1][0][c] + red[2][0][c] + red[3][0][c];
+    d4[i] = beta * (vs[c] - u);
+  }
+  float o4[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int r = 0; r < 8; r++) {
+    const float kr = ks[rg * 8 + r], qr = qs[rg * 8 + r];
+    st[r].x = fmaf(kr, d4[0], st[r].x); st[r].y = fmaf(kr, d4[1], st[r].y);
+    st[r].z = fmaf(kr, d4[2], st[r].z); st[r].w = fmaf(kr, d4[3], st[r].w);
+    o4[0] = fmaf(st[r].x, qr, o4[0]); o4[1] = fmaf(st[r].y, qr, o4[1]);
+    o4[2] = fmaf(st[r].z, qr, o4[2]); o4[3] = fmaf(st[r].w, qr, o4[3]);
+  }
+#pragma unroll
+  for (int r = 0; r < 8; r++) S4[(rg * 8 + r) * 32 + s * 8 + cg] = st[r];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    o4[i] += __shfl_xor_sync(0xffffffffu, o4[i], 8);
+    o4[i] += __shfl_xor_sync(0xffffffffu, o4[i], 16);
+  }
+  if (lane < 8) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) red[warp][1][cg * 4 + i] = o4[i];
+  }
+  __syncthreads();
+  // 3. gated RMSNorm over the head's 128 outputs: this CTA's 32, summed over the cluster
+  float o = 0.f;
+  if (tid < 32) o = red[0][1][tid] + red[1][1][tid] + red[2][1][tid] + red[3][1][tid];
+  float ss = tid < 32 ? warp_sum(o * o) : 0.f;
+  if (tid == 0) part = ss;
+  cluster.sync();  // every CTA has read the old conv state of q / k and published its partial
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < DEC_CS; i++) tot += *cluster.map_shared_rank(&part, i);
+  if (tid < 32) {
+    const int j = j0 + tid;
+    const float rms = rsqrtf(tot / 128.f + a.eps);
+    const float z = to_f(static_cast<const T*>(a.z)[(long)b * a.z_stride + h * 128 + j]);
+    const float hs = a.head_scale ? a.head_scale[h] : 1.f;
+    static_cast<T*>(a.o)[(long)b * a.o_stride + h * 128 + j] = from_f<T>(o * rms * a.norm_w[j] * siluf_(z) * hs);
+    // shift the conv state of this CTA's v channels
+    float* cs = ca.conv_state + ((long)R * 3) * conv_dim + 2 * ca.hk * 128 + h * 128 + j;
+    const float x1 = cs[(long)conv_dim], x2 = cs[2L * conv_dim];
+    cs[0] = x1; cs[(long)conv_dim] = x2; cs[2L * conv_dim] = vx;
+  }
+  if (s == 0) {  // rank 0 shifts the q / k conv state of the head, after every rank has read it
+#pragma unroll
+    for (int which = 0; which < 2; which++) {
+      const int ch = which * ca.hk * 128 + h * 128 + tid;
+      float* cs = ca.conv_state + ((long)R * 3) * conv_dim + ch;
+      const float x1 = cs[(long)conv_dim], x2 = cs[2L * conv_dim];
+      cs[0] = x1; cs[(long)conv_dim] = x2; cs[2L * conv_dim] = which ? kx : qx;
+    }
+  }
+  cluster.sync();  // peers may still read this CTA's `part`
+}
+
+int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cudaStream_t st) {
+  if (a.b == 0) return DUO_OK;
+  if (a.t != 1 || ca.t != 1) return fail(DUO_EINVAL, "gdn_decode: one token per row");
+  if (a.dk != 128 || a.dv != 128 || ca.ks != 4 || ca.hk != ca.hv || !a.norm_w)
+    return fail(DUO_EINVAL, "gdn_decode: needs dk = dv = 128, ks = 4, hk == hv and the gated norm");
+  return with_act(dtype, [&](auto tag) -> int {
+    gdn_decode_kernel<decltype(tag)><<<dim3(DEC_CS, a.h, a.b), 128, 0, st>>>(ca, a);
+    DUO_LAUNCH_CHECK("gdn_decode_kernel");
+    return DUO_OK;
+  });
+}
+
 static int check_gdn_op(const void* q, const void* k, const void* v, int in_dtype, const float* g, const float* beta,
                         float* state, void* o, int o_dtype, int b, int t, int h, int dk, int dv) {
   DUO_CHECK_ARG(b >= 0 && t >= 0 && h > 0, "gdn: bad shape");

@@ -35,19 +35,23 @@ __device__ __forceinline__ float push_apply(const PushTable& pt, int r, int n, f
 
 constexpr int TC_BM = 128, TC_BK = 64, TC_THREADS = 192;
 
-template <int BN> struct TcCfg {
+// LITE: a ~96 KB ring so two CTAs share an SM (small grids, e.g. decode), else a ~192 KB ring (one CTA per SM)
+template <int BN, bool LITE> struct TcCfg {
   static constexpr int A_BYTES = TC_BM * TC_BK * 2;
   static constexpr int B_BYTES = BN * TC_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = ((LITE ? 96 : 192) * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-template <int BN, int EPI, bool F16>
+template <int BN, int EPI, bool F16, bool LITE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, int M, int N,
-                   int K, GemmEpiArgs ep, unsigned* fault) {
-  using C = TcCfg<BN>;
+                   int K, int kper, GemmEpiArgs ep, unsigned* fault) {
+  using C = TcCfg<BN, LITE>;
+  static_assert(C::STAGES >= 2, "ring too small");
+  static_assert(TC_BM * ((EPI == EPI_SWIGLU ? BN / 2 : BN) + 4) * 4 <= C::STAGES * C::STAGE_BYTES,
+                "the epilogue tile must fit in the ring");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
@@ -59,7 +63,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_n = blockIdx.x * BN, tile_m = blockIdx.y * TC_BM;
-  const int num_k = K / TC_BK;
+  // split-K (residual-add epilogue only): this CTA reduces k blocks [kb0, kb0 + num_k)
+  const int kb0 = blockIdx.z * kper;
+  const int num_k = min(kper, K / TC_BK - kb0);
+  const bool split = gridDim.z > 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; s++) {
@@ -86,8 +93,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         break;
       }
       tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-      tc::tma_load_2d(sa + s * C::A_BYTES, &tma_a, kb * TC_BK, tile_m, &full[s]);
-      tc::tma_load_2d(sb + s * C::B_BYTES, &tma_b, kb * TC_BK, tile_n, &full[s]);
+      tc::tma_load_2d(sa + s * C::A_BYTES, &tma_a, (kb0 + kb) * TC_BK, tile_m, &full[s]);
+      tc::tma_load_2d(sb + s * C::B_BYTES, &tma_b, (kb0 + kb) * TC_BK, tile_n, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = tc::idesc_16_f32(TC_BM, BN, F16);
@@ -173,8 +180,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           if (EPI == EPI_ADD_F32) {
             float* X = static_cast<float*>(ep.c) + off;
-            const float* vr = ep.vec ? ep.vec + (long)r * ep.ldc + n : nullptr;
-            if (vec4) {
+            const float* vr = (ep.vec && blockIdx.z == 0) ? ep.vec + (long)r * ep.ldc + n : nullptr;
+            if (split) {  // partial sums of a K split: accumulate atomically
+              for (int i = 0; i < 4 && n + i < ncols; i++) atomicAdd(X + i, x[i] + (vr ? vr[i] : 0.f));
+            } else if (vec4) {
               float4 o = *reinterpret_cast<float4*>(X);
               o.x += x[0]; o.y += x[1]; o.z += x[2]; o.w += x[3];
               if (vr) {
@@ -281,35 +290,46 @@ int tc_fault_read_clear(unsigned* out) {
   return DUO_OK;
 }
 
-template <int BN, int EPI, bool F16>
-static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, int k, const GemmEpiArgs& ep,
-                  cudaStream_t st) {
-  using C = TcCfg<BN>;
+template <int BN, int EPI, bool F16, bool LITE>
+static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, int k, int ksplit,
+                  const GemmEpiArgs& ep, cudaStream_t st) {
+  using C = TcCfg<BN, LITE>;
   static bool attr_set = false;
   if (!attr_set) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    DUO_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, F16, LITE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      C::SMEM));
     attr_set = true;
   }
   unsigned* fault = tc_fault_ptr();
   if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
-  dim3 grid(cdiv(n, BN), cdiv(m, TC_BM));
-  gemm_tc_kernel<BN, EPI, F16><<<grid, TC_THREADS, C::SMEM, st>>>(ta, tb, m, n, k, ep, fault);
+  const int num_k = k / TC_BK;
+  const int kper = cdiv(num_k, ksplit);
+  dim3 grid(cdiv(n, BN), cdiv(m, TC_BM), cdiv(num_k, kper));
+  gemm_tc_kernel<BN, EPI, F16, LITE><<<grid, TC_THREADS, C::SMEM, st>>>(ta, tb, m, n, k, kper, ep, fault);
   DUO_LAUNCH_CHECK("gemm_tc_kernel");
   return DUO_OK;
 }
 
 template <bool F16>
-static int dispatch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int m, int n, int k, const GemmEpiArgs& ep,
-                       cudaStream_t st) {
-  if (ep.epi == EPI_SWIGLU) return run_tc<256, EPI_SWIGLU, F16>(ta, tb, m, n, k, ep, st);
+static int dispatch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int bn, bool lite, int ksplit, int m, int n,
+                       int k, const GemmEpiArgs& ep, cudaStream_t st) {
+  if (ep.epi == EPI_SWIGLU)
+    return lite ? run_tc<128, EPI_SWIGLU, F16, true>(ta, tb, m, n, k, 1, ep, st)
+                : run_tc<128, EPI_SWIGLU, F16, false>(ta, tb, m, n, k, 1, ep, st);
   if (ep.epi == EPI_ADD_F32) {
-    if (bn == 256) return run_tc<256, EPI_ADD_F32, F16>(ta, tb, m, n, k, ep, st);
-    if (bn == 128) return run_tc<128, EPI_ADD_F32, F16>(ta, tb, m, n, k, ep, st);
-    return run_tc<64, EPI_ADD_F32, F16>(ta, tb, m, n, k, ep, st);
+    if (bn == 256) return run_tc<256, EPI_ADD_F32, F16, false>(ta, tb, m, n, k, 1, ep, st);
+    if (bn == 128)
+      return lite ? run_tc<128, EPI_ADD_F32, F16, true>(ta, tb, m, n, k, ksplit, ep, st)
+                  : run_tc<128, EPI_ADD_F32, F16, false>(ta, tb, m, n, k, 1, ep, st);
+    return lite ? run_tc<64, EPI_ADD_F32, F16, true>(ta, tb, m, n, k, ksplit, ep, st)
+                : run_tc<64, EPI_ADD_F32, F16, false>(ta, tb, m, n, k, 1, ep, st);
   }
-  if (bn == 256) return run_tc<256, EPI_STORE, F16>(ta, tb, m, n, k, ep, st);
-  if (bn == 128) return run_tc<128, EPI_STORE, F16>(ta, tb, m, n, k, ep, st);
-  return run_tc<64, EPI_STORE, F16>(ta, tb, m, n, k, ep, st);
+  if (bn == 256) return run_tc<256, EPI_STORE, F16, false>(ta, tb, m, n, k, 1, ep, st);
+  if (bn == 128)
+    return lite ? run_tc<128, EPI_STORE, F16, true>(ta, tb, m, n, k, 1, ep, st)
+                : run_tc<128, EPI_STORE, F16, false>(ta, tb, m, n, k, 1, ep, st);
+  return lite ? run_tc<64, EPI_STORE, F16, true>(ta, tb, m, n, k, 1, ep, st)
+              : run_tc<64, EPI_STORE, F16, false>(ta, tb, m, n, k, 1, ep, st);
 }
 
 int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dtype, const GemmEpiArgs& ep,
@@ -317,20 +337,29 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dty
   if (m == 0 || n == 0) return DUO_OK;
   DUO_CHECK_ARG(k % TC_BK == 0, "gemm_tc: k must be a multiple of 64");
   DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_tc: operands must be bf16 or f16");
-  // choose the widest N tile that still gives every SM work; SwiGLU needs 256 (gate/up interleaved per 128)
-  int bn = 256;
-  if (ep.epi != EPI_SWIGLU) {
-    const long tiles_m = cdiv(m, TC_BM);
-    if (tiles_m * cdiv(n, 256) < sm_count()) bn = 128;
-    if (tiles_m * cdiv(n, 128) < sm_count()) bn = 64;
+  const int sms = sm_count();
+  const long tiles_m = cdiv(m, TC_BM);
+  // the widest N tile that still gives every SM work; SwiGLU tiles are 128 wide (gate / up interleaved per 64)
+  int bn = 128;
+  if (ep.epi == EPI_SWIGLU) {
+    DUO_CHECK_ARG(n % 128 == 0, "gemm_tc: SwiGLU epilogue needs n a multiple of 128");
   } else {
-    DUO_CHECK_ARG(n % 256 == 0, "gemm_tc: SwiGLU epilogue needs n a multiple of 256");
+    bn = 256;
+    if (tiles_m * cdiv(n, 256) < sms) bn = 128;
+    if (tiles_m * cdiv(n, 128) < sms) bn = 64;
+  }
+  const long tiles = tiles_m * cdiv(n, bn);
+  const bool lite = bn <= 128 && tiles < 2L * sms;  // small grid: two CTAs per SM
+  int ksplit = 1;
+  if (ep.epi == EPI_ADD_F32 && lite) {  // still too few CTAs: split K, partial sums added atomically
+    const int num_k = k / TC_BK;
+    ksplit = (int)std::max<long>(1, std::min<long>({2L * sms / tiles, 8, num_k / 4}));
   }
   CUtensorMap ta, tb;
   DUO_TRY(make_tmap_16(&ta, a, ab_dtype, m, k, k, TC_BM, TC_BK));
   DUO_TRY(make_tmap_16(&tb, b, ab_dtype, n, k, k, bn, TC_BK));
-  return ab_dtype == DUO_F16 ? dispatch_tc<true>(ta, tb, bn, m, n, k, ep, st)
-                             : dispatch_tc<false>(ta, tb, bn, m, n, k, ep, st);
+  return ab_dtype == DUO_F16 ? dispatch_tc<true>(ta, tb, bn, lite, ksplit, m, n, k, ep, st)
+                             : dispatch_tc<false>(ta, tb, bn, lite, ksplit, m, n, k, ep, st);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

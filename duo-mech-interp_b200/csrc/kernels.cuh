@@ -19,7 +19,7 @@ struct PushTable {
 enum GemmEpi {
   EPI_STORE = 0,   // C[m, n] = acc * colscale[n]                   (bf16 or f32 C)
   EPI_ADD_F32 = 1, // X[m, n] += acc * colscale[n] (+ vec[row(m), n])  (f32 residual stream)
-  EPI_SWIGLU = 2   // gate/up interleaved per 128 columns: A[m, j] = silu(g) * u, then pushes   (bf16 A)
+  EPI_SWIGLU = 2   // gate/up interleaved per 64 columns: A[m, j] = silu(g) * u, then pushes   (16-bit A)
 };
 
 struct GemmEpiArgs {
@@ -89,6 +89,8 @@ struct GdnScanArgs {
   const float* norm_w; const float* head_scale; float eps;
 };
 int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st);
+// decode step (t = 1): conv + gates + l2norm + delta rule + gated norm in one kernel (needs hk == hv)
+int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cudaStream_t st);
 int launch_gdn_chunk(const GdnScanArgs& a, int dtype, cudaStream_t st);
 
 // ---- gated attention
@@ -122,12 +124,16 @@ struct AttnArgs {
 };
 int launch_attention(const AttnArgs& a, int dtype, cudaStream_t st);
 long attn_work_floats(int b, int nh, int max_len);
-// split-K scratch (floats) the decode planner fills when the workspace does not limit it; 0 = no split
-long attn_decode_scratch_floats(int b, int nh, int nkv, int max_len);
+// split-K scratch (floats) the decode planner of `dtype` fills when the workspace does not limit it; 0 = no split
+long attn_decode_scratch_floats(int b, int nh, int nkv, int max_len, int dtype);
+// 16-bit decode (t == 1) on the tensor cores, its split plan (splits; *split_len keys per split) and the combine
+int launch_attn_decode_mma(const AttnArgs& a, int dtype, cudaStream_t st);
+int attn_decode_mma_plan(int b, int nkv, int max_len, int* split_len);
+int launch_attn_combine(const AttnArgs& a, int dtype, int nsplit, cudaStream_t st);
 int launch_attn_prefill_mma(const AttnArgs& a, int dtype, cudaStream_t st);  // bf16 / f16, t > 1, hd 256
 
 // int8 -> 16-bit (bf16 or f16) copy of a weight matrix for the tensor-core GEMM: dst row of src row n is n, or
-// (interleave > 0) the gate/up interleaved order [gate 128 | up 128]* with `interleave` = rows of each half.
+// (interleave > 0) the gate/up interleaved order [gate 64 | up 64]* with `interleave` = rows of each half.
 // apply_scale = 0 writes the int8 values exactly (the per-row scale then goes to the GEMM's column scale).
 int launch_pack16(const int8_t* q, const float* s, int n, int k, int group, int interleave, int apply_scale,
                   int out_dtype, void* out, float* colscale_out, cudaStream_t st);

@@ -207,7 +207,7 @@ __device__ __forceinline__ int pack_dst_row(int n, int interleave) {
   if (interleave <= 0) return n;
   const int half = n >= interleave;            // 0: gate row, 1: up row
   const int r = n - half * interleave;
-  return (r / 128) * 256 + half * 128 + (r % 128);
+  return (r / 64) * 128 + half * 64 + (r % 64);
 }
 
 template <typename TO>
@@ -236,8 +236,8 @@ __global__ void q8_pack16_kernel(const int8_t* __restrict__ q, const float* __re
 int launch_pack16(const int8_t* q, const float* s, int n, int k, int group, int interleave, int apply_scale,
                   int out_dtype, void* out, float* colscale_out, cudaStream_t st) {
   if (n == 0) return DUO_OK;
-  if (interleave > 0 && (interleave % 128 || n != 2 * interleave))
-    return fail(DUO_EINVAL, "pack: interleave needs n = 2 * interleave, a multiple of 128");
+  if (interleave > 0 && (interleave % 64 || n != 2 * interleave))
+    return fail(DUO_EINVAL, "pack: interleave needs n = 2 * interleave, a multiple of 64");
   if (out_dtype == DUO_F16)
     q8_pack16_kernel<__half><<<n, 128, 0, st>>>(q, s, k, group, interleave, apply_scale, static_cast<__half*>(out),
                                                 colscale_out);
