@@ -18,13 +18,6 @@ namespace {
 
 constexpr int DHD = 256, DP = DHD + 8, DBK = 64, DST = 3;
 
-__device__ __forceinline__ void cpa16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(wm::saddr(dst)), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cpa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 }  // namespace
 
 constexpr int kDecodeSmem = (16 + 2 * DST * DBK) * DP * 2;
@@ -60,14 +53,14 @@ __global__ void __launch_bounds__(128, 1) attn_decode_mma_kernel(AttnArgs a, int
       const int key = kbeg + kt * DBK + r;
       const bool ok = key < kend;
       const long at = (((long)R * a.max_len + (ok ? key : 0)) * a.nkv + kvh) * DHD + c;
-      cpa16(Ks + (stage * DBK + r) * DP + c, kc + at, ok);
-      cpa16(Vs + (stage * DBK + r) * DP + c, vc + at, ok);
+      cp_async16(Ks + (stage * DBK + r) * DP + c, kc + at, ok);
+      cp_async16(Vs + (stage * DBK + r) * DP + c, vc + at, ok);
     }
   };
 #pragma unroll
   for (int s = 0; s < DST - 1; s++) {
     if (s < ntiles) load_tile(s, s);
-    cpa_commit();
+    cp_commit();
   }
   const float sl2 = a.scale * 1.4426950408889634f;
   float O[32][4];
@@ -78,10 +71,10 @@ __global__ void __launch_bounds__(128, 1) attn_decode_mma_kernel(AttnArgs a, int
   float mrow = -INFINITY, lrow = 0.f;  // row g (rows g + 8 are padding)
 
   for (int kt = 0; kt < ntiles; kt++) {
-    cpa_wait<DST - 2>();
+    cp_wait<DST - 2>();
     __syncthreads();  // tile kt is in; every warp is done with tile kt - 1
     if (kt + DST - 1 < ntiles) load_tile(kt + DST - 1, (kt + DST - 1) % DST);
-    cpa_commit();
+    cp_commit();
     const int stage = kt % DST;
     const T16* Kb = Ks + stage * DBK * DP;
     const T16* Vb = Vs + stage * DBK * DP;
@@ -134,7 +127,7 @@ __global__ void __launch_bounds__(128, 1) attn_decode_mma_kernel(AttnArgs a, int
       wm::Ops<T16>::mma(O[2 * nn + 1], pf, bv + 2);
     }
   }
-  cpa_wait<0>();
+  cp_wait<0>();
   __syncthreads();  // the K / V ring is free: reuse it for the merge
   float* mw = reinterpret_cast<float*>(Ks);    // [4 warps][16]
   float* lw = mw + 4 * 16;                     // [4 warps][16]

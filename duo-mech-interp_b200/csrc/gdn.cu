@@ -223,137 +223,157 @@ int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st) {
 // ---------------------------------------------------------------------------------------------------------------
 // decode step (t = 1) of the engine, everything of a Gated DeltaNet layer between the projection and out_proj in one
 // kernel: conv1d + SiLU on this token (with the carried state, which it also shifts), l2norm of q and k, the gates,
-// the delta-rule update of the f32 state and the gated RMSNorm.  One cluster of 4 CTAs per (row, head); CTA s owns
-// state columns [32 s, 32 s + 32) and all 128 rows; thread (rg = tid / 8, cg = tid % 8) holds rows 8 rg .. 8 rg + 7 of
-// columns 32 s + 4 cg .. + 3 as 8 float4 (16-byte state traffic).  Needs hk == hv (each q/k channel belongs to one
-// head, so one CTA of one cluster owns its conv-state shift).
+// the delta-rule update of the f32 state and the gated RMSNorm.
+//
+// The step is bound by the state: 64 KB read and written per (row, head).  A persistent grid (DEC_CPS CTAs per SM)
+// walks the (row, head) items; each item is two slices of 64 state columns x 128 rows (32 KB) that stream through a
+// DEC_NS-deep shared-memory ring filled by cp.async, so while one slice is updated the next two are in flight, across
+// item boundaries too.  Thread (rg = tid / 16, cg = tid % 16) owns rows 8 rg .. 8 rg + 7 of the slice's columns
+// 4 cg .. 4 cg + 3: it copies exactly those 8 float4 into the ring and is their only reader, so the ring needs no
+// barrier (a thread's cp.async.wait_group makes its own copies visible to it).  Needs hk == hv (one CTA owns each
+// q/k channel's conv-state shift).
 
-constexpr int DEC_CS = 4;
+constexpr int DEC_THREADS = 256, DEC_NS = 3, DEC_CPS = 2;
+constexpr int DEC_SLICE = 128 * 64;  // floats
+constexpr int DEC_SMEM = DEC_NS * DEC_SLICE * 4;
 
 template <typename T>
-__global__ void __cluster_dims__(DEC_CS, 1, 1) __launch_bounds__(128) gdn_decode_kernel(GdnConvArgs ca,
-                                                                                       GdnScanArgs a) {
-  __shared__ float qs[128], ks[128], vs[32];
-  __shared__ float red[4][2][32];  // per warp, per reduction (u, o), per column
-  __shared__ float red32[32];
-  __shared__ float part;
-  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+__global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnConvArgs ca, GdnScanArgs a) {
+  extern __shared__ __align__(16) float ring[];  // [DEC_NS][128 rows][64 columns]
+  __shared__ float qs[128], ks[128], vs[128], os[128];
+  __shared__ __align__(16) float red[8][64];
+  __shared__ float red8[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int cg = tid & 7, rg = tid >> 3;
-  const int j0 = s * 32;
-  const int R = a.state_row0 + b;
+  const int cg = tid & 15, rg = tid >> 4;
+  const int H = a.h;
+  const int items = a.b * H;
   const int conv_dim = 2 * ca.hk * 128 + ca.hv * 128;
   const T* y = static_cast<const T*>(ca.y);
-  const long yrow = (long)b * ca.w;
-  cg::cluster_group cluster = cg::this_cluster();
-
-  // 1. issue the state loads first (the long-latency part), then the conv while they fly
-  float4* S4 = reinterpret_cast<float4*>(a.state + (((long)R * a.h + h) * 128) * 128);
-  float4 st[8];
-#pragma unroll
-  for (int r = 0; r < 8; r++) st[r] = S4[(rg * 8 + r) * 32 + s * 8 + cg];
-
-  auto conv_ch = [&](int ch, float* xin_new) {
-    const float* cs = ca.conv_state + ((long)R * 3) * conv_dim + ch;
-    const float x0 = cs[0], x1 = cs[(long)conv_dim], x2 = cs[2L * conv_dim];
-    const float x3 = to_f(y[yrow + ch]);
-    const float* w = ca.conv_w + (long)ch * 4;
-    *xin_new = x3;
-    return siluf_(w[0] * x0 + w[1] * x1 + w[2] * x2 + w[3] * x3);
+  // this CTA's items are blockIdx.x + j gridDim.x; its slices are numbered 2 j + half
+  const int my_items = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nslices = 2 * my_items;
+  auto state_of = [&](int j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    const int b = item / H, h = item % H;
+    return reinterpret_cast<float4*>(a.state + (((long)(a.state_row0 + b) * H + h) * 128) * 128);
   };
-  // q and k channel `tid` of head h (hk == hv); v channels j0 .. j0 + 31 of head h
-  float qx, kx;
-  const float qv = conv_ch(h * 128 + tid, &qx);
-  const float kv = conv_ch(ca.hk * 128 + h * 128 + tid, &kx);
-  float vx = 0.f, vv = 0.f;
-  if (tid < 32) vv = conv_ch(2 * ca.hk * 128 + h * 128 + j0 + tid, &vx);
-  const float sq = block_sum(qv * qv, red32);
-  const float sk = block_sum(kv * kv, red32);
-  qs[tid] = qv * rsqrtf(sq + 1e-6f) * rsqrtf(128.f);
-  ks[tid] = kv * rsqrtf(sk + 1e-6f);
-  if (tid < 32) vs[tid] = vv;
-  const long gb = yrow + conv_dim + ca.hv * 128;
-  const float beta = sigmoidf_(to_f(y[gb + h]));
-  const float gdec = expf(-expf(ca.a_log[h]) * softplusf_(to_f(y[gb + ca.hv + h]) + ca.dt_bias[h]));
-  __syncthreads();
-
-  // 2. u = S^T k after the decay; then delta, S += k delta^T, o = S^T q
-  float u4[4] = {0, 0, 0, 0};
+  auto issue = [&](int g) {  // cp.async this thread's 8 float4 of slice g into its ring slot
+    if (g < nslices) {
+      const float4* src = state_of(g >> 1) + (g & 1) * 16 + cg;
+      float* dst = ring + (g % DEC_NS) * DEC_SLICE + cg * 4;
 #pragma unroll
-  for (int r = 0; r < 8; r++) {
-    const float kr = ks[rg * 8 + r];
-    st[r].x *= gdec; st[r].y *= gdec; st[r].z *= gdec; st[r].w *= gdec;
-    u4[0] = fmaf(st[r].x, kr, u4[0]); u4[1] = fmaf(st[r].y, kr, u4[1]);
-    u4[2] = fmaf(st[r].z, kr, u4[2]); u4[3] = fmaf(st[r].w, kr, u4[3]);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    u4[i] += __shfl_xor_sync(0xffffffffu, u4[i], 8);
-    u4[i] += __shfl_xor_sync(0xffffffffu, u4[i], 16);
-  }
-  if (lane < 8) {
-#pragma unroll
-    for (int i = 0; i < 4; i++) red[warp][0][cg * 4 + i] = u4[i];
-  }
-  __syncthreads();
-  float d4[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int c = cg * 4 + i;
-    const float u = red[0][0][c] + red[1][0][c] + red[2][0][c] + red[3][0][c];
-    d4[i] = beta * (vs[c] - u);
-  }
-  float o4[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int r = 0; r < 8; r++) {
-    const float kr = ks[rg * 8 + r], qr = qs[rg * 8 + r];
-    st[r].x = fmaf(kr, d4[0], st[r].x); st[r].y = fmaf(kr, d4[1], st[r].y);
-    st[r].z = fmaf(kr, d4[2], st[r].z); st[r].w = fmaf(kr, d4[3], st[r].w);
-    o4[0] = fmaf(st[r].x, qr, o4[0]); o4[1] = fmaf(st[r].y, qr, o4[1]);
-    o4[2] = fmaf(st[r].z, qr, o4[2]); o4[3] = fmaf(st[r].w, qr, o4[3]);
-  }
-#pragma unroll
-  for (int r = 0; r < 8; r++) S4[(rg * 8 + r) * 32 + s * 8 + cg] = st[r];
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    o4[i] += __shfl_xor_sync(0xffffffffu, o4[i], 8);
-    o4[i] += __shfl_xor_sync(0xffffffffu, o4[i], 16);
-  }
-  if (lane < 8) {
-#pragma unroll
-    for (int i = 0; i < 4; i++) red[warp][1][cg * 4 + i] = o4[i];
-  }
-  __syncthreads();
-  // 3. gated RMSNorm over the head's 128 outputs: this CTA's 32, summed over the cluster
-  float o = 0.f;
-  if (tid < 32) o = red[0][1][tid] + red[1][1][tid] + red[2][1][tid] + red[3][1][tid];
-  float ss = tid < 32 ? warp_sum(o * o) : 0.f;
-  if (tid == 0) part = ss;
-  cluster.sync();  // every CTA has read the old conv state of q / k and published its partial
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < DEC_CS; i++) tot += *cluster.map_shared_rank(&part, i);
-  if (tid < 32) {
-    const int j = j0 + tid;
-    const float rms = rsqrtf(tot / 128.f + a.eps);
-    const float z = to_f(static_cast<const T*>(a.z)[(long)b * a.z_stride + h * 128 + j]);
-    const float hs = a.head_scale ? a.head_scale[h] : 1.f;
-    static_cast<T*>(a.o)[(long)b * a.o_stride + h * 128 + j] = from_f<T>(o * rms * a.norm_w[j] * siluf_(z) * hs);
-    // shift the conv state of this CTA's v channels
-    float* cs = ca.conv_state + ((long)R * 3) * conv_dim + 2 * ca.hk * 128 + h * 128 + j;
-    const float x1 = cs[(long)conv_dim], x2 = cs[2L * conv_dim];
-    cs[0] = x1; cs[(long)conv_dim] = x2; cs[2L * conv_dim] = vx;
-  }
-  if (s == 0) {  // rank 0 shifts the q / k conv state of the head, after every rank has read it
-#pragma unroll
-    for (int which = 0; which < 2; which++) {
-      const int ch = which * ca.hk * 128 + h * 128 + tid;
-      float* cs = ca.conv_state + ((long)R * 3) * conv_dim + ch;
-      const float x1 = cs[(long)conv_dim], x2 = cs[2L * conv_dim];
-      cs[0] = x1; cs[(long)conv_dim] = x2; cs[2L * conv_dim] = which ? kx : qx;
+      for (int r = 0; r < 8; r++) cp_async16(dst + (rg * 8 + r) * 64, src + (rg * 8 + r) * 32);
     }
+    cp_commit();  // possibly empty: keeps one group per slice so the wait count stays fixed
+  };
+#pragma unroll
+  for (int g = 0; g < DEC_NS - 1; g++) issue(g);
+
+  for (int j = 0; j < my_items; j++) {
+    const int item = blockIdx.x + j * gridDim.x;
+    const int b = item / H, h = item % H;
+    const int R = a.state_row0 + b;
+    const long yrow = (long)b * ca.w;
+    // 1. conv + SiLU of the head's q (threads 0..127, also v) and k (128..255) channels, shifting their conv state
+    const int c = tid & 127;
+    float z = 0.f;
+    if (tid < 128) z = to_f(static_cast<const T*>(a.z)[(long)b * a.z_stride + h * 128 + c]);
+    auto conv_ch = [&](int ch) {
+      float* cs = ca.conv_state + ((long)R * 3) * conv_dim + ch;
+      const float x0 = cs[0], x1 = cs[(long)conv_dim], x2 = cs[2L * conv_dim];
+      const float x3 = to_f(y[yrow + ch]);
+      const float4 w = *reinterpret_cast<const float4*>(ca.conv_w + (long)ch * 4);
+      cs[0] = x1; cs[(long)conv_dim] = x2; cs[2L * conv_dim] = x3;
+      return siluf_(w.x * x0 + w.y * x1 + w.z * x2 + w.w * x3);
+    };
+    const float qk = conv_ch((tid < 128 ? 0 : ca.hk * 128) + h * 128 + c);
+    if (tid < 128) vs[c] = conv_ch(2 * ca.hk * 128 + h * 128 + c);
+    const float ssq = warp_sum(qk * qk);
+    if (lane == 0) red8[warp] = ssq;
+    const long gb = yrow + conv_dim + ca.hv * 128;
+    const float beta = sigmoidf_(to_f(y[gb + h]));
+    const float gdec = expf(-expf(ca.a_log[h]) * softplusf_(to_f(y[gb + ca.hv + h]) + ca.dt_bias[h]));
+    __syncthreads();
+    {
+      const int w0 = tid < 128 ? 0 : 4;
+      const float tot = red8[w0] + red8[w0 + 1] + red8[w0 + 2] + red8[w0 + 3];
+      if (tid < 128) qs[c] = qk * rsqrtf(tot + 1e-6f) * rsqrtf(128.f);
+      else ks[c] = qk * rsqrtf(tot + 1e-6f);
+    }
+    __syncthreads();
+
+    // 2. per 64-column slice: decay, u = S^T k, delta = beta (v - u), S += k delta^T, o = S^T q
+#pragma unroll 1
+    for (int half = 0; half < 2; half++) {
+      const int g = 2 * j + half;
+      issue(g + DEC_NS - 1);
+      cp_wait<DEC_NS - 1>();
+      const float* sl = ring + (g % DEC_NS) * DEC_SLICE + cg * 4;
+      float4 st[8];
+#pragma unroll
+      for (int r = 0; r < 8; r++) st[r] = *reinterpret_cast<const float4*>(sl + (rg * 8 + r) * 64);
+      float u4[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int r = 0; r < 8; r++) {
+        const float kr = ks[rg * 8 + r];
+        st[r].x *= gdec; st[r].y *= gdec; st[r].z *= gdec; st[r].w *= gdec;
+        u4[0] = fmaf(st[r].x, kr, u4[0]); u4[1] = fmaf(st[r].y, kr, u4[1]);
+        u4[2] = fmaf(st[r].z, kr, u4[2]); u4[3] = fmaf(st[r].w, kr, u4[3]);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; i++) u4[i] += __shfl_xor_sync(0xffffffffu, u4[i], 16);
+      if (lane < 16) *reinterpret_cast<float4*>(&red[warp][cg * 4]) = make_float4(u4[0], u4[1], u4[2], u4[3]);
+      __syncthreads();
+      float d4[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int col = cg * 4 + i;
+        float u = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) u += red[w][col];
+        d4[i] = beta * (vs[half * 64 + col] - u);
+      }
+      __syncthreads();  // red is reused below
+      float o4[4] = {0, 0, 0, 0};
+      float4* S4 = state_of(j) + half * 16 + cg;
+#pragma unroll
+      for (int r = 0; r < 8; r++) {
+        const float kr = ks[rg * 8 + r], qr = qs[rg * 8 + r];
+        st[r].x = fmaf(kr, d4[0], st[r].x); st[r].y = fmaf(kr, d4[1], st[r].y);
+        st[r].z = fmaf(kr, d4[2], st[r].z); st[r].w = fmaf(kr, d4[3], st[r].w);
+        o4[0] = fmaf(st[r].x, qr, o4[0]); o4[1] = fmaf(st[r].y, qr, o4[1]);
+        o4[2] = fmaf(st[r].z, qr, o4[2]); o4[3] = fmaf(st[r].w, qr, o4[3]);
+        S4[(rg * 8 + r) * 32] = st[r];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; i++) o4[i] += __shfl_xor_sync(0xffffffffu, o4[i], 16);
+      if (lane < 16) *reinterpret_cast<float4*>(&red[warp][cg * 4]) = make_float4(o4[0], o4[1], o4[2], o4[3]);
+      __syncthreads();
+      if (tid < 64) {
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) o += red[w][tid];
+        os[half * 64 + tid] = o;
+      }
+      __syncthreads();  // os complete; red free for the next slice
+    }
+
+    // 3. gated RMSNorm over the head's 128 outputs (warps 0..3)
+    if (tid < 128) {
+      const float o = os[c];
+      const float ss = warp_sum(o * o);
+      if (lane == 0) red8[warp] = ss;
+    }
+    __syncthreads();
+    if (tid < 128) {
+      const float tot = red8[0] + red8[1] + red8[2] + red8[3];
+      const float rms = rsqrtf(tot / 128.f + a.eps);
+      const float hs = a.head_scale ? a.head_scale[h] : 1.f;
+      static_cast<T*>(a.o)[(long)b * a.o_stride + h * 128 + c] = from_f<T>(os[c] * rms * a.norm_w[c] * siluf_(z) * hs);
+    }
+    __syncthreads();  // qs / ks / vs / os / red8 are rewritten by the next item
   }
-  cluster.sync();  // peers may still read this CTA's `part`
+  cp_wait<0>();
 }
 
 int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cudaStream_t st) {
@@ -361,8 +381,19 @@ int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cu
   if (a.t != 1 || ca.t != 1) return fail(DUO_EINVAL, "gdn_decode: one token per row");
   if (a.dk != 128 || a.dv != 128 || ca.ks != 4 || ca.hk != ca.hv || !a.norm_w)
     return fail(DUO_EINVAL, "gdn_decode: needs dk = dv = 128, ks = 4, hk == hv and the gated norm");
+  const int items = a.b * a.h;
+  const int slots = DEC_CPS * sm_count();
+  // as many CTAs as fit, trimmed so that the busiest CTA's item count is unchanged
+  const int per = cdiv(items, slots);
+  const int grid = cdiv(items, per);
   return with_act(dtype, [&](auto tag) -> int {
-    gdn_decode_kernel<decltype(tag)><<<dim3(DEC_CS, a.h, a.b), 128, 0, st>>>(ca, a);
+    using T = decltype(tag);
+    static bool attr_set = false;
+    if (!attr_set) {
+      DUO_CUDA_TRY(cudaFuncSetAttribute(gdn_decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM));
+      attr_set = true;
+    }
+    gdn_decode_kernel<T><<<grid, DEC_THREADS, DEC_SMEM, st>>>(ca, a);
     DUO_LAUNCH_CHECK("gdn_decode_kernel");
     return DUO_OK;
   });

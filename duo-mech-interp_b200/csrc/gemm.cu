@@ -137,15 +137,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < NC; c0 += 32) {
         float v[32];
-        tc::tmem_ld32(trow + c0, v);
+        if (EPI != EPI_SWIGLU) tc::tmem_ld32(trow + c0, v);
         if (EPI == EPI_SWIGLU) {
-          // columns [0, BN/2) are gate rows j0 .. and [BN/2, BN) the matching up rows
+          // the tile's columns come in 128-wide groups [64 gate rows | the matching 64 up rows]; output columns
+          // c0 .. c0 + 31 take gate column gc and up column gc + 64
+          const int gc = (c0 / 64) * 128 + (c0 % 64);
+          tc::tmem_ld32(trow + gc, v);
           float u[32];
-          tc::tmem_ld32(trow + BN / 2 + c0, u);
+          tc::tmem_ld32(trow + gc + 64, u);
 #pragma unroll
           for (int j = 0; j < 32; j++) {
-            const float gs = ep.colscale ? v[j] * ep.colscale[tile_n + c0 + j] : v[j];
-            const float us = ep.colscale ? u[j] * ep.colscale[tile_n + BN / 2 + c0 + j] : u[j];
+            const float gs = ep.colscale ? v[j] * ep.colscale[tile_n + gc + j] : v[j];
+            const float us = ep.colscale ? u[j] * ep.colscale[tile_n + gc + 64 + j] : u[j];
             v[j] = siluf_(gs) * us;
           }
         } else if (ep.colscale) {
@@ -313,9 +316,11 @@ static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, in
 template <bool F16>
 static int dispatch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int bn, bool lite, int ksplit, int m, int n,
                        int k, const GemmEpiArgs& ep, cudaStream_t st) {
-  if (ep.epi == EPI_SWIGLU)
+  if (ep.epi == EPI_SWIGLU) {
+    if (bn == 256) return run_tc<256, EPI_SWIGLU, F16, false>(ta, tb, m, n, k, 1, ep, st);
     return lite ? run_tc<128, EPI_SWIGLU, F16, true>(ta, tb, m, n, k, 1, ep, st)
                 : run_tc<128, EPI_SWIGLU, F16, false>(ta, tb, m, n, k, 1, ep, st);
+  }
   if (ep.epi == EPI_ADD_F32) {
     if (bn == 256) return run_tc<256, EPI_ADD_F32, F16, false>(ta, tb, m, n, k, 1, ep, st);
     if (bn == 128)
@@ -339,15 +344,11 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dty
   DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_tc: operands must be bf16 or f16");
   const int sms = sm_count();
   const long tiles_m = cdiv(m, TC_BM);
-  // the widest N tile that still gives every SM work; SwiGLU tiles are 128 wide (gate / up interleaved per 64)
-  int bn = 128;
-  if (ep.epi == EPI_SWIGLU) {
-    DUO_CHECK_ARG(n % 128 == 0, "gemm_tc: SwiGLU epilogue needs n a multiple of 128");
-  } else {
-    bn = 256;
-    if (tiles_m * cdiv(n, 256) < sms) bn = 128;
-    if (tiles_m * cdiv(n, 128) < sms) bn = 64;
-  }
+  // the widest N tile that still gives every SM work (SwiGLU: gate / up interleaved per 64 rows, tiles >= 128)
+  if (ep.epi == EPI_SWIGLU) DUO_CHECK_ARG(n % 128 == 0, "gemm_tc: SwiGLU epilogue needs n a multiple of 128");
+  int bn = 256;
+  if (tiles_m * cdiv(n, 256) < sms) bn = 128;
+  if (ep.epi != EPI_SWIGLU && tiles_m * cdiv(n, 128) < sms) bn = 64;
   const long tiles = tiles_m * cdiv(n, bn);
   const bool lite = bn <= 128 && tiles < 2L * sms;  // small grid: two CTAs per SM
   int ksplit = 1;
