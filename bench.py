@@ -160,8 +160,9 @@ def peaks():
 
 
 def algorithmic_work(cfg, rows, prompt, decode):
-    """Algorithmic FLOPs / bytes of each (phase, kernel class) of one step on one rank (rows = rows of this rank).
-    See DESIGN.md for the per-unit figures."""
+    """Algorithmic FLOPs / bytes of each (phase, kernel class) of one step on one rank (rows = rows of this rank):
+    the per-unit figure of each class (per token, per row-layer, per chunk-head, per cached key) times the units of
+    the step, as the comments below state; param_bytes counts one byte per int8 weight, i.e. the parameter count."""
     from duo.weights import param_bytes
     H, V = cfg.hidden_size, cfg.vocab_size
     n_lin = sum(1 for l in range(cfg.num_hidden_layers) if not cfg.is_full(l))

@@ -1,4 +1,4 @@
-// Gated GQA attention, prefill (t > 1) of the bf16 engine on the tensor cores.
+// Gated GQA attention, prefill (t > 1) of the 16-bit (bf16 / f16) engine on the tensor cores.
 //
 // One CTA = (row, kv head, tile of 128 / rep queries); its 128 query rows are the rep q heads of that kv head over the
 // same query positions, so every K / V tile is loaded once for all of them.  8 warps x 16 rows; head dim 256.

@@ -312,6 +312,22 @@ int logits_impl(duo_engine* e, int row0, int n, float* out, cudaStream_t st) {
   return DUO_OK;
 }
 
+// Greedy tokens of rows row0 .. row0 + n - 1.  On the tensor-core engine the LM head runs with the argmax epilogue
+// (the same f32 values the logits would hold, lowest index on ties, no logits written); otherwise logits + argmax.
+int greedy_impl(duo_engine* e, int row0, int n, int32_t* out, cudaStream_t st) {
+  const duo_config& c = e->cfg;
+  if (e->act == DUO_F32 || n <= kGemvMax) {
+    DUO_TRY(logits_impl(e, row0, n, e->logits, st));
+    PROF_TRY(DUO_PROF_OTHER, launch_argmax(e->logits, n, c.vocab, out, st));
+    return DUO_OK;
+  }
+  const int H = c.hidden;
+  PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->last + (size_t)row0 * H, n, H, e->w.final_norm, c.eps, 1, e->xn_last, e->act, st));
+  PROF_TRY(DUO_PROF_GEMM, launch_lm_argmax(e->xn_last, n, H, e->p_embed.w, c.vocab, e->act, e->p_embed.colscale,
+                                           e->logits, out, st));
+  return DUO_OK;
+}
+
 int check_rows(duo_engine* e, int row_base, int rows, int T) {
   DUO_CHECK_ARG(rows >= 1 && T >= 1, "forward: rows and T must be >= 1");
   DUO_CHECK_ARG(row_base >= 0 && row_base + rows <= e->rows, "forward: rows out of range");
@@ -584,14 +600,12 @@ extern "C" int duo_engine_argmax(duo_engine* e, int row0, int n, int32_t* out, d
   DUO_TRY(check_engine(e, true, true));
   DUO_CHECK_ARG(out && n >= 1 && row0 >= 0 && row0 + n <= e->rows, "argmax: bad rows");
   cudaStream_t st = as_stream(stream);
-  DUO_TRY(logits_impl(e, row0, n, e->logits, st));
-  return launch_argmax(e->logits, n, e->cfg.vocab, out, st);
+  return greedy_impl(e, row0, n, out, st);
 }
 
 namespace {
 int generate_step(duo_engine* e, int vec_layer, int32_t* tokens_out, int n_steps, int step, cudaStream_t st) {
-  DUO_TRY(logits_impl(e, 0, e->rows, e->logits, st));
-  PROF_TRY(DUO_PROF_OTHER, launch_argmax(e->logits, e->rows, e->cfg.vocab, e->amax, st));
+  DUO_TRY(greedy_impl(e, 0, e->rows, e->amax, st));
   PROF_TRY(DUO_PROF_OTHER, launch_feed_tokens(e->amax, e->rows, e->ids, tokens_out, n_steps, step, st));
   return forward_impl(e, e->ids, 0, e->rows, 1, vec_layer, st);
 }

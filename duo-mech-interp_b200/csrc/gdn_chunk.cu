@@ -21,8 +21,8 @@ namespace duo {
 namespace {
 
 constexpr int CK = 64;         // chunk length
-constexpr int PD = 128 + 8;    // pitch (elements) of the 128-wide bf16 tiles
-constexpr int PC = 64 + 8;     // pitch of the 64-wide bf16 tiles
+constexpr int PD = 128 + 8;    // pitch (elements) of the 128-wide f16 tiles
+constexpr int PC = 64 + 8;     // pitch of the 64-wide f16 tiles
 constexpr int PF = 64 + 1;     // pitch of the f32 64 x 64 tiles
 
 struct ChunkSmem {
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
       }
       __syncthreads();
     }
-    // T1 = T diag(beta), T2 = T diag(beta e^G) in bf16
+    // T1 = T diag(beta), T2 = T diag(beta e^G) in f16
     for (int e = tid; e < CK * CK; e += 256) {
       const int i = e >> 6, j = e & 63;
       const float tv = sm.t[i * PF + j];
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
       }
     }
     __syncthreads();  // every warp is past its reads of sm.s; row sums are in
-    // write the new bf16 state copy for the next chunk
+    // write the new f16 state copy for the next chunk
     {
       const int r0 = warp * 16 + g;
 #pragma unroll

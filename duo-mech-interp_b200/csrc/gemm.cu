@@ -4,6 +4,8 @@
 //
 // The reference computes these products with `matvec` / `matmul` (engine/kernels.js:55-151) in f32 on int8 weights
 // dequantised per 128-group; model.js:382-396 picks between them by row count.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <mutex>
 
@@ -12,43 +14,34 @@
 
 namespace duo {
 
+namespace cg = cooperative_groups;
+
 __device__ unsigned g_tc_fault;
 
 // ---------------------------------------------------------------------------------------------------------------
-// epilogue helpers shared by both GEMMs
-
-__device__ __forceinline__ float push_apply(const PushTable& pt, int r, int n, float v) {
-  for (int i = 0; i < pt.count; i++) {
-    const int pn = pt.neuron[i];
-    if (pn == DUO_ALL_NEURONS || pn == n) {
-      const float val = pt.vals[(long)i * pt.rows + r];
-      v = pt.mode[i] == DUO_PUSH_MUL ? v * val : v + val;
-    }
-  }
-  return v;
-}
-
-// ---------------------------------------------------------------------------------------------------------------
-// tcgen05 GEMM.  CTA tile 128 x BN, K step 64 (one 128-byte swizzle row of bf16), STAGES-deep TMA ring.
-// Warp 0: TMA producer (one lane).  Warp 1: TMEM allocator and MMA issuer (one lane).  Warps 2-5: epilogue, one
-// accumulator row (TMEM lane) per thread, read 32 columns at a time.
+// tcgen05 GEMM for small grids (decode-sized M): one CTA per 128 x BN tile (x a K range), K step 64 (one 128-byte
+// swizzle row of 16-bit values), a ~96 KB TMA ring so that two CTAs share an SM.  Large grids go to the persistent
+// kernel (gemm_persist.cu).  Warp 0: TMA producer (one lane).  Warp 1: TMEM allocator and MMA issuer (one lane).
+// Warps 2-5: epilogue, one accumulator row (TMEM lane) per thread, read 32 columns at a time.
 
 constexpr int TC_BM = 128, TC_BK = 64, TC_THREADS = 192;
 
-// LITE: a ~96 KB ring so two CTAs share an SM (small grids, e.g. decode), else a ~192 KB ring (one CTA per SM)
-template <int BN, bool LITE> struct TcCfg {
+// the f32 epilogue tile reuses the pipeline buffers (idle once every MMA has completed)
+__device__ __forceinline__ float* stile_of(uint8_t* smem) { return reinterpret_cast<float*>(smem); }
+
+template <int BN> struct TcCfg {
   static constexpr int A_BYTES = TC_BM * TC_BK * 2;
   static constexpr int B_BYTES = BN * TC_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = ((LITE ? 96 : 192) * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (96 * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-template <int BN, int EPI, bool F16, bool LITE>
+template <int BN, int EPI, bool F16>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, int M, int N,
                    int K, int kper, GemmEpiArgs ep, unsigned* fault) {
-  using C = TcCfg<BN, LITE>;
+  using C = TcCfg<BN>;
   static_assert(C::STAGES >= 2, "ring too small");
   static_assert(TC_BM * ((EPI == EPI_SWIGLU ? BN / 2 : BN) + 4) * 4 <= C::STAGES * C::STAGE_BYTES,
                 "the epilogue tile must fit in the ring");
@@ -66,7 +59,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // split-K (residual-add epilogue only): this CTA reduces k blocks [kb0, kb0 + num_k)
   const int kb0 = blockIdx.z * kper;
   const int num_k = min(kper, K / TC_BK - kb0);
-  const bool split = gridDim.z > 1;
+  const bool split = gridDim.z > 1;  // launched as a cluster of gridDim.z CTAs along z (residual add only)
+  bool epi_ok = false;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; s++) {
@@ -124,10 +118,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // global load / store of the output (and the residual read-modify-write) is coalesced.
     constexpr int NC = (EPI == EPI_SWIGLU) ? BN / 2 : BN;  // output columns of this tile
     constexpr int P = NC + 4;                               // row pitch: rows start 4 banks apart
-    float* stile = reinterpret_cast<float*>(smem);
+    float* stile = stile_of(smem);
     const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31 belong to this warp
     const int row = quad * 32 + lane;
     const bool ok = tc::mbar_wait(tmem_full, 0);
+    epi_ok = ok;
     if (!ok) {
       if (lane == 0) atomicOr(fault, 4u);
     } else {
@@ -159,8 +154,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(srow + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
-    if (ok) {
+    if (!split) asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+    if (ok && !split) {
       const int ew = warp - 2;
       const int n0 = (EPI == EPI_SWIGLU) ? tile_n / 2 : tile_n;  // first output column of the tile
       const int ncols = (EPI == EPI_SWIGLU) ? N / 2 : N;          // output width
@@ -183,10 +178,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           if (EPI == EPI_ADD_F32) {
             float* X = static_cast<float*>(ep.c) + off;
-            const float* vr = (ep.vec && blockIdx.z == 0) ? ep.vec + (long)r * ep.ldc + n : nullptr;
-            if (split) {  // partial sums of a K split: accumulate atomically
-              for (int i = 0; i < 4 && n + i < ncols; i++) atomicAdd(X + i, x[i] + (vr ? vr[i] : 0.f));
-            } else if (vec4) {
+            const float* vr = ep.vec ? ep.vec + (long)r * ep.ldc + n : nullptr;
+            if (vec4) {
               float4 o = *reinterpret_cast<float4*>(X);
               o.x += x[0]; o.y += x[1]; o.z += x[2]; o.w += x[3];
               if (vr) {
@@ -227,6 +220,49 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
     }
+  }
+  if (split) {
+    // K split across the CTAs of this cluster (blockIdx.z = cluster rank): once every partial tile is in its CTA's
+    // shared memory, CTA z sums rows [z rpc, z rpc + rpc) of all of them over distributed shared memory, in rank
+    // order (deterministic), and does the residual read-modify-write for those rows.
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (warp >= 2 && epi_ok) {
+      constexpr int P = BN + 4;
+      const int ks = gridDim.z, z = blockIdx.z;
+      const int rpc = (TC_BM + ks - 1) / ks;
+      const int r_hi = min(TC_BM, (z + 1) * rpc);
+      const bool al = ((reinterpret_cast<uintptr_t>(ep.c) & 15) == 0) && (ep.ldc % 4 == 0) &&
+                      (ep.vec == nullptr || (reinterpret_cast<uintptr_t>(ep.vec) & 15) == 0);
+      for (int rr = z * rpc + (warp - 2); rr < r_hi; rr += 4) {
+        const int m = tile_m + rr;
+        if (m >= M) break;
+        const int r = ep.row_base + m / ep.t;
+        for (int c = lane * 4; c < BN; c += 128) {
+          const int n = tile_n + c;
+          if (n >= N) break;
+          float x[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int q = 0; q < ks; q++) {
+            const float4 v = *reinterpret_cast<const float4*>(cluster.map_shared_rank(stile_of(smem), q) + rr * P + c);
+            x[0] += v.x; x[1] += v.y; x[2] += v.z; x[3] += v.w;
+          }
+          float* X = static_cast<float*>(ep.c) + (long)m * ep.ldc + n;
+          const float* vr = ep.vec ? ep.vec + (long)r * ep.ldc + n : nullptr;
+          if (al && n + 4 <= N) {
+            float4 o = *reinterpret_cast<float4*>(X);
+            o.x += x[0]; o.y += x[1]; o.z += x[2]; o.w += x[3];
+            if (vr) {
+              const float4 a = *reinterpret_cast<const float4*>(vr);
+              o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
+            }
+            *reinterpret_cast<float4*>(X) = o;
+          } else {
+            for (int i = 0; i < 4 && n + i < N; i++) X[i] += x[i] + (vr ? vr[i] : 0.f);
+          }
+        }
+      }
+    }
+    cluster.sync();  // no CTA leaves while a peer may still read its tile
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -293,13 +329,13 @@ int tc_fault_read_clear(unsigned* out) {
   return DUO_OK;
 }
 
-template <int BN, int EPI, bool F16, bool LITE>
+template <int BN, int EPI, bool F16>
 static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, int k, int ksplit,
                   const GemmEpiArgs& ep, cudaStream_t st) {
-  using C = TcCfg<BN, LITE>;
+  using C = TcCfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, F16, LITE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    DUO_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       C::SMEM));
     attr_set = true;
   }
@@ -308,33 +344,38 @@ static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, in
   const int num_k = k / TC_BK;
   const int kper = cdiv(num_k, ksplit);
   dim3 grid(cdiv(n, BN), cdiv(m, TC_BM), cdiv(num_k, kper));
-  gemm_tc_kernel<BN, EPI, F16, LITE><<<grid, TC_THREADS, C::SMEM, st>>>(ta, tb, m, n, k, kper, ep, fault);
+  if (grid.z == 1) {
+    gemm_tc_kernel<BN, EPI, F16><<<grid, TC_THREADS, C::SMEM, st>>>(ta, tb, m, n, k, kper, ep, fault);
+  } else {
+    // K split: the grid.z CTAs of one output tile form a cluster and reduce their partial tiles on chip
+    DUO_CHECK_ARG(EPI == EPI_ADD_F32 && grid.z <= 8, "gemm_tc: K split only for the residual add, at most 8 ways");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = grid.z;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    DUO_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, F16>, ta, tb, m, n, k, kper, ep, fault));
+  }
   DUO_LAUNCH_CHECK("gemm_tc_kernel");
   return DUO_OK;
 }
 
 template <bool F16>
-static int dispatch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int bn, bool lite, int ksplit, int m, int n,
-                       int k, const GemmEpiArgs& ep, cudaStream_t st) {
-  if (ep.epi == EPI_SWIGLU) {
-    if (bn == 256) return run_tc<256, EPI_SWIGLU, F16, false>(ta, tb, m, n, k, 1, ep, st);
-    return lite ? run_tc<128, EPI_SWIGLU, F16, true>(ta, tb, m, n, k, 1, ep, st)
-                : run_tc<128, EPI_SWIGLU, F16, false>(ta, tb, m, n, k, 1, ep, st);
-  }
-  if (ep.epi == EPI_ADD_F32) {
-    if (bn == 256) return run_tc<256, EPI_ADD_F32, F16, false>(ta, tb, m, n, k, 1, ep, st);
-    if (bn == 128)
-      return lite ? run_tc<128, EPI_ADD_F32, F16, true>(ta, tb, m, n, k, ksplit, ep, st)
-                  : run_tc<128, EPI_ADD_F32, F16, false>(ta, tb, m, n, k, 1, ep, st);
-    return lite ? run_tc<64, EPI_ADD_F32, F16, true>(ta, tb, m, n, k, ksplit, ep, st)
-                : run_tc<64, EPI_ADD_F32, F16, false>(ta, tb, m, n, k, 1, ep, st);
-  }
-  if (bn == 256) return run_tc<256, EPI_STORE, F16, false>(ta, tb, m, n, k, 1, ep, st);
-  if (bn == 128)
-    return lite ? run_tc<128, EPI_STORE, F16, true>(ta, tb, m, n, k, 1, ep, st)
-                : run_tc<128, EPI_STORE, F16, false>(ta, tb, m, n, k, 1, ep, st);
-  return lite ? run_tc<64, EPI_STORE, F16, true>(ta, tb, m, n, k, 1, ep, st)
-              : run_tc<64, EPI_STORE, F16, false>(ta, tb, m, n, k, 1, ep, st);
+static int dispatch_tc(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int ksplit, int m, int n, int k,
+                       const GemmEpiArgs& ep, cudaStream_t st) {
+  if (ep.epi == EPI_SWIGLU) return run_tc<128, EPI_SWIGLU, F16>(ta, tb, m, n, k, 1, ep, st);
+  if (ep.epi == EPI_ADD_F32)
+    return bn == 128 ? run_tc<128, EPI_ADD_F32, F16>(ta, tb, m, n, k, ksplit, ep, st)
+                     : run_tc<64, EPI_ADD_F32, F16>(ta, tb, m, n, k, ksplit, ep, st);
+  return bn == 128 ? run_tc<128, EPI_STORE, F16>(ta, tb, m, n, k, 1, ep, st)
+                   : run_tc<64, EPI_STORE, F16>(ta, tb, m, n, k, 1, ep, st);
 }
 
 int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dtype, const GemmEpiArgs& ep,
@@ -350,17 +391,19 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dty
   if (tiles_m * cdiv(n, 256) < sms) bn = 128;
   if (ep.epi != EPI_SWIGLU && tiles_m * cdiv(n, 128) < sms) bn = 64;
   const long tiles = tiles_m * cdiv(n, bn);
-  const bool lite = bn <= 128 && tiles < 2L * sms;  // small grid: two CTAs per SM
-  int ksplit = 1;
-  if (ep.epi == EPI_ADD_F32 && lite) {  // still too few CTAs: split K, partial sums added atomically
-    const int num_k = k / TC_BK;
-    ksplit = (int)std::max<long>(1, std::min<long>({2L * sms / tiles, 8, num_k / 4}));
-  }
+  // small grid: per-tile kernel, two CTAs per SM; otherwise the persistent kernel
+  const bool small = bn == 64 || (bn == 128 && tiles < 2L * sms);
   CUtensorMap ta, tb;
   DUO_TRY(make_tmap_16(&ta, a, ab_dtype, m, k, k, TC_BM, TC_BK));
   DUO_TRY(make_tmap_16(&tb, b, ab_dtype, n, k, k, bn, TC_BK));
-  return ab_dtype == DUO_F16 ? dispatch_tc<true>(ta, tb, bn, lite, ksplit, m, n, k, ep, st)
-                             : dispatch_tc<false>(ta, tb, bn, lite, ksplit, m, n, k, ep, st);
+  if (!small) return launch_gemm_persist(ta, tb, bn, m, n, k, ab_dtype, ep, st);
+  int ksplit = 1;
+  if (ep.epi == EPI_ADD_F32) {  // still too few CTAs: split K over a cluster, partial tiles summed on chip
+    const int num_k = k / TC_BK;
+    ksplit = (int)std::max<long>(1, std::min<long>({2L * sms / tiles, 8, num_k / 4}));
+  }
+  return ab_dtype == DUO_F16 ? dispatch_tc<true>(ta, tb, bn, ksplit, m, n, k, ep, st)
+                             : dispatch_tc<false>(ta, tb, bn, ksplit, m, n, k, ep, st);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -447,6 +490,31 @@ extern "C" int duo_gemm_bf16(const void* a, int m, int k, const void* b, int n, 
   ep.ldc = ldc;
   ep.colscale = col_scale;
   return launch_gemm_tc(a, m, k, b, n, DUO_BF16, ep, as_stream(stream));
+}
+
+extern "C" int duo_gemm_swiglu(const void* a, int m, int k, const void* b, int inter, int ab_dtype,
+                               const float* col_scale, void* out, int ldo, const int32_t* push_neurons,
+                               const int32_t* push_modes, const float* push_vals, int push_count, int push_rows, int t,
+                               int row_base, duo_stream stream) {
+  DUO_CHECK_ARG(m >= 0 && inter >= 0 && k > 0 && t > 0 && row_base >= 0, "gemm_swiglu: bad shape");
+  DUO_CHECK_ARG(k % 64 == 0 && inter % 64 == 0, "gemm_swiglu: k and inter must be multiples of 64");
+  DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_swiglu: operands must be bf16 or f16");
+  DUO_CHECK_ARG(m == 0 || inter == 0 || (a && b && out), "gemm_swiglu: null pointer");
+  DUO_CHECK_ARG(ldo >= inter, "gemm_swiglu: ldo < inter");
+  DUO_CHECK_ARG(push_count >= 0 && (push_count == 0 || (push_neurons && push_modes && push_vals)),
+                "gemm_swiglu: null push table");
+  DUO_CHECK_ARG(push_count == 0 || row_base + (m > 0 ? (m - 1) / t : 0) < push_rows,
+                "gemm_swiglu: rows beyond the push table");
+  GemmEpiArgs ep;
+  ep.epi = EPI_SWIGLU;
+  ep.c = out;
+  ep.c_dtype = ab_dtype;
+  ep.ldc = ldo;
+  ep.colscale = col_scale;
+  ep.t = t;
+  ep.row_base = row_base;
+  ep.push = PushTable{push_neurons, push_modes, push_vals, push_count, push_rows};
+  return launch_gemm_tc(a, m, k, b, 2 * inter, ab_dtype, ep, as_stream(stream));
 }
 
 extern "C" int duo_fault_status(unsigned* out) {

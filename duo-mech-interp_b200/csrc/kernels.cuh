@@ -1,6 +1,8 @@
 // Host-side launchers shared between the kernel files and the engine.  All are stream-ordered and return a duo
 // status; none allocates memory.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace duo {
@@ -15,11 +17,25 @@ struct PushTable {
   int rows;
 };
 
+// Neuron pushes of the SwiGLU epilogue (the reference's push list, engine/model.js:8, 410-425): every entry whose neuron is n
+// (or DUO_ALL_NEURONS) adds its per-row value to, or multiplies it into, activation n of row r, in list order.
+__device__ __forceinline__ float push_apply(const PushTable& pt, int r, int n, float v) {
+  for (int i = 0; i < pt.count; i++) {
+    const int pn = pt.neuron[i];
+    if (pn == DUO_ALL_NEURONS || pn == n) {
+      const float val = pt.vals[(long)i * pt.rows + r];
+      v = pt.mode[i] == DUO_PUSH_MUL ? v * val : v + val;
+    }
+  }
+  return v;
+}
+
 // Epilogues of the tensor-core GEMM.
 enum GemmEpi {
   EPI_STORE = 0,   // C[m, n] = acc * colscale[n]                   (bf16 or f32 C)
   EPI_ADD_F32 = 1, // X[m, n] += acc * colscale[n] (+ vec[row(m), n])  (f32 residual stream)
-  EPI_SWIGLU = 2   // gate/up interleaved per 64 columns: A[m, j] = silu(g) * u, then pushes   (16-bit A)
+  EPI_SWIGLU = 2,  // gate/up interleaved per 64 columns: A[m, j] = silu(g) * u, then pushes   (16-bit A)
+  EPI_ARGMAX = 3   // per (row, 256-column tile): max of acc * colscale and its lowest column -> c / idx [m, ldc]
 };
 
 struct GemmEpiArgs {
@@ -31,7 +47,18 @@ struct GemmEpiArgs {
   const float* vec = nullptr;   // ADD: optional per-row vector table [rows_total, n]
   int t = 1, row_base = 0;      // row(m) = row_base + m / t
   PushTable push{};             // SWIGLU
+  int32_t* idx = nullptr;       // ARGMAX: column of each partial maximum (c holds the f32 maxima)
 };
+
+// persistent tcgen05 GEMM over prepared tensor maps (A box 128 x 64, B box bn x 64; bn = 256)
+int launch_gemm_persist(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int m, int n, int k, int ab_dtype,
+                        const GemmEpiArgs& ep, cudaStream_t st);
+
+// Greedy next tokens straight from the LM head: out[i] = argmax_n (A[i, :] . B[n, :]) * colscale[n] (lowest n on
+// ties; the values are those the f32 logits would hold), through the persistent GEMM's ARGMAX epilogue and a per-row
+// reduction of its partials.  scratch: m * ceil(n / 256) * 2 words.
+int launch_lm_argmax(const void* a, int m, int k, const void* b, int n, int ab_dtype, const float* colscale,
+                     float* scratch, int32_t* out, cudaStream_t st);
 
 int launch_gemv(const void* x, int x_dtype, int m, int k, const int8_t* q, const float* s, int group, int n, void* y,
                 int y_dtype, int accumulate, cudaStream_t st);

@@ -69,6 +69,34 @@ def gemm_bf16(a, b, col_scale=None, out=None, out_dtype=torch.bfloat16, accumula
     return out
 
 
+def interleave_gate_up(gate, up):
+    """[inter, k] gate and up weights -> the [2 inter, k] row order duo_gemm_swiglu reads (blocks of 64 rows:
+    64 gate rows, then the matching 64 up rows)."""
+    inter, k = gate.shape
+    if inter % 64:
+        raise ValueError("inter must be a multiple of 64")
+    return torch.stack([gate.reshape(inter // 64, 64, k), up.reshape(inter // 64, 64, k)], 1).reshape(2 * inter, k)
+
+
+def gemm_swiglu(a, gu, col_scale=None, pushes=None, t=1, row_base=0, stream=None):
+    """silu(gate) * up of (A . GU^T) * col_scale with the neuron pushes of one layer (kernels_qwen35.js:250-280).
+    gu is in interleave_gate_up order.  pushes = (neurons int32 [P], modes int32 [P], vals f32 [P, rows])."""
+    _dev(a, gu, col_scale)
+    m, k = a.shape
+    inter = gu.shape[0] // 2
+    out = torch.empty(m, inter, dtype=a.dtype, device=a.device)
+    if pushes is None:
+        pn = pm = pv = None
+        count = rows = 0
+    else:
+        pn, pm, pv = pushes
+        _dev(pn, pm, pv)
+        count, rows = pv.shape
+    call("duo_gemm_swiglu", ptr(a), m, k, ptr(gu), inter, dtype_code(a.dtype), ptr(col_scale), ptr(out), out.stride(0),
+         ptr(pn), ptr(pm), ptr(pv), count, rows, t, row_base, stream_ptr(stream))
+    return out
+
+
 def rmsnorm(x, w, eps=1e-6, offset=True, out_dtype=torch.float32, stream=None):
     """y = x * rsqrt(mean(x^2) + eps) * (1 + w) (engine/kernels.js:226-246)."""
     _dev(x, w)

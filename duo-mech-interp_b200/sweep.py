@@ -1,6 +1,6 @@
 """Op-level sweeps of the mixer kernels (BASELINE configs 2 and 3, and the projection GEMM) with CUDA-event timing.
 
-    python duo-mech-interp_b200/sweep.py gemm [--m M --n N --k K]
+    python duo-mech-interp_b200/sweep.py gemm [--m M --n N --k K] [--acc]
     python duo-mech-interp_b200/sweep.py gdn-decode [--b B --steps S]      # config 2b
     python duo-mech-interp_b200/sweep.py gdn-prefill [--b B --t T]         # config 2a
     python duo-mech-interp_b200/sweep.py attn-prefill [--b B --t T]        # config 3a
@@ -60,16 +60,21 @@ def report(case, shape, ms, flops=None, bytes_=None, extra=None):
     return line
 
 
-def gemm(m, n, k, iters=10, compare=True):
+def gemm(m, n, k, iters=10, compare=True, accumulate=False):
+    """bf16 C = A B^T, or (accumulate) the residual-add epilogue X += A B^T into an f32 X; cuBLAS beside it
+    (for the residual add: an f32-output matmul plus the add)."""
     g = torch.Generator(device="cuda").manual_seed(0)
     a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
     b = (torch.randn(n, k, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
-    c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
-    ms = timed(lambda: ops.gemm_bf16(a, b, out=c), iters)
-    extra = {}
+    c = torch.zeros(m, n, device="cuda", dtype=torch.float32 if accumulate else torch.bfloat16)
+    ms = timed(lambda: ops.gemm_bf16(a, b, out=c, accumulate=accumulate), iters)
+    extra = {"epilogue": "add_f32" if accumulate else "store_bf16"}
     if compare:
-        ms_ref = timed(lambda: torch.matmul(a, b.T, out=c), iters)
-        extra = {"cublas_ms": ms_ref, "cublas_tflops": 2.0 * m * n * k / ms_ref / 1e9}
+        if accumulate:
+            ms_ref = timed(lambda: c.add_(torch.matmul(a, b.T).float()), iters)
+        else:
+            ms_ref = timed(lambda: torch.matmul(a, b.T, out=c), iters)
+        extra.update({"cublas_ms": ms_ref, "cublas_tflops": 2.0 * m * n * k / ms_ref / 1e9})
     return report("gemm_bf16", [m, n, k], ms, flops=2.0 * m * n * k, extra=extra)
 
 
@@ -155,9 +160,10 @@ def main():
     ap.add_argument("--len", type=int, default=8192)
     ap.add_argument("--fn", default="gdn_chunk")
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--acc", action="store_true", help="gemm: residual-add epilogue into f32")
     a = ap.parse_args()
     if a.case == "gemm":
-        gemm(a.m, a.n, a.k, a.iters)
+        gemm(a.m, a.n, a.k, a.iters, accumulate=a.acc)
     elif a.case == "gdn-decode":
         gdn_decode(a.b or 1, a.steps)
     elif a.case == "gdn-prefill":

@@ -82,6 +82,17 @@ int duo_q8_gather(const int32_t* ids, int t, const int8_t* q, const float* s, in
 int duo_gemm_bf16(const void* a, int m, int k, const void* b, int n, const float* col_scale, void* c, int c_dtype,
                   int ldc, int accumulate, duo_stream stream);
 
+/* Fused MLP up-projection: gu = (A[m, k] . B[2 inter, k]^T) * col_scale, then out[i, j] = silu(gate_j) * up_j with the
+ * layer's neuron pushes applied in list order to row r = row_base + i / t (row i of A): entry p adds push_vals[p *
+ * push_rows + r] to neuron push_neurons[p] (DUO_PUSH_ADD) or multiplies it in (DUO_PUSH_MUL); neuron -1 is every
+ * neuron.  B holds gate and up rows interleaved in blocks of 64: B rows [128 b, 128 b + 64) are gate rows 64 b ..
+ * 64 b + 63 and B rows [128 b + 64, 128 b + 128) the matching up rows (col_scale in the same order, may be NULL).
+ * A and B are bf16 or f16 (ab_dtype); out has the same dtype, leading dim ldo.  k and inter multiples of 64.
+ * Replaces `_mm(xn, gu)` + `swiglu`, engine/model.js:448-457 and engine/kernels_qwen35.js:250-280. */
+int duo_gemm_swiglu(const void* a, int m, int k, const void* b, int inter, int ab_dtype, const float* col_scale,
+                    void* out, int ldo, const int32_t* push_neurons, const int32_t* push_modes, const float* push_vals,
+                    int push_count, int push_rows, int t, int row_base, duo_stream stream);
+
 /* y[m, :] = x[m, :] * rsqrt(mean(x^2) + eps) * (1 + w) (offset != 0) or * w.  x f32, y f32 / bf16.
  * Replaces `rmsnorm(offset)`, engine/kernels.js:226-246. */
 int duo_rmsnorm(const float* x, int m, int d, const float* w, float eps, int offset, void* y, int y_dtype,

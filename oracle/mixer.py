@@ -27,6 +27,19 @@ def rmsnorm(x, w, eps, offset=True):
     return xf * r * ((1.0 + w.float()) if offset else w.float())
 
 
+def swiglu_push(gu, inter, pushes, row_of):
+    """a = silu(gate) * up of the fused [M, 2 inter] gate|up projection, then the layer's neuron pushes in record
+    order ([WGSL] kernels_qwen35.js:250-280): (neuron or None = every neuron, "add" | "mul", per-row values), row i
+    of `gu` taking the value of row row_of[i]."""
+    a = F.silu(gu[:, :inter]) * gu[:, inter:]
+    for n, mode, vals in pushes:
+        v = torch.as_tensor(vals, dtype=a.dtype)[torch.as_tensor(row_of)]
+        cols = slice(None) if n is None else n
+        v = v[:, None] if n is None else v
+        a[:, cols] = a[:, cols] * v if mode == "mul" else a[:, cols] + v
+    return a
+
+
 def l2norm(x, eps=1e-6):
     """x * rsqrt(sum(x^2) + eps) over the last dim.  [HF] 228-231; [WGSL] kernels_qwen35.js:215-223."""
     return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)

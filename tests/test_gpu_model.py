@@ -154,6 +154,35 @@ def test_generate_matches_step_loop(tiny):
     assert torch.equal(toks.long(), torch.stack(ref_toks, 1))
 
 
+@pytest.mark.parametrize("act", ["f16", "bf16"])
+def test_greedy_from_lm_head_epilogue(tiny, act):
+    """More than 8 rows on the tensor-core engine: argmax_all and generate take the LM head's argmax epilogue (no
+    logits written).  Their tokens equal argmax of the engine's own logits (model.js argmaxAll, analysis.js:127-142),
+    lowest index on ties; only a top-2 gap within f32 rounding may differ between the two GEMM tilings."""
+    from duo import Model
+    types, packs = tiny
+    W, _ = packs[128]
+    rows, T, steps = 12, 9, 4
+    ids = torch.randint(0, TINY["vocab"], (rows, T), generator=torch.Generator().manual_seed(3))
+    cfg = duo_cfg_from_tiny(types, act)
+    m = Model(cfg, W).alloc(rows=rows, max_len=32, max_t=T, max_tokens=rows * T)
+    m.forward(ids.reshape(-1), 0, rows, T)
+    logits = m.logits_all().cpu()
+    fused = torch.tensor(m.argmax_all())
+    top2 = logits.topk(2, -1).values
+    near_tie = (top2[:, 0] - top2[:, 1]) <= 1e-6 * top2[:, 0].abs()
+    assert bool(((fused.long() == logits.argmax(-1)) | near_tie).all())
+    gen = m.generate(steps).cpu()
+    m2 = Model(cfg, W).alloc(rows=rows, max_len=32, max_t=T, max_tokens=rows * T)
+    m2.forward(ids.reshape(-1), 0, rows, T)
+    loop = []
+    for _ in range(steps):
+        nxt = m2.logits_all().argmax(-1)
+        loop.append(nxt.cpu())
+        m2.step(nxt.tolist())
+    assert torch.equal(gen.long(), torch.stack(loop, 1))
+
+
 def test_engine_errors(tiny):
     from duo import DuoError, Model
     types, packs = tiny

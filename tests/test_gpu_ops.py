@@ -83,8 +83,10 @@ def test_q8_gemv(ops, m, k, group):
 # tcgen05 GEMM vs a torch fp32 matmul of the same bf16 operands
 
 
+# small grids run the per-tile kernel (K split for the residual add); (4173, 1064, 1024) and (8269, 2088, 512) run the
+# persistent kernel with ragged edge tiles and one to four tiles per CTA
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (200, 300, 1024), (1024, 1024, 3584), (40, 7168, 1024),
-                                   (3000, 512, 2048)])
+                                   (3000, 512, 2048), (4173, 1064, 1024), (8269, 2088, 512)])
 def test_gemm_bf16(ops, m, n, k):
     a = (torch.randn(m, k, generator=_seed(m)) ).to(torch.bfloat16)
     b = (torch.randn(n, k, generator=_seed(n)) * 0.05).to(torch.bfloat16)
@@ -97,6 +99,33 @@ def test_gemm_bf16(ops, m, n, k):
     x0 = torch.randn(m, n, generator=_seed(2))
     acc = ops.gemm_bf16(a.cuda(), b.cuda(), col_scale=cs.cuda(), out=x0.clone().cuda(), accumulate=True)
     assert rel_max(acc, x0 + ref * cs) < 1e-5 * max(1.0, k / 1024)
+    assert ops.fault_status() == 0
+
+
+@pytest.mark.parametrize("m,inter,k,dt", [(37, 128, 256, torch.bfloat16), (100, 3584, 1024, torch.bfloat16),
+                                          (1000, 3584, 1024, torch.bfloat16), (1000, 3584, 1024, torch.float16)])
+def test_gemm_swiglu(ops, m, inter, k, dt):
+    """Fused gate|up GEMM + SwiGLU + neuron pushes (kernels_qwen35.js:250-280) against the oracle on the same 16-bit
+    operands; the 16-bit output rounding bounds the error (m = 1000 runs the persistent kernel)."""
+    a = torch.randn(m, k, generator=_seed(m)).to(dt)
+    wg = (torch.randn(inter, k, generator=_seed(inter)) * 0.05).to(dt)
+    wu = (torch.randn(inter, k, generator=_seed(inter + 1)) * 0.05).to(dt)
+    cs = torch.rand(2, inter, generator=_seed(3)) + 0.5
+    t, row_base, rows = (m + 2) // 3, 1, 4
+    row_of = row_base + torch.arange(m) // t
+    neurons = torch.tensor([5, -1, inter - 1], dtype=torch.int32)
+    modes = torch.tensor([0, 1, 0], dtype=torch.int32)
+    vals = torch.randn(3, rows, generator=_seed(4))
+    gu = ops.interleave_gate_up(wg, wu)
+    csi = ops.interleave_gate_up(cs[0][:, None], cs[1][:, None]).reshape(-1)
+    out = ops.gemm_swiglu(a.cuda(), gu.cuda(), col_scale=csi.cuda(),
+                          pushes=(neurons.cuda(), modes.cuda(), vals.cuda()), t=t, row_base=row_base)
+    g = (a.float() @ wg.float().T) * cs[0]
+    u = (a.float() @ wu.float().T) * cs[1]
+    plist = [(None if n < 0 else n, "mul" if md else "add", vals[i])
+             for i, (n, md) in enumerate(zip(neurons.tolist(), modes.tolist()))]
+    ref = mixer.swiglu_push(torch.cat([g, u], 1), inter, plist, row_of)
+    assert rel_max(out.float(), ref) < 1e-2
     assert ops.fault_status() == 0
 
 
