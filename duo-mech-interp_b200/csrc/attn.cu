@@ -16,6 +16,7 @@ namespace duo {
 
 template <typename T>
 __global__ void attn_prep_kernel(AttnPrepArgs a) {
+  pdl_enter();
   extern __shared__ float buf[];  // [hd]
   __shared__ float red[32];
   const int m = blockIdx.x, hh = blockIdx.y, i = threadIdx.x;
@@ -56,7 +57,7 @@ int launch_attn_prep(const AttnPrepArgs& a, int dtype, cudaStream_t st) {
   dim3 grid(m, a.nh + a.nkv);
   const size_t sm = a.hd * sizeof(float);
   return with_act(dtype, [&](auto tag) -> int {
-    attn_prep_kernel<decltype(tag)><<<grid, a.hd, sm, st>>>(a);
+    DUO_CUDA_TRY(::duo::launch_kernel(attn_prep_kernel<decltype(tag)>, grid, a.hd, sm, st, a));
     DUO_LAUNCH_CHECK("attn_prep_kernel");
     return DUO_OK;
   });
@@ -76,6 +77,7 @@ __device__ __forceinline__ int q_start(const AttnArgs& a, int b) {
 
 template <typename T>
 __global__ void __launch_bounds__(256) attn_prefill_kernel(AttnArgs a) {
+  pdl_enter();
   extern __shared__ float sm[];
   float* Qs = sm;                            // [BQ][HD + 1]
   float* Ks = Qs + AP_BQ * (AP_HD + 1);      // [BK][HD + 1]
@@ -189,6 +191,7 @@ __device__ __forceinline__ void ld8f(const T* p, float* o) { load8(p, o); }
 
 template <typename T>
 __global__ void __launch_bounds__(256) attn_decode_kernel(AttnArgs a, int nsplit, int split_len) {
+  pdl_enter();
   __shared__ float sm_m[AD_WARPS][AD_REP], sm_l[AD_WARPS][AD_REP];
   __shared__ float sm_o[AD_WARPS][AD_REP][AP_HD];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -268,6 +271,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnArgs a, int nsplit
 
 template <typename T>
 __global__ void attn_combine_kernel(AttnArgs a, int nsplit) {
+  pdl_enter();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const float* wp = a.work + ((long)b * a.nh + h) * nsplit * (AP_HD + 2);
   float M = -INFINITY;
@@ -309,7 +313,7 @@ long attn_decode_scratch_floats(int b, int nh, int nkv, int max_len, int dtype) 
 
 int launch_attn_combine(const AttnArgs& a, int dtype, int nsplit, cudaStream_t st) {
   return with_act(dtype, [&](auto tag) -> int {
-    attn_combine_kernel<decltype(tag)><<<dim3(a.nh, a.b), AP_HD, 0, st>>>(a, nsplit);
+    DUO_CUDA_TRY(::duo::launch_kernel(attn_combine_kernel<decltype(tag)>, dim3(a.nh, a.b), AP_HD, 0, st, a, nsplit));
     DUO_LAUNCH_CHECK("attn_combine_kernel");
     return DUO_OK;
   });
@@ -332,10 +336,10 @@ static int run_attention(const AttnArgs& a, cudaStream_t st) {
   if (a.t == 1) {
     int ns, sl;
     decode_plan(a, &ns, &sl);
-    attn_decode_kernel<T><<<dim3(ns, a.nkv, a.b), 256, 0, st>>>(a, ns, sl);
+    DUO_CUDA_TRY(::duo::launch_kernel(attn_decode_kernel<T>, dim3(ns, a.nkv, a.b), 256, 0, st, a, ns, sl));
     DUO_LAUNCH_CHECK("attn_decode_kernel");
     if (ns > 1) {
-      attn_combine_kernel<T><<<dim3(a.nh, a.b), AP_HD, 0, st>>>(a, ns);
+      DUO_CUDA_TRY(::duo::launch_kernel(attn_combine_kernel<T>, dim3(a.nh, a.b), AP_HD, 0, st, a, ns));
       DUO_LAUNCH_CHECK("attn_combine_kernel");
     }
     return DUO_OK;
@@ -346,7 +350,7 @@ static int run_attention(const AttnArgs& a, cudaStream_t st) {
     DUO_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr = true;
   }
-  attn_prefill_kernel<T><<<dim3(cdiv(a.t, AP_BQ), a.nh, a.b), 256, smem, st>>>(a);
+  DUO_CUDA_TRY(::duo::launch_kernel(attn_prefill_kernel<T>, dim3(cdiv(a.t, AP_BQ), a.nh, a.b), 256, smem, st, a));
   DUO_LAUNCH_CHECK("attn_prefill_kernel");
   return DUO_OK;
 }

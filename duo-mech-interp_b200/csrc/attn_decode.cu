@@ -24,6 +24,7 @@ constexpr int kDecodeSmem = (16 + 2 * DST * DBK) * DP * 2;
 
 template <int REP, typename T16>
 __global__ void __launch_bounds__(128, 1) attn_decode_mma_kernel(AttnArgs a, int nsplit, int split_len) {
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t smem[];
   T16* Qs = reinterpret_cast<T16*>(smem);
   T16* Ks = Qs + 16 * DP;
@@ -221,7 +222,7 @@ int launch_attn_decode_mma(const AttnArgs& a, int dtype, cudaStream_t st) {
                                         kDecodeSmem));
       attr = true;
     }
-    attn_decode_mma_kernel<RP, T16><<<dim3(ns, a.nkv, a.b), 128, kDecodeSmem, st>>>(a, ns, split_len);
+    DUO_CUDA_TRY(::duo::launch_kernel(attn_decode_mma_kernel<RP, T16>, dim3(ns, a.nkv, a.b), 128, kDecodeSmem, st, a, ns, split_len));
     DUO_LAUNCH_CHECK("attn_decode_mma_kernel");
     return DUO_OK;
   };

@@ -19,6 +19,7 @@ constexpr int HD = 256, PQ = HD + 8, BKEY = 64;
 
 template <int REP, typename T16>
 __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
+  pdl_enter();
   constexpr int QT = 128 / REP;  // query positions per CTA
   extern __shared__ __align__(16) uint8_t smem[];
   T16* Qs = reinterpret_cast<T16*>(smem);
@@ -188,7 +189,7 @@ static int run_prefill_mma(const AttnArgs& a, cudaStream_t st) {
     DUO_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_mma_kernel<REP, T16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  attn_prefill_mma_kernel<REP, T16><<<dim3(cdiv(a.t, 128 / REP), a.nkv, a.b), 256, smem, st>>>(a);
+  DUO_CUDA_TRY(::duo::launch_kernel(attn_prefill_mma_kernel<REP, T16>, dim3(cdiv(a.t, 128 / REP), a.nkv, a.b), 256, smem, st, a));
   DUO_LAUNCH_CHECK("attn_prefill_mma_kernel");
   return DUO_OK;
 }

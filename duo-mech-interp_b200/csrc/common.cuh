@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <string>
+#include <utility>
 
 #include "../../include/duo_mixer.h"
 
@@ -41,6 +42,35 @@ int fail(int code, const std::string& msg);
   } while (0)
 
 void count_launch();
+
+// ---------------------------------------------------------------------------------------------------------------
+// Programmatic dependent launch.  Kernels are launched with programmatic stream serialisation, so the CTAs of a kernel
+// may become resident while its predecessor in the stream is still running.  Every kernel calls pdl_wait()
+// (griddepcontrol.wait: returns once the preceding grid has completed and its writes are visible) before its first
+// access to memory that another kernel writes or reads, and only after that pdl_trigger()
+// (griddepcontrol.launch_dependents), which lets the successor's CTAs launch and run their prologue meanwhile.
+// Because no kernel triggers before its own wait, a kernel that starts early overlaps only its immediate predecessor:
+// every earlier kernel has completed.  A prologue may therefore read data that the immediate predecessor does not
+// write (the GEMMs prefetch constant weight tiles).  A grid launched without the attribute passes both at once.
+// DUO_PDL=0 in the environment launches without the attribute.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 
 #define DUO_TRY(expr)              \
   do {                             \
@@ -153,6 +183,14 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // wait until at most N of this thread's committed groups are still in flight
 template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// the common prologue: wait for the predecessor, then let the successor launch
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_trigger();
+}
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.f + expf(-x)); }

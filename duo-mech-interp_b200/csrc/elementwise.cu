@@ -13,6 +13,7 @@ namespace duo {
 template <typename TY>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, int d, const float* __restrict__ w,
                                                       float eps, int offset, TY* __restrict__ y) {
+  pdl_enter();
   __shared__ float red[32];
   const float* xr = x + (long)blockIdx.x * d;
   float ss = 0.f;
@@ -40,7 +41,7 @@ int launch_rmsnorm(const float* x, int m, int d, const float* w, float eps, int 
   const int threads = std::min(256, std::max(32, ((d / 8 + 31) / 32) * 32));
   return with_act(y_dtype, [&](auto yt) -> int {
     using TY = decltype(yt);
-    rmsnorm_kernel<TY><<<m, threads, 0, st>>>(x, d, w, eps, offset, static_cast<TY*>(y));
+    DUO_CUDA_TRY(::duo::launch_kernel(rmsnorm_kernel<TY>, m, threads, 0, st, x, d, w, eps, offset, static_cast<TY*>(y)));
     DUO_LAUNCH_CHECK("rmsnorm_kernel");
     return DUO_OK;
   });
@@ -53,6 +54,7 @@ int launch_rmsnorm(const float* x, int m, int d, const float* w, float eps, int 
 template <typename T>
 __global__ void __launch_bounds__(256) swiglu_push_kernel(const T* __restrict__ gu, int inter, int t, int row_base,
                                                           PushTable pt, T* __restrict__ a) {
+  pdl_enter();
   const int m = blockIdx.y;
   const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c0 >= inter) return;
@@ -81,7 +83,7 @@ int launch_swiglu_push(const void* gu, int m, int inter, int t, int row_base, co
   dim3 grid(cdiv(inter / 8, 256), m);
   return with_act(dtype, [&](auto tag) -> int {
     using T = decltype(tag);
-    swiglu_push_kernel<T><<<grid, 256, 0, st>>>(static_cast<const T*>(gu), inter, t, row_base, pt, static_cast<T*>(a));
+    DUO_CUDA_TRY(::duo::launch_kernel(swiglu_push_kernel<T>, grid, 256, 0, st, static_cast<const T*>(gu), inter, t, row_base, pt, static_cast<T*>(a)));
     DUO_LAUNCH_CHECK("swiglu_push_kernel");
     return DUO_OK;
   });
@@ -91,6 +93,7 @@ int launch_swiglu_push(const void* gu, int m, int inter, int t, int row_base, co
 // residual vector add (engine/kernels.js:190-203): x[m, :] += vec[row_base + m / t, :]
 
 __global__ void vec_add_kernel(float* __restrict__ x, int h, int t, int row_base, const float* __restrict__ vec) {
+  pdl_enter();
   const int m = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (c >= h) return;
@@ -104,7 +107,7 @@ __global__ void vec_add_kernel(float* __restrict__ x, int h, int t, int row_base
 
 int launch_vec_add(float* x, int m, int h, int t, int row_base, const float* vec, cudaStream_t st) {
   if (m == 0) return DUO_OK;
-  vec_add_kernel<<<dim3(cdiv(h / 4, 256), m), 256, 0, st>>>(x, h, t, row_base, vec);
+  DUO_CUDA_TRY(::duo::launch_kernel(vec_add_kernel, dim3(cdiv(h / 4, 256), m), 256, 0, st, x, h, t, row_base, vec));
   DUO_LAUNCH_CHECK("vec_add_kernel");
   return DUO_OK;
 }
@@ -113,6 +116,7 @@ int launch_vec_add(float* x, int m, int h, int t, int row_base, const float* vec
 // per-row argmax over the vocabulary (engine/kernels.js:261-284): ties go to the lower index
 
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int v, int32_t* __restrict__ out) {
+  pdl_enter();
   const float* row = logits + (long)blockIdx.x * v;
   float best = -INFINITY;
   int idx = 0x7fffffff;
@@ -147,7 +151,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
 
 int launch_argmax(const float* logits, int m, int v, int32_t* out, cudaStream_t st) {
   if (m == 0) return DUO_OK;
-  argmax_kernel<<<m, 1024, 0, st>>>(logits, v, out);
+  DUO_CUDA_TRY(::duo::launch_kernel(argmax_kernel, m, 1024, 0, st, logits, v, out));
   DUO_LAUNCH_CHECK("argmax_kernel");
   return DUO_OK;
 }
@@ -156,6 +160,7 @@ int launch_argmax(const float* logits, int m, int v, int32_t* out, cudaStream_t 
 // bookkeeping: last token of each row -> last[row], row lengths += t
 
 __global__ void copy_last_kernel(const float* __restrict__ x, int h, int t, int row_base, float* __restrict__ last) {
+  pdl_enter();
   const int r = blockIdx.x;
   const float* src = x + ((long)r * t + t - 1) * h;
   float* dst = last + (long)(row_base + r) * h;
@@ -164,6 +169,7 @@ __global__ void copy_last_kernel(const float* __restrict__ x, int h, int t, int 
 }
 
 __global__ void advance_len_kernel(int32_t* len, int row_base, int rows, int t) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < rows) len[row_base + i] += t;
 }
@@ -171,9 +177,9 @@ __global__ void advance_len_kernel(int32_t* len, int row_base, int rows, int t) 
 int launch_finish_rows(const float* x, int h, int t, int row_base, int rows, float* last, int32_t* len,
                        cudaStream_t st) {
   if (rows == 0) return DUO_OK;
-  copy_last_kernel<<<rows, 256, 0, st>>>(x, h, t, row_base, last);
+  DUO_CUDA_TRY(::duo::launch_kernel(copy_last_kernel, rows, 256, 0, st, x, h, t, row_base, last));
   DUO_LAUNCH_CHECK("copy_last_kernel");
-  advance_len_kernel<<<cdiv(rows, 256), 256, 0, st>>>(len, row_base, rows, t);
+  DUO_CUDA_TRY(::duo::launch_kernel(advance_len_kernel, cdiv(rows, 256), 256, 0, st, len, row_base, rows, t));
   DUO_LAUNCH_CHECK("advance_len_kernel");
   return DUO_OK;
 }
@@ -181,6 +187,7 @@ int launch_finish_rows(const float* x, int h, int t, int row_base, int rows, flo
 // ids for the next decode step from the argmax of the previous one, and the token log
 __global__ void feed_tokens_kernel(const int32_t* __restrict__ am, int rows, int32_t* __restrict__ ids,
                                    int32_t* __restrict__ log, int n_steps, int step) {
+  pdl_enter();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   const int tok = am[r];
@@ -190,7 +197,7 @@ __global__ void feed_tokens_kernel(const int32_t* __restrict__ am, int rows, int
 
 int launch_feed_tokens(const int32_t* am, int rows, int32_t* ids, int32_t* log, int n_steps, int step,
                        cudaStream_t st) {
-  feed_tokens_kernel<<<cdiv(rows, 128), 128, 0, st>>>(am, rows, ids, log, n_steps, step);
+  DUO_CUDA_TRY(::duo::launch_kernel(feed_tokens_kernel, cdiv(rows, 128), 128, 0, st, am, rows, ids, log, n_steps, step));
   DUO_LAUNCH_CHECK("feed_tokens_kernel");
   return DUO_OK;
 }

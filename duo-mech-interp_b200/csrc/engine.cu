@@ -162,6 +162,7 @@ int project(duo_engine* e, const void* xin, int m, int k, const duo_q8_view& wq,
   if (e->act == DUO_F32) return launch_gemm_f32_q8(static_cast<const float*>(xin), m, k, wq.q, wq.s, grp, n, ep, st);
   GemmEpiArgs ep2 = ep;
   ep2.colscale = pk.colscale;
+  ep2.b_const = true;  // packed once at creation, before any forward
   return launch_gemm_tc(xin, m, k, pk.w, n, e->act, ep2, st);
 }
 
@@ -324,7 +325,7 @@ int greedy_impl(duo_engine* e, int row0, int n, int32_t* out, cudaStream_t st) {
   const int H = c.hidden;
   PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->last + (size_t)row0 * H, n, H, e->w.final_norm, c.eps, 1, e->xn_last, e->act, st));
   PROF_TRY(DUO_PROF_GEMM, launch_lm_argmax(e->xn_last, n, H, e->p_embed.w, c.vocab, e->act, e->p_embed.colscale,
-                                           e->logits, out, st));
+                                           true, e->logits, out, st));
   return DUO_OK;
 }
 

@@ -21,6 +21,7 @@ constexpr int CONV_TT = 32, CONV_KS = 4;
 
 template <typename T>
 __global__ void __launch_bounds__(128) gdn_conv_kernel(GdnConvArgs a) {
+  pdl_enter();
   __shared__ float tile[CONV_TT][128 + 4];
   const int cgp = blockIdx.x, rr = blockIdx.y, t0 = blockIdx.z * CONV_TT;
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
@@ -97,7 +98,7 @@ int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
   dim3 grid(conv_dim / 128, a.rows, cdiv(a.t, CONV_TT));
   return with_act(dtype, [&](auto tag) -> int {
-    gdn_conv_kernel<decltype(tag)><<<grid, 128, 0, st>>>(a);
+    DUO_CUDA_TRY(::duo::launch_kernel(gdn_conv_kernel<decltype(tag)>, grid, 128, 0, st, a));
     DUO_LAUNCH_CHECK("gdn_conv_kernel");
     return DUO_OK;
   });
@@ -113,6 +114,7 @@ int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
 
 template <typename T, int CS, bool NORM>
 __global__ void __cluster_dims__(CS, 1, 1) __launch_bounds__(128) gdn_recurrent_kernel(GdnScanArgs a) {
+  pdl_enter();
   constexpr int CW = 128 / CS;   // columns per CTA
   constexpr int RPT = 128 / CS;  // state rows per thread (CS threads share a column)
   __shared__ float qs[128], ks[128];
@@ -203,8 +205,8 @@ template <typename T, bool NORM>
 static int run_recurrent(const GdnScanArgs& a, cudaStream_t st) {
   const long pairs = (long)a.b * a.h;
   // 8 column slices while the (row, head) pairs alone cannot fill the GPU, else 4 (32 state rows per thread)
-  if (pairs <= 64) gdn_recurrent_kernel<T, 8, NORM><<<dim3(8, a.h, a.b), 128, 0, st>>>(a);
-  else gdn_recurrent_kernel<T, 4, NORM><<<dim3(4, a.h, a.b), 128, 0, st>>>(a);
+  if (pairs <= 64) DUO_CUDA_TRY(::duo::launch_kernel(gdn_recurrent_kernel<T, 8, NORM>, dim3(8, a.h, a.b), 128, 0, st, a));
+  else DUO_CUDA_TRY(::duo::launch_kernel(gdn_recurrent_kernel<T, 4, NORM>, dim3(4, a.h, a.b), 128, 0, st, a));
   DUO_LAUNCH_CHECK("gdn_recurrent_kernel");
   return DUO_OK;
 }
@@ -268,6 +270,9 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnCon
   };
 #pragma unroll
   for (int g = 0; g < DEC_NS - 1; g++) issue(g);
+  // Programmatic launch: the first state slices stream in while the preceding kernel (the layer's in-projection,
+  // which never touches the recurrent state) finishes; the conv inputs, conv state and outputs wait for it.
+  pdl_enter();
 
   for (int j = 0; j < my_items; j++) {
     const int item = blockIdx.x + j * gridDim.x;
@@ -393,7 +398,7 @@ int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cu
       DUO_CUDA_TRY(cudaFuncSetAttribute(gdn_decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM));
       attr_set = true;
     }
-    gdn_decode_kernel<T><<<grid, DEC_THREADS, DEC_SMEM, st>>>(ca, a);
+    DUO_CUDA_TRY(::duo::launch_kernel(gdn_decode_kernel<T>, grid, DEC_THREADS, DEC_SMEM, st, ca, a));
     DUO_LAUNCH_CHECK("gdn_decode_kernel");
     return DUO_OK;
   });

@@ -69,6 +69,7 @@ __device__ __forceinline__ void st4h(__half* p, const float* v) {
 
 template <typename TI, bool NORM>
 __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnScanArgs a) {
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   ChunkSmem& sm = *reinterpret_cast<ChunkSmem*>(smem_raw);
   const int h = blockIdx.x, b = blockIdx.y;
@@ -403,7 +404,7 @@ static int run_chunk(const GdnScanArgs& a, cudaStream_t st) {
     DUO_CUDA_TRY(cudaFuncSetAttribute(gdn_chunk_kernel<TI, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  gdn_chunk_kernel<TI, NORM><<<dim3(a.h, a.b), 256, smem, st>>>(a);
+  DUO_CUDA_TRY(::duo::launch_kernel(gdn_chunk_kernel<TI, NORM>, dim3(a.h, a.b), 256, smem, st, a));
   DUO_LAUNCH_CHECK("gdn_chunk_kernel");
   return DUO_OK;
 }

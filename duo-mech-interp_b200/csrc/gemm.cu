@@ -78,10 +78,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
+  // Programmatic launch: constant weight tiles of the first stages stream in while the preceding kernel finishes;
+  // everything else waits for it.
+  const int pre = ep.b_const ? min(num_k, C::STAGES) : 0;
+  if (warp == 0 && lane == 0) {
+    for (int kb = 0; kb < pre; kb++) {
+      tc::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+      tc::tma_load_2d(sb + kb * C::B_BYTES, &tma_b, (kb0 + kb) * TC_BK, tile_n, &full[kb]);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+
   if (warp == 0 && lane == 0) {
     for (int kb = 0; kb < num_k; kb++) {
       const int s = kb % C::STAGES;
       const uint32_t ph = (kb / C::STAGES) & 1;
+      if (kb < pre) {  // its B tile is already on the way
+        tc::tma_load_2d(sa + s * C::A_BYTES, &tma_a, (kb0 + kb) * TC_BK, tile_m, &full[s]);
+        continue;
+      }
       if (kb >= C::STAGES && !tc::mbar_wait(&empty[s], ph ^ 1)) {
         atomicOr(fault, 1u);
         break;
@@ -345,7 +361,7 @@ static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, in
   const int kper = cdiv(num_k, ksplit);
   dim3 grid(cdiv(n, BN), cdiv(m, TC_BM), cdiv(num_k, kper));
   if (grid.z == 1) {
-    gemm_tc_kernel<BN, EPI, F16><<<grid, TC_THREADS, C::SMEM, st>>>(ta, tb, m, n, k, kper, ep, fault);
+    DUO_CUDA_TRY(::duo::launch_kernel(gemm_tc_kernel<BN, EPI, F16>, grid, TC_THREADS, C::SMEM, st, ta, tb, m, n, k, kper, ep, fault));
   } else {
     // K split: the grid.z CTAs of one output tile form a cluster and reduce their partial tiles on chip
     DUO_CHECK_ARG(EPI == EPI_ADD_F32 && grid.z <= 8, "gemm_tc: K split only for the residual add, at most 8 ways");
@@ -354,13 +370,15 @@ static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, in
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = grid.z;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     DUO_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, F16>, ta, tb, m, n, k, kper, ep, fault));
   }
   DUO_LAUNCH_CHECK("gemm_tc_kernel");
@@ -413,6 +431,7 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dty
 __global__ void __launch_bounds__(256) gemm_f32_q8_kernel(const float* __restrict__ A, int M, int K,
                                                            const int8_t* __restrict__ W, const float* __restrict__ S,
                                                            int group, int N, GemmEpiArgs ep) {
+  pdl_enter();
   __shared__ float As[32][64 + 4];
   __shared__ float Ws[32][64 + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -466,7 +485,7 @@ int launch_gemm_f32_q8(const float* a, int m, int k, const int8_t* q, const floa
   if (m == 0 || n == 0) return DUO_OK;
   DUO_CHECK_ARG(k % 32 == 0, "gemm_f32: k must be a multiple of 32");
   DUO_CHECK_ARG(ep.epi == EPI_STORE || ep.epi == EPI_ADD_F32, "gemm_f32: store or add epilogue only");
-  gemm_f32_q8_kernel<<<dim3(cdiv(n, 64), cdiv(m, 64)), 256, 0, st>>>(a, m, k, q, s, group, n, ep);
+  DUO_CUDA_TRY(::duo::launch_kernel(gemm_f32_q8_kernel, dim3(cdiv(n, 64), cdiv(m, 64)), 256, 0, st, a, m, k, q, s, group, n, ep));
   DUO_LAUNCH_CHECK("gemm_f32_q8_kernel");
   return DUO_OK;
 }

@@ -109,6 +109,20 @@ __global__ void __launch_bounds__(PTHREADS, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
+  // Programmatic launch: constant weight tiles of the first tile's first stages stream in while the preceding kernel
+  // finishes; everything else waits for it.
+  const int pre = ep.b_const ? min(num_k, C::STAGES) : 0;
+  if (warp == 0 && lane == 0 && pre > 0) {
+    int tile_m, tile_n;
+    tile_mn(blockIdx.x, tile_m, tile_n);
+    for (int kb = 0; kb < pre; kb++) {
+      tc::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+      tc::tma_load_2d(sb + kb * C::B_BYTES, &tma_b, kb * PBK, tile_n, &full[kb]);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+
   if (warp == 0) {
     if (lane == 0) {
       long fill = 0;
@@ -118,6 +132,10 @@ __global__ void __launch_bounds__(PTHREADS, 1)
         for (int kb = 0; kb < num_k; kb++, fill++) {
           const int s = (int)(fill % C::STAGES);
           const uint32_t ph = (uint32_t)((fill / C::STAGES) & 1);
+          if (fill < pre) {  // its B tile is already on the way
+            tc::tma_load_2d(sa + s * C::A_BYTES, &tma_a, kb * PBK, tile_m, &full[s]);
+            continue;
+          }
           if (fill >= C::STAGES && !pwait(&empty[s], ph ^ 1, abort)) {
             atomicOr(fault, 1u);
             break;
@@ -362,7 +380,8 @@ int run_persist(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, int 
   const long tiles = (long)cdiv(n, BN) * cdiv(m, PBM);
   const int grid = (int)std::min<long>(tiles, sm_count());
   const int m_fast = (long)m > (long)n ? 0 : 1;  // same element size: A is the larger operand iff m > n
-  gemm_persist_kernel<BN, EPI, F16><<<grid, PTHREADS, C::SMEM, st>>>(ta, tb, m, n, k, m_fast, ep, fault);
+  DUO_CUDA_TRY(::duo::launch_kernel(gemm_persist_kernel<BN, EPI, F16>, grid, PTHREADS, C::SMEM, st, ta, tb, m, n, k,
+                                    m_fast, ep, fault));
   DUO_LAUNCH_CHECK("gemm_persist_kernel");
   return DUO_OK;
 }
@@ -380,6 +399,7 @@ int dispatch_persist(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n,
 __global__ void __launch_bounds__(256) argmax_partials_kernel(const float* __restrict__ pv,
                                                               const int32_t* __restrict__ pi, int m, int parts,
                                                               int32_t* __restrict__ out) {
+  pdl_enter();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= m) return;
   float best = -INFINITY;
@@ -401,7 +421,7 @@ __global__ void __launch_bounds__(256) argmax_partials_kernel(const float* __res
 }  // namespace
 
 int launch_lm_argmax(const void* a, int m, int k, const void* b, int n, int ab_dtype, const float* colscale,
-                     float* scratch, int32_t* out, cudaStream_t st) {
+                     bool b_const, float* scratch, int32_t* out, cudaStream_t st) {
   if (m == 0) return DUO_OK;
   DUO_CHECK_ARG(k % PBK == 0 && n > 0, "lm_argmax: k must be a multiple of 64");
   DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "lm_argmax: operands must be bf16 or f16");
@@ -416,8 +436,9 @@ int launch_lm_argmax(const void* a, int m, int k, const void* b, int n, int ab_d
   ep.ldc = parts;
   ep.colscale = colscale;
   ep.idx = reinterpret_cast<int32_t*>(scratch + (long)m * parts);
+  ep.b_const = b_const;
   DUO_TRY(launch_gemm_persist(ta, tb, 256, m, n, k, ab_dtype, ep, st));
-  argmax_partials_kernel<<<cdiv(m, 8), 256, 0, st>>>(scratch, ep.idx, m, parts, out);
+  DUO_CUDA_TRY(::duo::launch_kernel(argmax_partials_kernel, cdiv(m, 8), 256, 0, st, scratch, ep.idx, m, parts, out));
   DUO_LAUNCH_CHECK("argmax_partials_kernel");
   return DUO_OK;
 }

@@ -48,6 +48,8 @@ struct GemmEpiArgs {
   int t = 1, row_base = 0;      // row(m) = row_base + m / t
   PushTable push{};             // SWIGLU
   int32_t* idx = nullptr;       // ARGMAX: column of each partial maximum (c holds the f32 maxima)
+  bool b_const = false;         // B is not written by the kernel launched just before (weight packs): its first
+                                // tiles may be fetched before the programmatic-launch wait
 };
 
 // persistent tcgen05 GEMM over prepared tensor maps (A box 128 x 64, B box bn x 64; bn = 256)
@@ -58,7 +60,7 @@ int launch_gemm_persist(const CUtensorMap& ta, const CUtensorMap& tb, int bn, in
 // ties; the values are those the f32 logits would hold), through the persistent GEMM's ARGMAX epilogue and a per-row
 // reduction of its partials.  scratch: m * ceil(n / 256) * 2 words.
 int launch_lm_argmax(const void* a, int m, int k, const void* b, int n, int ab_dtype, const float* colscale,
-                     float* scratch, int32_t* out, cudaStream_t st);
+                     bool b_const, float* scratch, int32_t* out, cudaStream_t st);
 
 int launch_gemv(const void* x, int x_dtype, int m, int k, const int8_t* q, const float* s, int group, int n, void* y,
                 int y_dtype, int accumulate, cudaStream_t st);

@@ -22,6 +22,7 @@ template <> __device__ __forceinline__ float ld_src<__half>(const __half* p, lon
 template <typename T>
 __global__ void __launch_bounds__(128) q8_quantize_kernel(const T* __restrict__ w, long groups, int group,
                                                           int8_t* __restrict__ q, float* __restrict__ s) {
+  pdl_enter();
   __shared__ float red[32];
   for (long g = blockIdx.x; g < groups; g += gridDim.x) {
     const long base = g * (long)group;
@@ -47,6 +48,7 @@ __global__ void __launch_bounds__(128) q8_quantize_kernel(const T* __restrict__ 
 template <typename TO>
 __global__ void q8_dequant_kernel(const int8_t* __restrict__ q, const float* __restrict__ s, long total16, int k,
                                   int group, TO* __restrict__ out) {
+  pdl_enter();
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total16; i += (long)gridDim.x * blockDim.x) {
     const long e = i * 16;
     const long row = e / k;
@@ -70,6 +72,7 @@ __global__ void q8_dequant_kernel(const int8_t* __restrict__ q, const float* __r
 
 __global__ void q8_gather_kernel(const int32_t* __restrict__ ids, const int8_t* __restrict__ q,
                                  const float* __restrict__ s, int k, int group, int vocab, float* __restrict__ y) {
+  pdl_enter();
   const int t = blockIdx.x;
   const int id = ids[t];
   float* yr = y + (long)t * k;
@@ -112,6 +115,7 @@ template <int M, typename TX, typename TY>
 __global__ void __launch_bounds__(128) q8_gemv_kernel(const TX* __restrict__ x, int k, const int8_t* __restrict__ q,
                                                       const float* __restrict__ s, int group, int n,
                                                       TY* __restrict__ y, int accumulate) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= n) return;
@@ -160,7 +164,7 @@ int launch_gemv_t(const void* x, int m, int k, const int8_t* q, const float* s, 
   TY* yp = static_cast<TY*>(y);
   switch (m) {
 #define DUO_GEMV_CASE(MM) \
-  case MM: q8_gemv_kernel<MM, TX, TY><<<grid, block, 0, st>>>(xp, k, q, s, group, n, yp, accumulate); break;
+  case MM: DUO_CUDA_TRY(::duo::launch_kernel(q8_gemv_kernel<MM, TX, TY>, grid, block, 0, st, xp, k, q, s, group, n, yp, accumulate)); break;
     DUO_GEMV_CASE(1) DUO_GEMV_CASE(2) DUO_GEMV_CASE(3) DUO_GEMV_CASE(4)
     DUO_GEMV_CASE(5) DUO_GEMV_CASE(6) DUO_GEMV_CASE(7) DUO_GEMV_CASE(8)
 #undef DUO_GEMV_CASE
@@ -182,7 +186,7 @@ int launch_gemv(const void* x, int x_dtype, int m, int k, const int8_t* q, const
 int launch_gather(const int32_t* ids, int t, const int8_t* q, const float* s, int group, int k, int vocab, float* y,
                   cudaStream_t st) {
   if (t == 0) return DUO_OK;
-  q8_gather_kernel<<<t, 128, 0, st>>>(ids, q, s, k, group, vocab, y);
+  DUO_CUDA_TRY(::duo::launch_kernel(q8_gather_kernel, t, 128, 0, st, ids, q, s, k, group, vocab, y));
   DUO_LAUNCH_CHECK("q8_gather_kernel");
   return DUO_OK;
 }
@@ -194,7 +198,7 @@ int launch_dequant(const int8_t* q, const float* s, int n, int k, int group, voi
   const int grid = (int)std::min<long>((total16 + 255) / 256, (long)sm_count() * 16);
   return with_act(out_dtype, [&](auto ot) -> int {
     using TO = decltype(ot);
-    q8_dequant_kernel<TO><<<grid, 256, 0, st>>>(q, s, total16, k, group, static_cast<TO*>(out));
+    DUO_CUDA_TRY(::duo::launch_kernel(q8_dequant_kernel<TO>, grid, 256, 0, st, q, s, total16, k, group, static_cast<TO*>(out)));
     DUO_LAUNCH_CHECK("q8_dequant_kernel");
     return DUO_OK;
   });
@@ -214,6 +218,7 @@ template <typename TO>
 __global__ void q8_pack16_kernel(const int8_t* __restrict__ q, const float* __restrict__ s, int k, int group,
                                     int interleave, int apply_scale, TO* __restrict__ out,
                                     float* __restrict__ colscale) {
+  pdl_enter();
   const int n = blockIdx.x;
   const int dn = pack_dst_row(n, interleave);
   const int8_t* qr = q + (long)n * k;
@@ -239,11 +244,11 @@ int launch_pack16(const int8_t* q, const float* s, int n, int k, int group, int 
   if (interleave > 0 && (interleave % 64 || n != 2 * interleave))
     return fail(DUO_EINVAL, "pack: interleave needs n = 2 * interleave, a multiple of 64");
   if (out_dtype == DUO_F16)
-    q8_pack16_kernel<__half><<<n, 128, 0, st>>>(q, s, k, group, interleave, apply_scale, static_cast<__half*>(out),
-                                                colscale_out);
+    DUO_CUDA_TRY(::duo::launch_kernel(q8_pack16_kernel<__half>, n, 128, 0, st, q, s, k, group, interleave, apply_scale, static_cast<__half*>(out),
+                                                colscale_out));
   else
-    q8_pack16_kernel<__nv_bfloat16><<<n, 128, 0, st>>>(q, s, k, group, interleave, apply_scale,
-                                                       static_cast<__nv_bfloat16*>(out), colscale_out);
+    DUO_CUDA_TRY(::duo::launch_kernel(q8_pack16_kernel<__nv_bfloat16>, n, 128, 0, st, q, s, k, group, interleave, apply_scale,
+                                                       static_cast<__nv_bfloat16*>(out), colscale_out));
   DUO_LAUNCH_CHECK("q8_pack16_kernel");
   return DUO_OK;
 }
@@ -268,11 +273,11 @@ extern "C" int duo_q8_quantize(const void* w, int w_dtype, int n, int k, int gro
   const int grid = (int)std::min<long>(groups, (long)sm_count() * 32);
   cudaStream_t st = as_stream(stream);
   if (w_dtype == DUO_F32)
-    q8_quantize_kernel<float><<<grid, 128, 0, st>>>(static_cast<const float*>(w), groups, group, q, s);
+    DUO_CUDA_TRY(::duo::launch_kernel(q8_quantize_kernel<float>, grid, 128, 0, st, static_cast<const float*>(w), groups, group, q, s));
   else if (w_dtype == DUO_BF16)
-    q8_quantize_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(w), groups, group, q, s);
+    DUO_CUDA_TRY(::duo::launch_kernel(q8_quantize_kernel<__nv_bfloat16>, grid, 128, 0, st, static_cast<const __nv_bfloat16*>(w), groups, group, q, s));
   else if (w_dtype == DUO_F16)
-    q8_quantize_kernel<__half><<<grid, 128, 0, st>>>(static_cast<const __half*>(w), groups, group, q, s);
+    DUO_CUDA_TRY(::duo::launch_kernel(q8_quantize_kernel<__half>, grid, 128, 0, st, static_cast<const __half*>(w), groups, group, q, s));
   else
     return fail(DUO_EINVAL, "q8_quantize: w_dtype must be f32, bf16 or f16");
   DUO_LAUNCH_CHECK("q8_quantize_kernel");

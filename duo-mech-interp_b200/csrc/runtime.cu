@@ -1,4 +1,5 @@
 // Error plumbing and device queries shared by every C entry point.
+#include <cstdlib>
 #include <atomic>
 #include <cstring>
 #include <mutex>
@@ -19,6 +20,14 @@ int fail(int code, const std::string& msg) {
 static std::atomic<unsigned long long> g_launches{0};
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("DUO_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int sm_count() {
   static int cached = 0;
