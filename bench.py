@@ -46,6 +46,10 @@ def parse():
 # the reference's CPU path (transformers Qwen3_5ForCausalLM, fp32), timed on a bounded sample
 
 
+# the bounded CPU sample: 8 prompts x 1024 ids + 16 greedy steps (about 15 s of work on 16 host cores)
+CPU_SAMPLE = (8, 1024, 16)
+
+
 def cpu_reference_sample(rows=2, prompt=256, decode=8, seed=0):
     """tok/s of the reference's PyTorch forward on the host cores for `rows` prompts of `prompt` ids plus `decode`
     greedy steps (the same per-token work as the GPU workload, on a slice of it)."""
@@ -77,7 +81,7 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    rows, prompt, decode = 4, 512, 16
+    rows, prompt, decode = CPU_SAMPLE
     for _ in range(a.warmup):
         pass  # each sample builds its own cache; the model build below is the warm-up
     vals = []
@@ -150,6 +154,19 @@ class Clocks:
 
 # ---------------------------------------------------------------------------------------------------------------
 # our engine
+
+
+def measured_traffic(kernel, rows, prompt):
+    """DRAM bytes (read + write) per launch of a (phase:class) kernel from the committed ncu summary
+    profiles/traffic.json, when it was measured on this rank's rows and prompt length; None otherwise."""
+    try:
+        t = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+    except (OSError, ValueError):
+        return None
+    e = t.get("kernels", {}).get(kernel)
+    if not e or e.get("rows") != rows or e.get("prompt", prompt) != prompt:
+        return None
+    return e["bytes_per_launch"]
 
 
 def peaks():
@@ -280,7 +297,9 @@ def main():
             serve()
     torch.cuda.synchronize()
     work = algorithmic_work(cfg, rows, a.prompt, a.decode)
-    dominant = max(((ph, k) for ph in phase_prof for k in phase_prof[ph]), key=lambda pk_: phase_prof[pk_[0]][pk_[1]][0])
+    # the class with the most device time among those with a defined algorithmic work
+    dominant = max(((ph, k) for ph in phase_prof for k in phase_prof[ph] if (ph, k) in work),
+                   key=lambda pk_: phase_prof[pk_[0]][pk_[1]][0])
 
     # timed region: K steps between barrier + synchronize; the dominant class is timed per launch with events
     clocks = Clocks(local)
@@ -341,6 +360,8 @@ def main():
         peak = pk.get("hbm_gbs")
         unit = "GB/s"
 
+    traffic = measured_traffic(f"{dominant[0]}:{dominant[1]}", rows, a.prompt)
+
     # end to end through the public API with host buffers (ids from pinned host memory, tokens back to the host)
     e2e = None
     if not a.no_e2e:
@@ -365,9 +386,10 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        v, dt, cores = cpu_reference_sample(4, 512, 16, a.seed)
+        v, dt, cores = cpu_reference_sample(*CPU_SAMPLE, a.seed)
         cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
-               "sample": f"4 prompts x 512 ids + 16 greedy steps, transformers fp32 on {cpu_desc()} ({dt:.1f} s)"}
+               "sample": f"{CPU_SAMPLE[0]} prompts x {CPU_SAMPLE[1]} ids + {CPU_SAMPLE[2]} greedy steps, transformers fp32 "
+                         f"on {cpu_desc()} ({dt:.1f} s)"}
 
     if rank == 0:
         line = {
@@ -382,7 +404,7 @@ def main():
                        "l2": "inputs larger than L2 (state, KV cache and weights far exceed 126 MB)",
                        "prefill_rows_per_call": group_rows},
             "roofline": {"kernel": f"{dominant[0]}:{dominant[1]}", "bound": bound, "achieved": achieved,
-                         "peak": peak, "unit": unit, "frac": achieved / peak if peak else None, "traffic": None,
+                         "peak": peak, "unit": unit, "frac": achieved / peak if peak else None, "traffic": traffic,
                          "peak_source": pk_src, "launches": dom_n, "avg_launch_ms": dom_ms / max(dom_n, 1)},
             "breakdown_ms": {ph: {k: round(v[0], 3) for k, v in d.items()} for ph, d in phase_prof.items()},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk,
