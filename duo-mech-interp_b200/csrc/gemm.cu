@@ -401,6 +401,9 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dty
   if (m == 0 || n == 0) return DUO_OK;
   DUO_CHECK_ARG(k % TC_BK == 0, "gemm_tc: k must be a multiple of 64");
   DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_tc: operands must be bf16 or f16");
+  // decode-sized row counts: the weights-on-M kernel for wide outputs (one K split of its 128-row weight blocks covers
+  // the SMs); the residual adds (narrow N, long K) stay on the per-tile kernel below, whose K split reduces less data
+  if (m <= 256 && ep.epi != EPI_ARGMAX && ep.epi != EPI_ADD_F32) return launch_gemm_dec(a, m, k, b, n, ab_dtype, ep, st);
   const int sms = sm_count();
   const long tiles_m = cdiv(m, TC_BM);
   // the widest N tile that still gives every SM work (SwiGLU: gate / up interleaved per 64 rows, tiles >= 128)

@@ -52,6 +52,10 @@ struct GemmEpiArgs {
                                 // tiles may be fetched before the programmatic-launch wait
 };
 
+// decode-sized tcgen05 GEMM (m <= 256 rows; weights on the MMA's M side, K split over a cluster): y = x . w^T
+int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dtype, const GemmEpiArgs& ep,
+                    cudaStream_t st);
+
 // persistent tcgen05 GEMM over prepared tensor maps (A box 128 x 64, B box bn x 64; bn = 256)
 int launch_gemm_persist(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int m, int n, int k, int ab_dtype,
                         const GemmEpiArgs& ep, cudaStream_t st);
