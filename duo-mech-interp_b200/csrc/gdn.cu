@@ -12,78 +12,150 @@ namespace cg = cooperative_groups;
 namespace duo {
 
 // ---------------------------------------------------------------------------------------------------------------
-// conv prologue.  Block = (128-channel group = one q, k or v head, row, 32-token tile).  Thread c owns channel c of
-// the group: causal depthwise conv (KS = 4) over its inputs with the row's carried state, SiLU, into shared memory;
-// then one warp per token l2-normalises q / k heads (eps 1e-6).  v-head blocks also compute beta and g for their
-// tokens.  The block of tile 0 is the only reader of the old conv state and writes the new one after reading it.
+// conv prologue.  Block = (128-channel group = one q, k or v head, row, 64-token tile), 256 threads.  The tile's inputs
+// (tokens t0 - 3 .. t0 + 63; before the call's first token they come from the row's carried f32 state) are staged in
+// shared memory as f32 with 16-byte loads.  Half-warp h of the block handles tokens h, h + 16, h + 32, h + 48; its
+// thread c owns channels 4c .. 4c + 3 and 64 + 4c .. 64 + 4c + 3 (conflict-free float4 reads): causal depthwise conv
+// (KS = 4) + SiLU, the head's l2norm (eps 1e-6) for q / k by half-warp shuffles, two 8-byte stores.  v-head blocks
+// also compute beta and g for their tokens.  The block of tile 0 is the only reader of the old conv state and writes
+// the new one after reading it.
 
-constexpr int CONV_TT = 32, CONV_KS = 4;
+constexpr int CONV_TT = 64, CONV_KS = 4, CONV_ROWS = CONV_TT + CONV_KS - 1, CONV_P = 128 + 4;
 
 template <typename T>
-__global__ void __launch_bounds__(128) gdn_conv_kernel(GdnConvArgs a) {
+__device__ __forceinline__ void load8(const T* p, float* o);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float* o) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* o) {  // 8 x 16-bit
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; i++) o[i] = to_f(h[i]);
+}
+__device__ __forceinline__ uint32_t pack2(__nv_bfloat16*, float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(__half*, float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <typename T>
+__device__ __forceinline__ void store4(T* p, const float* v) {  // p 8-byte (16-bit T) / 16-byte (f32) aligned
+  if constexpr (sizeof(T) == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack2(p, v[0], v[1]), pack2(p, v[2], v[3]));
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) gdn_conv_kernel(GdnConvArgs a) {
   pdl_enter();
-  __shared__ float tile[CONV_TT][128 + 4];
+  __shared__ __align__(16) float xs[CONV_ROWS][CONV_P];
   const int cgp = blockIdx.x, rr = blockIdx.y, t0 = blockIdx.z * CONV_TT;
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
-  const int c = threadIdx.x;
-  const int ch = cgp * 128 + c;
+  const int tid = threadIdx.x;
   const int R = a.row_base + rr;
   const long m0 = (long)rr * a.t;
   const T* y = static_cast<const T*>(a.y);
   const int tn = min(CONV_TT, a.t - t0);
+  const float* st = a.conv_state + ((long)R * (CONV_KS - 1)) * conv_dim + cgp * 128;  // st[j * conv_dim + c]
 
-  float w[CONV_KS];
+  // 1. stage rows r = 0 .. tn + 2 (token t0 - 3 + r), 16 threads x 8 channels per row (16-byte loads when the
+  // projection rows allow it)
+  const bool vec = a.w % 8 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+  constexpr int NIT = (CONV_ROWS * 16 + 255) / 256;  // staging iterations per thread (5)
+  const int nq = (tn + CONV_KS - 1) * 16;
+  float v[NIT][8];
 #pragma unroll
-  for (int i = 0; i < CONV_KS; i++) w[i] = a.conv_w[(long)ch * CONV_KS + i];
-  float* st = a.conv_state + ((long)R * (CONV_KS - 1)) * conv_dim + ch;  // st[j * conv_dim], j = 0 oldest
-  // inputs at tokens t0-3 .. t0-1
-  float win[CONV_KS - 1];
-#pragma unroll
-  for (int i = 0; i < CONV_KS - 1; i++) {
-    const int tt = t0 - (CONV_KS - 1) + i;
-    win[i] = tt >= 0 ? to_f(y[(m0 + tt) * a.w + ch]) : st[(long)((CONV_KS - 1) + tt) * conv_dim];
+  for (int it = 0; it < NIT; it++) {  // every load is issued before any shared-memory store
+    const int q = tid + 256 * it;
+    if (q >= nq) continue;
+    const int r = q >> 4, c8 = (q & 15) * 8;
+    const int tt = t0 - (CONV_KS - 1) + r;
+    if (tt < 0) {
+      load8<float>(st + (long)((CONV_KS - 1) + tt) * conv_dim + c8, v[it]);
+    } else {
+      const T* src = y + (m0 + tt) * a.w + cgp * 128 + c8;
+      if (vec) load8<T>(src, v[it]);
+      else for (int i = 0; i < 8; i++) v[it][i] = to_f(src[i]);
+    }
   }
-  if (blockIdx.z == 0) {
-    // new state = last KS-1 inputs of (old state ++ this call's inputs)
-    float ns[CONV_KS - 1];
+#pragma unroll
+  for (int it = 0; it < NIT; it++) {
+    const int q = tid + 256 * it;
+    if (q >= nq) continue;
+    const int r = q >> 4, c8 = (q & 15) * 8;
+    *reinterpret_cast<float4*>(&xs[r][c8]) = make_float4(v[it][0], v[it][1], v[it][2], v[it][3]);
+    *reinterpret_cast<float4*>(&xs[r][c8 + 4]) = make_float4(v[it][4], v[it][5], v[it][6], v[it][7]);
+  }
+  // the new conv state = the last KS-1 inputs of (old state ++ this call's inputs); only tile 0 reads the old state
+  float ns[CONV_KS - 1];
+  const int sc = tid & 127;
+  if (blockIdx.z == 0 && tid < 128) {
 #pragma unroll
     for (int j = 0; j < CONV_KS - 1; j++) {
       const int idx = a.t + j;  // index into old ++ new
-      ns[j] = idx < CONV_KS - 1 ? win[idx] : to_f(y[(m0 + idx - (CONV_KS - 1)) * a.w + ch]);
+      ns[j] = idx < CONV_KS - 1 ? st[(long)idx * conv_dim + sc]
+                                : to_f(y[(m0 + idx - (CONV_KS - 1)) * a.w + cgp * 128 + sc]);
     }
-#pragma unroll
-    for (int j = 0; j < CONV_KS - 1; j++) st[(long)j * conv_dim] = ns[j];
-  }
-  for (int i = 0; i < tn; i++) {
-    const float x = to_f(y[(m0 + t0 + i) * a.w + ch]);
-    const float acc = w[0] * win[0] + w[1] * win[1] + w[2] * win[2] + w[3] * x;
-    tile[i][c] = siluf_(acc);
-    win[0] = win[1];
-    win[1] = win[2];
-    win[2] = x;
   }
   __syncthreads();
-  const bool norm = cgp < 2 * a.hk;  // q and k heads are l2-normalised; v heads pass through
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  T* out = static_cast<T*>(a.qkv_out);
-  for (int i = warp; i < tn; i += 4) {
-    float v[4];
+  if (blockIdx.z == 0 && tid < 128) {
+    float* stw = a.conv_state + ((long)R * (CONV_KS - 1)) * conv_dim + cgp * 128 + sc;
 #pragma unroll
-    for (int j = 0; j < 4; j++) v[j] = tile[i][lane * 4 + j];
+    for (int j = 0; j < CONV_KS - 1; j++) stw[(long)j * conv_dim] = ns[j];
+  }
+
+  // 2. conv + SiLU (+ l2norm) per token, half-warp per token
+  const int c = tid & 15, hw = tid >> 4;
+  const bool norm = cgp < 2 * a.hk;  // q and k heads are l2-normalised; v heads pass through
+  float w[8][CONV_KS];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int ch = cgp * 128 + (j < 4 ? 4 * c + j : 64 + 4 * c + j - 4);
+    const float4 ww = *reinterpret_cast<const float4*>(a.conv_w + (long)ch * CONV_KS);
+    w[j][0] = ww.x; w[j][1] = ww.y; w[j][2] = ww.z; w[j][3] = ww.w;
+  }
+  T* out = static_cast<T*>(a.qkv_out);
+  for (int i = hw; i < tn; i += 16) {
+    float v[8];
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+      const int col = half * 64 + 4 * c;
+      float4 x[CONV_KS];
+#pragma unroll
+      for (int d = 0; d < CONV_KS; d++) x[d] = *reinterpret_cast<const float4*>(&xs[i + d][col]);
+      const float xv[CONV_KS][4] = {{x[0].x, x[0].y, x[0].z, x[0].w}, {x[1].x, x[1].y, x[1].z, x[1].w},
+                                    {x[2].x, x[2].y, x[2].z, x[2].w}, {x[3].x, x[3].y, x[3].z, x[3].w}};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float* wj = w[half * 4 + j];
+        v[half * 4 + j] = siluf_(wj[0] * xv[0][j] + wj[1] * xv[1][j] + wj[2] * xv[2][j] + wj[3] * xv[3][j]);
+      }
+    }
     if (norm) {
-      float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-      ss = warp_sum(ss);
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) ss += v[j] * v[j];
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float inv = rsqrtf(ss + 1e-6f);
 #pragma unroll
-      for (int j = 0; j < 4; j++) v[j] *= inv;
+      for (int j = 0; j < 8; j++) v[j] *= inv;
     }
-    T* o = out + (m0 + t0 + i) * conv_dim + cgp * 128 + lane * 4;
-#pragma unroll
-    for (int j = 0; j < 4; j++) o[j] = from_f<T>(v[j]);
+    T* o = out + (m0 + t0 + i) * conv_dim + cgp * 128;
+    store4<T>(o + 4 * c, v);
+    store4<T>(o + 64 + 4 * c, v + 4);
   }
-  if (!norm && c < tn) {
+  if (!norm && tid < tn) {
     const int h = cgp - 2 * a.hk;
-    const long m = m0 + t0 + c;
+    const long m = m0 + t0 + tid;
     const long base = m * a.w + conv_dim + a.hv * a.dv;
     const float b = to_f(y[base + h]);
     const float av = to_f(y[base + a.hv + h]);
@@ -98,7 +170,7 @@ int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
   dim3 grid(conv_dim / 128, a.rows, cdiv(a.t, CONV_TT));
   return with_act(dtype, [&](auto tag) -> int {
-    DUO_CUDA_TRY(::duo::launch_kernel(gdn_conv_kernel<decltype(tag)>, grid, 128, 0, st, a));
+    DUO_CUDA_TRY(::duo::launch_kernel(gdn_conv_kernel<decltype(tag)>, grid, 256, 0, st, a));
     DUO_LAUNCH_CHECK("gdn_conv_kernel");
     return DUO_OK;
   });

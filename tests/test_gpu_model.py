@@ -140,6 +140,23 @@ def test_chunked_prefill_and_row_lengths(tiny, act):
     assert rel_max(m.logits_row(1).cpu(), om.logits([1])[0]) < tol
 
 
+@pytest.mark.parametrize("act", ["f32", "f16", "bf16"])
+def test_long_prefill(tiny, act):
+    """One 150-token forward per row (several conv tiles and scan chunks, ragged last ones) and a second 37-token
+    forward that continues from the carried state, against the oracle (model.js:404-466)."""
+    from duo import Model
+    types, packs = tiny
+    W, Wd = packs[128]
+    ids = torch.randint(0, TINY["vocab"], (2, 187), generator=torch.Generator().manual_seed(11))
+    m = Model(duo_cfg_from_tiny(types, act), W).alloc(rows=2, max_len=200, max_t=150, max_tokens=300)
+    om = OracleModel(oracle_cfg(types), Wd, rows=2, max_len=200)
+    tol = {"f32": 1e-4, "f16": 2e-2, "bf16": BF16_TOL}[act]
+    for a, b in ((0, 150), (150, 187)):
+        m.forward(ids[:, a:b].reshape(-1), 0, 2, b - a)
+        om.forward(ids[:, a:b].reshape(-1), 0, 2, b - a)
+        assert rel_max(m.logits_all().cpu(), om.logits()) < tol, (a, b)
+
+
 def test_generate_matches_step_loop(tiny):
     from duo import Model
     types, packs = tiny
