@@ -72,6 +72,8 @@ struct duo_engine {
   float* vec = nullptr;
   float* attn_work = nullptr;
   long attn_work_floats_n = 0;
+  void* chunk_ws = nullptr;  // chunked DeltaNet scan workspace (16-bit engines)
+  long chunk_ws_bytes = 0;
   std::vector<int> len;
   std::vector<LayerState> ls;
   std::vector<void*> state_owned;
@@ -221,6 +223,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       sa.z = static_cast<const char*>(e->y) + (size_t)e->conv_dim * es;
       sa.z_stride = wproj;
       sa.norm_w = L.gnorm; sa.head_scale = S.head_scale; sa.eps = c.eps;
+      sa.chunk_ws = e->chunk_ws; sa.chunk_ws_bytes = e->chunk_ws_bytes;
       if (T == 1 && c.hk == c.hv) {
         // decode: one fused kernel from the projection to the gated norm
         PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_decode(ca, sa, act, st));
@@ -453,6 +456,14 @@ extern "C" int duo_engine_alloc(duo_engine* e, int rows, int max_len, int max_to
   DUO_TRY(A(&p, (size_t)rows * c.hidden * 4)); e->vec = (float*)p;
   e->attn_work_floats_n = attn_work_floats(rows, c.nh, max_len);
   DUO_TRY(A(&p, e->attn_work_floats_n * 4)); e->attn_work = (float*)p;
+  // chunk workspace: a forward of r rows x T tokens (r T <= max_tokens, r <= rows) has r ceil(T / 64) <=
+  // (max_tokens + 63 rows) / 64 chunks per head
+  e->chunk_ws_bytes = 0;
+  e->chunk_ws = nullptr;
+  if (e->act != DUO_F32 && c.layers > 0) {
+    e->chunk_ws_bytes = gdn_chunk_ws_bytes(1, (int)std::min<long>(max_tokens + 63L * rows, 1L << 30), c.hv);
+    DUO_TRY(A(&e->chunk_ws, e->chunk_ws_bytes));
+  }
   e->ls.assign(c.layers, LayerState{});
   std::vector<float> ones(std::max(c.hv, 1), 1.f);
   for (int l = 0; l < c.layers; l++) {

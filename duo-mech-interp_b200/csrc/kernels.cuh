@@ -120,7 +120,10 @@ struct GdnScanArgs {
   // optional fused gated RMSNorm + head scale (the engine path): o = o * rms * w * silu(z) * hs[h]
   const void* z; long z_stride;
   const float* norm_w; const float* head_scale; float eps;
+  // chunked scan only: workspace of gdn_chunk_ws_bytes(b, t, h) bytes (per chunk T diag(beta), A and W in f16)
+  void* chunk_ws; long chunk_ws_bytes;
 };
+long gdn_chunk_ws_bytes(int b, int t, int h);
 int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st);
 // decode step (t = 1): conv + gates + l2norm + delta rule + gated norm in one kernel (needs hk == hv)
 int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cudaStream_t st);
