@@ -14,8 +14,9 @@
 // V' = U - W S, the output and the state update, with 4 block barriers per chunk.  All products run on the tensor
 // cores (f16 operands, f32 accumulation; f16 keeps 8x more mantissa than bf16 for these normalised, decay-bounded
 // intermediates); the state lives in registers as f32 accumulators for the whole sequence and is rounded to f16
-// only as an operand copy.  T is formed in f32 by blocked forward substitution (16 x 16 diagonal blocks, then the
-// off-diagonal blocks by distance).  The gated RMSNorm of the engine path is fused into the output.
+// only as an operand copy.  T is formed by blocked forward substitution: the 16 x 16 diagonal blocks in f32 (registers
+// and shuffles), then the off-diagonal blocks by distance as 16 x 16 tensor-core products.  The gated RMSNorm of the
+// engine path is fused into the output.
 #include <mutex>
 #include <type_traits>
 
@@ -36,9 +37,10 @@ constexpr long CHUNK_WS = 64 * 64 * 2 * 2 + 64 * 128 * 2;  // per chunk: T1 [64]
 struct PrepSmem {
   __half q[CK * PD], k[CK * PD];  // chunk inputs (q scaled by 1/sqrt(dk))
   __half t2[CK * PC];              // T diag(beta e^G)
+  __half lh[CK * PC], th[CK * PC];  // f16 copies of L and T for the off-diagonal block products
+  __half xh[3 * 16 * 24];          // per-warp 16 x 16 scratch of the off-diagonal solve
   float a[CK * PF];                // L (strictly lower), f32
   float t[CK * PF];                // T = (I + L)^-1, f32
-  float x[3 * 16 * 17];            // off-diagonal solve scratch
   float gcum[CK], eg[CK], beta[CK];
 };
 
@@ -200,48 +202,88 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(GdnScanArgs a) {
 #pragma unroll
     for (int hf = 0; hf < 2; hf++) {
       const int i = wr + g + hf * 8, jc = wc + 8 * j + 2 * q4;
-      float av[2];
+      float av[2], lv[2];
 #pragma unroll
       for (int e2 = 0; e2 < 2; e2++) {
         const int jj = jc + e2;
         const float dec = jj <= i ? expf(sm.gcum[i] - sm.gcum[jj]) : 0.f;
-        sm.a[i * PF + jj] = jj < i ? sm.beta[i] * kk[j][hf * 2 + e2] * dec : 0.f;
+        lv[e2] = jj < i ? sm.beta[i] * kk[j][hf * 2 + e2] * dec : 0.f;
+        sm.a[i * PF + jj] = lv[e2];
         sm.t[i * PF + jj] = 0.f;
         av[e2] = qk[j][hf * 2 + e2] * dec;
       }
       *reinterpret_cast<uint32_t*>(gA + i * CK + jc) = wm::pack_f16(av[0], av[1]);
+      *reinterpret_cast<uint32_t*>(sm.lh + i * PC + jc) = wm::pack_f16(lv[0], lv[1]);
+      *reinterpret_cast<uint32_t*>(sm.th + i * PC + jc) = 0u;
     }
   }
   __syncthreads();
-  // ---- T = (I + L)^-1: 16 x 16 diagonal blocks by forward substitution (warp b, lane = column) ...
-  if (warp < 4 && lane < 16) {
-    const int o = warp * 16, col = lane;
+  // ---- T = (I + L)^-1.  The four 16 x 16 diagonal blocks by forward substitution in f32: 4 threads per column
+  // (column = tid / 4 of the 64), thread `sub` keeping rows sub, sub + 4, ... of its column in registers and the
+  // partial dot products combined by two shuffles.
+  {
+    const int col = tid >> 2, sub = tid & 3, o = (col >> 4) * 16, cl = col & 15;
+    float tr[4] = {0.f, 0.f, 0.f, 0.f};  // T[o + 4u + sub][o + cl]
+#pragma unroll
     for (int i = 0; i < 16; i++) {
-      float v = (i == col) ? 1.f : 0.f;
-      for (int j = col; j < i; j++) v -= sm.a[(o + i) * PF + o + j] * sm.t[(o + j) * PF + o + col];
-      sm.t[(o + i) * PF + o + col] = v;
+      float part = 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int j = 4 * u + sub;
+        if (j < i) part += sm.a[(o + i) * PF + o + j] * tr[u];
+      }
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      const float v = (i == cl ? 1.f : 0.f) - part;
+      if ((i & 3) == sub) tr[i >> 2] = v;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int r = o + 4 * u + sub;
+      sm.t[r * PF + o + cl] = tr[u];
+      sm.th[r * PC + o + cl] = __float2half_rn(tr[u]);
     }
   }
   __syncthreads();
-  // ... then the off-diagonal blocks by distance: T[bi][bj] = -T[bi][bi] sum_{bj <= bk < bi} L[bi][bk] T[bk][bj]
+  // ... then the off-diagonal blocks by distance d on the tensor cores (f16 operands, f32 accumulation; T is rounded
+  // to f16 for its uses anyway): T[bi][bj] = -T[bi][bi] (sum_{bj <= bk < bi} L[bi][bk] T[bk][bj]), warp bj of 4 - d
   for (int d = 1; d < 4; d++) {
-    const int nb = 4 - d;
-    for (int e = tid; e < nb * 256; e += 256) {
-      const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15, bi = bj + d;
-      float x = 0.f;
-      for (int bk = bj; bk < bi; bk++)
-#pragma unroll 4
-        for (int kk2 = 0; kk2 < 16; kk2++)
-          x += sm.a[(bi * 16 + r) * PF + bk * 16 + kk2] * sm.t[(bk * 16 + kk2) * PF + bj * 16 + cc];
-      sm.x[bj * 272 + r * 17 + cc] = x;
-    }
-    __syncthreads();
-    for (int e = tid; e < nb * 256; e += 256) {
-      const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15, bi = bj + d;
-      float y = 0.f;
-#pragma unroll 4
-      for (int kk2 = 0; kk2 <= r; kk2++) y += sm.t[(bi * 16 + r) * PF + bi * 16 + kk2] * sm.x[bj * 272 + kk2 * 17 + cc];
-      sm.t[(bi * 16 + r) * PF + bj * 16 + cc] = -y;
+    if (warp < 4 - d) {
+      const int bj = warp, bi = warp + d;
+      float X[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int bk = bj; bk < bi; bk++) {
+        uint32_t af[4], bf[4];
+        wm::lda(af, sm.lh, PC, bi * 16, bk * 16);
+        wm::ldb_kn(bf, sm.th, PC, bj * 16, bk * 16);
+        wm::mma_f16(X[0], af, bf);
+        wm::mma_f16(X[1], af, bf + 2);
+      }
+      __half* xh = sm.xh + warp * 16 * 24;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; h2++) {
+        *reinterpret_cast<uint32_t*>(xh + g * 24 + h2 * 8 + 2 * q4) = wm::pack_f16(X[h2][0], X[h2][1]);
+        *reinterpret_cast<uint32_t*>(xh + (g + 8) * 24 + h2 * 8 + 2 * q4) = wm::pack_f16(X[h2][2], X[h2][3]);
+      }
+      __syncwarp();
+      float Y[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      {
+        uint32_t af[4], bf[4];
+        wm::lda(af, sm.th, PC, bi * 16, bi * 16);
+        wm::ldb_kn(bf, xh, 24, 0, 0);
+        wm::mma_f16(Y[0], af, bf);
+        wm::mma_f16(Y[1], af, bf + 2);
+      }
+#pragma unroll
+      for (int h2 = 0; h2 < 2; h2++) {
+        const int cc = bj * 16 + h2 * 8 + 2 * q4;
+        const int r0 = bi * 16 + g, r1 = r0 + 8;
+        sm.t[r0 * PF + cc] = -Y[h2][0];
+        sm.t[r0 * PF + cc + 1] = -Y[h2][1];
+        sm.t[r1 * PF + cc] = -Y[h2][2];
+        sm.t[r1 * PF + cc + 1] = -Y[h2][3];
+        *reinterpret_cast<uint32_t*>(sm.th + r0 * PC + cc) = wm::pack_f16(-Y[h2][0], -Y[h2][1]);
+        *reinterpret_cast<uint32_t*>(sm.th + r1 * PC + cc) = wm::pack_f16(-Y[h2][2], -Y[h2][3]);
+      }
     }
     __syncthreads();
   }
