@@ -3,9 +3,10 @@
 Workload ("throughput serving"): 256 independent prompts of 2048 random token ids, then 512 greedy
 decode steps; int8 weights with one scale per output row, bf16 activations; rows 0..127 carry a random layer-12
 residual steering vector N(0,1) * 0.5 * median residual norm.  Random-init weights of the 0.8B architecture
-(transformers' init distributions), synthetic seeded ids.  Rows are batch-sharded over the ranks (strong scaling:
-256 rows in total); the generated tokens are gathered to every rank with one NCCL all_gather at the end of each
-step.  One step = one full serve of the batch (reset, prefill, 512 decode steps, gather).
+(transformers' init distributions), synthetic seeded ids.  Rows are independent, so the batch is sharded by rows
+across the ranks with no exchange in the forward (weak scaling: each rank serves its own 256-row batch, seeded by
+rank); the generated tokens of all ranks are gathered with one NCCL all_gather at the end of each step.  One step =
+one full serve of every rank's batch (reset, prefill, 512 decode steps, gather).
 
     python bench.py [--gpus N --steps K --warmup W]          # our engine (one JSON line on rank 0)
     python bench.py --impl reference [--steps K --warmup W]   # the reference's CPU PyTorch path, bounded sample
@@ -223,21 +224,17 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     import duo
     from duo import lib as L
+    from duo import serve
     from duo.weights import random_weights
 
     cfg = duo.qwen35_0p8b(group=0, act_dtype="bf16")
-    if a.rows % world:
-        raise SystemExit("rows must divide by the number of GPUs")
-    rows = a.rows // world
-    row0 = rank * rows
+    rows = a.rows  # per rank (weak scaling)
     group_rows = max(1, min(rows, a.max_tokens // a.prompt))
     W = random_weights(cfg, seed=a.seed)
     stream = torch.cuda.Stream()
     m = duo.Model(cfg, W, stream=stream)
     m.alloc(rows=rows, max_len=a.prompt + a.decode + 1, max_t=a.prompt, max_tokens=group_rows * a.prompt)
-    gen = torch.Generator().manual_seed(a.seed)
-    ids_all = torch.randint(0, cfg.vocab_size, (a.rows, a.prompt), generator=gen, dtype=torch.int32)
-    ids_host = ids_all[row0:row0 + rows].contiguous().pin_memory()
+    ids_host = serve.rank_prompts(rank, rows, a.prompt, cfg.vocab_size, a.seed).pin_memory()
     ids_dev = ids_host.to("cuda")
 
     # dose unit of the steering vector: median residual norm after layer 12 over a calibration prompt (token 0
@@ -249,13 +246,11 @@ def main():
         stream.synchronize()
         p50 = float(cap[1:a.prompt].norm(dim=-1).median())
         m.capture_resid(None)
-    vg = torch.Generator().manual_seed(a.seed + 1)
-    vecs = torch.randn(a.rows, cfg.hidden_size, generator=vg) * 0.5 * p50
-    vecs[a.rows // 2:] = 0  # rows 0..127 carry the vector
-    m.set_vectors(list(vecs[row0:row0 + rows]))
+    vecs = serve.rank_vectors(rank, rows, cfg.hidden_size, 0.5 * p50, a.seed)  # rows 0..127 carry the vector
+    m.set_vectors(list(vecs))
 
     tokens = torch.empty(rows, a.decode, dtype=torch.int32, device="cuda")
-    gathered = torch.empty(world, rows, a.decode, dtype=torch.int32, device="cuda") if world > 1 else None
+    gathered = None
     ev = lambda: torch.cuda.Event(enable_timing=True)
 
     def serve(host_io=False):
@@ -270,13 +265,12 @@ def main():
                       a.prompt)
         e1.record(stream)
         toks = m.generate(a.decode, vec=a.vec_layer)
-        if gathered is not None:
-            with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(gathered, toks.contiguous())
+        with torch.cuda.stream(stream):
+            allt = serve.gather_rows(toks, world)  # [world, rows, decode]
         e2.record(stream)
         out = None
         if host_io:
-            out = (gathered if gathered is not None else toks).to("cpu", non_blocking=False)
+            out = allt.to("cpu", non_blocking=False)
         return e0, e1, e2, out
 
     pk, pk_src = peaks()
@@ -327,7 +321,7 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t.item())
-    tokens_total = a.rows * (a.prompt + a.decode) * a.steps
+    tokens_total = world * rows * (a.prompt + a.decode) * a.steps
     value = tokens_total / (total_ms / 1000)
 
     # live per-launch timing of the dominant kernel class (one more step, profiled for that class only)
@@ -380,8 +374,9 @@ def main():
         te = torch.tensor([e_ms], device="cuda")
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": a.rows * (a.prompt + a.decode) * k2 / (float(te.item()) / 1000), "unit": "tok/s",
-               "h2d_bytes_per_step": rows * a.prompt * 4, "d2h_bytes_per_step": a.rows * a.decode * 4,
+        # per rank and step: its ids in (rows x prompt int32); out: every rank's gathered tokens (world x rows x decode)
+        e2e = {"value": world * rows * (a.prompt + a.decode) * k2 / (float(te.item()) / 1000), "unit": "tok/s",
+               "h2d_bytes_per_step": rows * a.prompt * 4, "d2h_bytes_per_step": world * rows * a.decode * 4,
                "steps": k2}
 
     cpu = None
@@ -394,13 +389,14 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": total_ms / a.steps, "higher_is_better": True, "scaling": "strong",
+            "warmup": a.warmup, "ms_per_step": total_ms / a.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random ids, random-init weights)",
-            "config": {"workload": "config5: 256 prompts x 2048 random ids + 512 greedy decode steps, int8 weights "
-                                   "(per-row absmax), bf16 activations, layer-12 vector on rows 0..127",
-                       "rows": a.rows, "prompt": a.prompt, "decode": a.decode, "parallelism": f"dp{world}",
-                       "prefill_tok_s": a.rows * a.prompt / (pre_ms / 1000),
-                       "decode_tok_s": a.rows * a.decode / (dec_ms / 1000),
+            "config": {"workload": "config5: 256 prompts x 2048 random ids + 512 greedy decode steps per GPU, int8 "
+                                   "weights (per-row absmax), bf16 activations, layer-12 vector on rows 0..127",
+                       "rows_per_gpu": rows, "rows_total": world * rows, "prompt": a.prompt, "decode": a.decode,
+                       "parallelism": f"dp{world} (rows sharded, no exchange; tokens gathered once per step)",
+                       "prefill_tok_s": world * rows * a.prompt / (pre_ms / 1000),
+                       "decode_tok_s": world * rows * a.decode / (dec_ms / 1000),
                        "l2": "inputs larger than L2 (state, KV cache and weights far exceed 126 MB)",
                        "prefill_rows_per_call": group_rows},
             "roofline": {"kernel": f"{dominant[0]}:{dominant[1]}", "bound": bound, "achieved": achieved,
