@@ -224,7 +224,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     import duo
     from duo import lib as L
-    from duo import serve
+    from duo import serve as rowshard
     from duo.weights import random_weights
 
     cfg = duo.qwen35_0p8b(group=0, act_dtype="bf16")
@@ -234,7 +234,7 @@ def main():
     stream = torch.cuda.Stream()
     m = duo.Model(cfg, W, stream=stream)
     m.alloc(rows=rows, max_len=a.prompt + a.decode + 1, max_t=a.prompt, max_tokens=group_rows * a.prompt)
-    ids_host = serve.rank_prompts(rank, rows, a.prompt, cfg.vocab_size, a.seed).pin_memory()
+    ids_host = rowshard.rank_prompts(rank, rows, a.prompt, cfg.vocab_size, a.seed).pin_memory()
     ids_dev = ids_host.to("cuda")
 
     # dose unit of the steering vector: median residual norm after layer 12 over a calibration prompt (token 0
@@ -246,7 +246,7 @@ def main():
         stream.synchronize()
         p50 = float(cap[1:a.prompt].norm(dim=-1).median())
         m.capture_resid(None)
-    vecs = serve.rank_vectors(rank, rows, cfg.hidden_size, 0.5 * p50, a.seed)  # rows 0..127 carry the vector
+    vecs = rowshard.rank_vectors(rank, rows, cfg.hidden_size, 0.5 * p50, a.seed)  # rows 0..127 carry the vector
     m.set_vectors(list(vecs))
 
     tokens = torch.empty(rows, a.decode, dtype=torch.int32, device="cuda")
@@ -266,7 +266,7 @@ def main():
         e1.record(stream)
         toks = m.generate(a.decode, vec=a.vec_layer)
         with torch.cuda.stream(stream):
-            allt = serve.gather_rows(toks, world)  # [world, rows, decode]
+            allt = rowshard.gather_rows(toks, world)  # [world, rows, decode]
         e2.record(stream)
         out = None
         if host_io:
