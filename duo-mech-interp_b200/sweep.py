@@ -1,15 +1,16 @@
 """Op-level sweeps of the mixer kernels (BASELINE configs 2 and 3, and the projection GEMM) with CUDA-event timing.
 
     python duo-mech-interp_b200/sweep.py gemm [--m M --n N --k K] [--acc]
+    python duo-mech-interp_b200/sweep.py gemv [--m M --n N --k K]             # int8 GEMV, m <= 8
     python duo-mech-interp_b200/sweep.py gdn-decode [--b B --steps S]      # config 2b
     python duo-mech-interp_b200/sweep.py gdn-prefill [--b B --t T]         # config 2a
     python duo-mech-interp_b200/sweep.py attn-prefill [--b B --t T]        # config 3a
     python duo-mech-interp_b200/sweep.py attn-decode [--b B --len L]       # config 3b
     python duo-mech-interp_b200/sweep.py all                               # every config, one JSON line each
 
-Each case prints one JSON line: the algorithmic work per launch, the mean launch time (CUDA events on the launching
-stream, after warm-up, inputs larger than L2 or rotated through several copies), achieved GB/s or TFLOP/s and the
-fraction of the measured peak of this pool (MEASURED_PEAKS.json).
+Each case prints one JSON line: the algorithmic work per launch, the mean launch time (CUDA events around replays of
+a CUDA graph of the launches, after warm-up, so host launch cost is excluded; inputs larger than L2 or rotated through
+several copies), achieved GB/s or TFLOP/s and the fraction of the measured peak of this pool (MEASURED_PEAKS.json).
 """
 import argparse
 import json
@@ -32,17 +33,34 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
-def timed(fn, iters=10, warmup=3):
+def timed(fn, iters=10, warmup=3, graph=True):
+    """Mean device time (ms) of one fn() call: after `warmup` eager calls, `iters` calls are captured into a CUDA
+    graph and the graph is replayed, so the host's per-call launch cost (Python, ctypes) is not what is measured.
+    graph=False times an eager loop instead."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if not graph:
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / iters
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    reps = 3
     a.record()
-    for _ in range(iters):
-        fn()
+    for _ in range(reps):
+        g.replay()
     b.record()
     torch.cuda.synchronize()
-    return a.elapsed_time(b) / iters
+    return a.elapsed_time(b) / (reps * iters)
 
 
 def report(case, shape, ms, flops=None, bytes_=None, extra=None):
@@ -76,6 +94,27 @@ def gemm(m, n, k, iters=10, compare=True, accumulate=False):
             ms_ref = timed(lambda: torch.matmul(a, b.T, out=c), iters)
         extra.update({"cublas_ms": ms_ref, "cublas_tflops": 2.0 * m * n * k / ms_ref / 1e9})
     return report("gemm_bf16", [m, n, k], ms, flops=2.0 * m * n * k, extra=extra)
+
+
+def gemv(m, n, k, group=128):
+    """The int8 GEMV of decode (m <= 8 rows): y = x . dequant(W)^T with int8 W [n, k] and one f32 scale per 128-group,
+    bf16 x and y.  Weight copies are rotated so that every launch streams W from HBM."""
+    copies = max(1, math.ceil(4 * 126e6 / (n * k)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qs = [torch.randint(-127, 128, (n, k), device="cuda", generator=g, dtype=torch.int8) for _ in range(copies)]
+    ss = [torch.rand(n, k // group, device="cuda", generator=g) * 0.01 for _ in range(copies)]
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    it = {"i": 0}
+
+    def one():
+        i = it["i"] % copies
+        it["i"] += 1
+        ops.q8_gemv(x, qs[i], ss[i], y=y)
+
+    ms = timed(one, iters=max(8, copies), warmup=copies)
+    bytes_ = n * k + n * (k // group) * 4 + m * k * 2 + m * n * 2
+    return report("q8_gemv", {"m": m, "n": n, "k": k, "group": group, "weight_copies": copies}, ms, bytes_=bytes_)
 
 
 def gdn_inputs(b, t, h=16, dtype=torch.bfloat16, copies=1, seed=0):
@@ -150,7 +189,7 @@ def attn_decode(b, length):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "gdn-decode", "gdn-prefill", "attn-prefill", "attn-decode", "all"])
+    ap.add_argument("case", choices=["gemm", "gemv", "gdn-decode", "gdn-prefill", "attn-prefill", "attn-decode", "all"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=7168)
     ap.add_argument("--k", type=int, default=1024)
@@ -164,6 +203,8 @@ def main():
     a = ap.parse_args()
     if a.case == "gemm":
         gemm(a.m, a.n, a.k, a.iters, accumulate=a.acc)
+    elif a.case == "gemv":
+        gemv(a.m if a.m <= 8 else 1, a.n, a.k)
     elif a.case == "gdn-decode":
         gdn_decode(a.b or 1, a.steps)
     elif a.case == "gdn-prefill":
@@ -173,9 +214,11 @@ def main():
     elif a.case == "attn-decode":
         attn_decode(a.b or 32, a.len)
     else:
-        for m, n, k in [(65536, 8224, 1024), (65536, 7168, 1024), (65536, 1024, 3584), (256, 1024, 3584),
-                        (8192, 8192, 8192)]:
+        for m, n, k in [(65536, 8224, 1024), (65536, 7168, 1024), (65536, 1024, 3584), (256, 8224, 1024),
+                        (256, 7168, 1024), (256, 248320, 1024), (8192, 8192, 8192)]:
             gemm(m, n, k)
+        for m, n, k in [(1, 8224, 1024), (3, 8224, 1024), (8, 7168, 1024), (1, 248320, 1024), (3, 248320, 1024)]:
+            gemv(m, n, k)
         for b in (1, 8):
             gdn_decode(b, a.steps)
         for b in (1, 8):
