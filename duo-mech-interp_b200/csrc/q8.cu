@@ -95,8 +95,8 @@ __global__ void q8_gather_kernel(const int32_t* __restrict__ ids, const int8_t* 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// GEMV for m <= 8 rows of activations: one warp per output row, 16 int8 weights per lane per step (one 128-bit
-// streaming load), f32 FMAs, per-16 partial sums scaled by the group scale, warp-shuffle reduction.
+// GEMV for m <= 8 rows of activations: 16 int8 weights per lane per step (one 128-bit streaming load), f32 FMAs,
+// per-16 partial sums scaled by the group scale, warp-shuffle reduction per output.
 
 __device__ __forceinline__ uint4 ld_stream16(const int8_t* p) {
   uint4 r;
@@ -111,60 +111,83 @@ template <typename TX> __device__ __forceinline__ void ld_x16(const TX* p, float
   load8(p + 8, o + 8);
 }
 
-template <int M, typename TX, typename TY>
-__global__ void __launch_bounds__(128) q8_gemv_kernel(const TX* __restrict__ x, int k, const int8_t* __restrict__ q,
+// Each warp owns R consecutive weight rows at a time and issues the 16-byte loads of all of them before using any,
+// so R KiB-rows are in flight per warp; blocks of 8 warps stride over the row groups (a grid sized to the SMs).  Per
+// row the arithmetic is the one-warp-per-row order: lane l takes bytes 16 l + 512 j of the row, 16 products summed in
+// f32, times the group scale, accumulated over j, then a warp butterfly.
+template <int M, int R, typename TX, typename TY>
+__global__ void __launch_bounds__(256) q8_gemv_kernel(const TX* __restrict__ x, int k, const int8_t* __restrict__ q,
                                                       const float* __restrict__ s, int group, int n,
                                                       TY* __restrict__ y, int accumulate) {
   pdl_enter();
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= n) return;
-  const int8_t* wr = q + (long)row * k;
-  const float* sr = s + (long)row * (k / group);
-  float acc[M];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ng = k / group;
+  for (int r0 = (blockIdx.x * 8 + warp) * R; r0 < n; r0 += gridDim.x * 8 * R) {
+    float acc[M][R];
 #pragma unroll
-  for (int i = 0; i < M; i++) acc[i] = 0.f;
-#pragma unroll 4
-  for (int c = lane * 16; c < k; c += 512) {
-    const uint4 u = ld_stream16(wr + c);
-    const float sc = sr[c / group];
-    float w[16];
-    i8x4_to_f32(u.x, w);
-    i8x4_to_f32(u.y, w + 4);
-    i8x4_to_f32(u.z, w + 8);
-    i8x4_to_f32(u.w, w + 12);
+    for (int i = 0; i < M; i++)
 #pragma unroll
-    for (int i = 0; i < M; i++) {
-      float xv[16];
-      ld_x16(x + (long)i * k + c, xv);
-      float d = 0.f;
+      for (int r = 0; r < R; r++) acc[i][r] = 0.f;
+#pragma unroll 2
+    for (int c = lane * 16; c < k; c += 512) {
+      uint4 u[R];
+      float sc[R];
 #pragma unroll
-      for (int j = 0; j < 16; j++) d = fmaf(w[j], xv[j], d);
-      acc[i] = fmaf(d, sc, acc[i]);
+      for (int r = 0; r < R; r++) {
+        const int row = min(r0 + r, n - 1);
+        u[r] = ld_stream16(q + (long)row * k + c);
+        sc[r] = s[(long)row * ng + c / group];
+      }
+#pragma unroll
+      for (int i = 0; i < M; i++) {
+        float xv[16];
+        ld_x16(x + (long)i * k + c, xv);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          float w[16];
+          i8x4_to_f32(u[r].x, w);
+          i8x4_to_f32(u[r].y, w + 4);
+          i8x4_to_f32(u[r].z, w + 8);
+          i8x4_to_f32(u[r].w, w + 12);
+          float d = 0.f;
+#pragma unroll
+          for (int j = 0; j < 16; j++) d = fmaf(w[j], xv[j], d);
+          acc[i][r] = fmaf(d, sc[r], acc[i][r]);
+        }
+      }
     }
-  }
 #pragma unroll
-  for (int i = 0; i < M; i++) acc[i] = warp_sum(acc[i]);
-  if (lane < M) {
-    float v = acc[0];
+    for (int i = 0; i < M; i++)
 #pragma unroll
-    for (int i = 1; i < M; i++)
-      if (lane == i) v = acc[i];
-    TY* yp = y + (long)lane * n + row;
-    if (accumulate) v += to_f(*yp);
-    *yp = from_f<TY>(v);
+      for (int r = 0; r < R; r++) acc[i][r] = warp_sum(acc[i][r]);
+    // lane i * R + r writes y[i][r0 + r]
+#pragma unroll
+    for (int i = 0; i < M; i++)
+#pragma unroll
+      for (int r = 0; r < R; r++)
+        if (lane == i * R + r && r0 + r < n) {
+          TY* yp = y + (long)i * n + r0 + r;
+          float v = acc[i][r];
+          if (accumulate) v += to_f(*yp);
+          *yp = from_f<TY>(v);
+        }
   }
 }
+
+template <int M> constexpr int gemv_rows() { return M <= 2 ? 8 : M <= 4 ? 4 : 2; }
 
 template <typename TX, typename TY>
 int launch_gemv_t(const void* x, int m, int k, const int8_t* q, const float* s, int group, int n, void* y,
                   int accumulate, cudaStream_t st) {
-  dim3 block(128), grid(cdiv(n, 4));
   const TX* xp = static_cast<const TX*>(x);
   TY* yp = static_cast<TY*>(y);
+  auto grid_for = [&](int rows_per_warp) { return std::max(1, std::min(cdiv(n, 8 * rows_per_warp), 4 * sm_count())); };
   switch (m) {
-#define DUO_GEMV_CASE(MM) \
-  case MM: DUO_CUDA_TRY(::duo::launch_kernel(q8_gemv_kernel<MM, TX, TY>, grid, block, 0, st, xp, k, q, s, group, n, yp, accumulate)); break;
+#define DUO_GEMV_CASE(MM)                                                                                          \
+  case MM:                                                                                                         \
+    DUO_CUDA_TRY(::duo::launch_kernel(q8_gemv_kernel<MM, gemv_rows<MM>(), TX, TY>, grid_for(gemv_rows<MM>()), 256, 0, \
+                                      st, xp, k, q, s, group, n, yp, accumulate));                                 \
+    break;
     DUO_GEMV_CASE(1) DUO_GEMV_CASE(2) DUO_GEMV_CASE(3) DUO_GEMV_CASE(4)
     DUO_GEMV_CASE(5) DUO_GEMV_CASE(6) DUO_GEMV_CASE(7) DUO_GEMV_CASE(8)
 #undef DUO_GEMV_CASE
