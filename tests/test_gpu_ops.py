@@ -79,6 +79,21 @@ def test_q8_gemv(ops, m, k, group):
     assert rel_max(yb.float(), refb) < 1e-2
 
 
+@pytest.mark.parametrize("m", [1, 3])
+@pytest.mark.parametrize("n,k,group", [(70000, 1024, 128), (33000, 2048, 2048)])
+def test_q8_gemv_streaming(ops, m, n, k, group):
+    """Matrices of the LM head's size class (grid-stride row groups, ragged last group)."""
+    w = torch.randn(n, k, generator=_seed(n + m)) * 0.02
+    x = torch.randn(m, k, generator=_seed(k + 7 * m))
+    q, s = ops.q8_quantize(w.cuda(), group)
+    ref = oq8.matvec(x.numpy(), q.cpu().numpy(), s.cpu().numpy(), group)
+    assert rel_max(ops.q8_gemv(x.cuda(), q, s), ref) < 1e-5
+    y0 = torch.randn(m, n, generator=_seed(6))
+    y2 = ops.q8_gemv(x.cuda(), q, s, y=y0.clone().cuda(), accumulate=True)
+    assert rel_max(y2, ref + y0.numpy()) < 1e-5
+    assert ops.fault_status() == 0
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # tcgen05 GEMM vs a torch fp32 matmul of the same bf16 operands
 
