@@ -12,52 +12,80 @@
 namespace duo {
 
 // ---------------------------------------------------------------------------------------------------------------
-// prep: block per (token, head of q ∪ kv), one thread per head dim
+// prep: block per token, warp per head of q ∪ kv (head dim 256: 8 consecutive dims per lane, 16-byte accesses).  The
+// token's RoPE angles are computed once per block; RMSNorm by a warp butterfly; the rotate-half partner of dim i
+// (i +- rot / 2) sits rot / 16 lanes away and comes by shuffle.
 
 template <typename T>
-__global__ void attn_prep_kernel(AttnPrepArgs a) {
+__global__ void __launch_bounds__(1024) attn_prep_kernel(AttnPrepArgs a) {
   pdl_enter();
-  extern __shared__ float buf[];  // [hd]
-  __shared__ float red[32];
-  const int m = blockIdx.x, hh = blockIdx.y, i = threadIdx.x;
-  const int hd = a.hd;
+  extern __shared__ float trig[];  // [rot / 2] cos, then [rot / 2] sin
+  const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int HD = 256;
   const int rr = m / a.t, R = a.row_base + rr;
   const int pos = a.len[R] + m % a.t;
+  const int half = a.rot / 2;
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    float sn, cs;
+    sincosf((float)pos * a.inv_freq[j], &sn, &cs);
+    trig[j] = cs;
+    trig[half + j] = sn;
+  }
+  __syncthreads();
+  const int hh = warp;
   const bool isq = hh < a.nh;
   const T* y = static_cast<const T*>(a.y);
-  const long src = isq ? (long)m * a.w + (long)hh * 2 * hd : (long)m * a.w + (long)a.nh * 2 * hd + (long)(hh - a.nh) * hd;
-  const float v = to_f(y[src + i]);
-  const float ss = block_sum(v * v, red);
-  const float r = rsqrtf(ss / (float)hd + a.eps);
-  const float xn = v * r * (1.f + (isq ? a.q_norm[i] : a.k_norm[i]));
-  buf[i] = xn;
-  __syncthreads();
-  float out = xn;
-  const int half = a.rot / 2;
-  if (i < a.rot) {
-    const float ang = (float)pos * a.inv_freq[i % half];
-    float sn, cs;
-    sincosf(ang, &sn, &cs);
-    out = i < half ? xn * cs - buf[i + half] * sn : xn * cs + buf[i - half] * sn;
+  const long src = isq ? (long)m * a.w + (long)hh * 2 * HD : (long)m * a.w + (long)a.nh * 2 * HD + (long)(hh - a.nh) * HD;
+  const int d0 = lane * 8;
+  float v[8];
+  load8(y + src + d0, v);
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; e++) ss += v[e] * v[e];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)HD + a.eps);
+  const float* nw = (isq ? a.q_norm : a.k_norm) + d0;
+  float xn[8], out[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) xn[e] = v[e] * r * (1.f + nw[e]);
+  // rotate-half RoPE on dims [0, rot): lanes [0, rot / 8); partner lane = lane -+ half / 8
+  const int hl = half / 8;
+  const int rl = a.rot / 8;
+  const int partner = lane < hl ? lane + hl : (lane < rl ? lane - hl : lane);
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    const float p = __shfl_sync(0xffffffffu, xn[e], partner);
+    const int i = d0 + e;
+    if (i < a.rot) {
+      const int j = i < half ? i : i - half;
+      const float cs = trig[j], sn = trig[half + j];
+      out[e] = i < half ? xn[e] * cs - p * sn : xn[e] * cs + p * sn;
+    } else {
+      out[e] = xn[e];
+    }
   }
   if (isq) {
-    static_cast<T*>(a.q_out)[((long)m * a.nh + hh) * hd + i] = from_f<T>(out);
+    store8(static_cast<T*>(a.q_out) + ((long)m * a.nh + hh) * HD + d0, out);
   } else {
     const int kvh = hh - a.nh;
-    const long at = (((long)R * a.max_len + pos) * a.nkv + kvh) * hd + i;
-    static_cast<T*>(a.kc)[at] = from_f<T>(out);
-    static_cast<T*>(a.vc)[at] = y[(long)m * a.w + (long)a.nh * 2 * hd + (long)a.nkv * hd + (long)kvh * hd + i];
+    const long at = (((long)R * a.max_len + pos) * a.nkv + kvh) * HD + d0;
+    store8(static_cast<T*>(a.kc) + at, out);
+    float vv[8];
+    load8(y + (long)m * a.w + (long)a.nh * 2 * HD + (long)a.nkv * HD + (long)kvh * HD + d0, vv);
+    store8(static_cast<T*>(a.vc) + at, vv);
   }
 }
 
 int launch_attn_prep(const AttnPrepArgs& a, int dtype, cudaStream_t st) {
   const int m = a.rows * a.t;
   if (m == 0) return DUO_OK;
-  if (a.hd % 32 || a.hd > 1024 || a.rot > a.hd || a.rot % 2) return fail(DUO_EINVAL, "attn_prep: bad head dims");
-  dim3 grid(m, a.nh + a.nkv);
-  const size_t sm = a.hd * sizeof(float);
+  if (a.hd != 256 || a.rot > a.hd || a.rot % 16 || a.nh + a.nkv > 32)
+    return fail(DUO_EINVAL, "attn_prep: needs head dim 256, rot a multiple of 16, at most 32 heads");
+  if (a.w % 8) return fail(DUO_EINVAL, "attn_prep: projection width must be a multiple of 8");
+  const int threads = 32 * (a.nh + a.nkv);
+  const size_t sm = (size_t)a.rot * sizeof(float);
   return with_act(dtype, [&](auto tag) -> int {
-    DUO_CUDA_TRY(::duo::launch_kernel(attn_prep_kernel<decltype(tag)>, grid, a.hd, sm, st, a));
+    DUO_CUDA_TRY(::duo::launch_kernel(attn_prep_kernel<decltype(tag)>, dim3(m), threads, sm, st, a));
     DUO_LAUNCH_CHECK("attn_prep_kernel");
     return DUO_OK;
   });
