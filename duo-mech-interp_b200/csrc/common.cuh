@@ -194,6 +194,9 @@ __device__ __forceinline__ void pdl_enter() {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.f + expf(-x)); }
+// SiLU on the hardware exponential and the approximate divide (a few ulp; x -> -inf gives -0), for the SwiGLU
+// epilogues of the 16-bit GEMMs, whose result is rounded to bf16 / f16 right after
+__device__ __forceinline__ float silu16_(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 // torch's softplus (beta 1, threshold 20) and the reference WGSL's (kernels_qwen35.js:11)
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 

@@ -275,6 +275,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.t = T;
       ep.row_base = row_base;
       ep.push = pt;
+      ep.b_const = true;  // weight packs are written once, at creation
       PROF_TRY(DUO_PROF_GEMM, launch_gemm_tc(e->xn, M, H, e->p_gu[l].w, 2 * c.inter, act, ep, st));
     } else {
       GemmEpiArgs ep;

@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int j = 0; j < 32; j++) {
             const float gs = ep.colscale ? v[j] * ep.colscale[tile_n + gc + j] : v[j];
             const float us = ep.colscale ? u[j] * ep.colscale[tile_n + gc + 64 + j] : u[j];
-            v[j] = siluf_(gs) * us;
+            v[j] = silu16_(gs) * us;
           }
         } else if (ep.colscale) {
 #pragma unroll
@@ -326,6 +326,26 @@ int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long 
   return DUO_OK;
 }
 
+int make_tmap_plain(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
+                    int box_cols) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int es = dtype == DUO_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * es) % 16 || (box_cols * es) % 16)
+    return fail(DUO_EINVAL, "tensor map: base, rows and box rows must be multiples of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == DUO_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == DUO_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return DUO_OK;
+}
+
 unsigned* tc_fault_ptr() {
   static unsigned* ptr = nullptr;
   static std::once_flag once;
@@ -401,9 +421,8 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dty
   if (m == 0 || n == 0) return DUO_OK;
   DUO_CHECK_ARG(k % TC_BK == 0, "gemm_tc: k must be a multiple of 64");
   DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_tc: operands must be bf16 or f16");
-  // decode-sized row counts: the weights-on-M kernel for wide outputs (one K split of its 128-row weight blocks covers
-  // the SMs); the residual adds (narrow N, long K) stay on the per-tile kernel below, whose K split reduces less data
-  if (m <= 256 && ep.epi != EPI_ARGMAX && ep.epi != EPI_ADD_F32) return launch_gemm_dec(a, m, k, b, n, ab_dtype, ep, st);
+  // decode-sized row counts: the weights-on-M kernel (row groups x weight blocks x K slices)
+  if (m <= 256 && ep.epi != EPI_ARGMAX) return launch_gemm_dec(a, m, k, b, n, ab_dtype, ep, st);
   const int sms = sm_count();
   const long tiles_m = cdiv(m, TC_BM);
   // the widest N tile that still gives every SM work (SwiGLU: gate / up interleaved per 64 rows, tiles >= 128)

@@ -1,20 +1,25 @@
-// Decode-sized tcgen05 GEMM (8 < M <= 256 rows): C[m, n] = sum_k X[m, k] W[n, k] with the weights on the MMA's M side.
+// Decode-sized tcgen05 GEMM (M <= 256 rows): C[m, n] = sum_k X[m, k] W[n, k] with the weights on the MMA's M side.
 //
-// With few rows the cost of a GEMM is streaming the weights, and tiling the row side re-reads the activations once per
-// weight tile.  Here a CTA owns 128 weight rows (MMA M = 128) and ALL rows of X (MMA N = NB = 64 / 128 / 256, rows
-// past M read as zeros), so X is read once per 128 weight rows, and K is split over a thread-block cluster of KS <= 8
-// CTAs (grid y = cluster rank) so that each CTA's K slice is in flight at once.  Each CTA moves its 128 x NB f32
-// partial tile TMEM -> shared memory (m-major); after a cluster barrier CTA z sums rows [z R, z R + R) of the KS
-// partials over distributed shared memory in rank order (deterministic) and runs the epilogue on them with
-// consecutive lanes on consecutive weight rows n, i.e. coalesced along the output row: store (16-bit or f32) or
-// SwiGLU (+ pushes) for gate/up packs interleaved per 64 rows.  (The residual-add projections, N = 1024 with long K,
-// stay on gemm.cu's per-tile kernel: split 8 ways here, every CTA would pull 128 KB of partials over DSMEM.)
+// With few rows the cost of a GEMM is streaming the weights once and getting every SM to work on them.  A CTA owns
+// 128 weight rows (MMA M = 128) and a group of NB = 64 or 128 X rows (MMA N = NB; rows past M read as zeros), so
+// grid = (weight blocks, row groups, K slices).  Wide outputs (the in-projections, gate|up) fill the SMs with the
+// first two dimensions and need no K split; narrow ones (N = 1024, long K) split K over a thread-block cluster of
+// KS <= 8 CTAs (grid z = cluster rank).
+//
+// Epilogues.  Without a K split the accumulator goes TMEM -> registers -> (colscale, SwiGLU + pushes, 16-bit or f32
+// convert) -> a dense shared-memory tile -> one TMA store, so the tile leaves the SM as whole rows.  With a K split,
+// or for the residual add, each CTA drains its raw f32 partial into shared memory (m-major); after a cluster barrier
+// CTA z takes rows [z R, z R + R) of the group (R = NB / KS), sums the KS partials over distributed shared memory in
+// rank order (deterministic) and runs the epilogue with consecutive lanes on consecutive weight rows n, i.e.
+// coalesced along the output row: store, SwiGLU (+ pushes; gate / up packs interleaved per 64 rows) or
+// X += acc * colscale (+ vec).
 //
 // The arithmetic is the reference's matmul (engine/kernels.js:97-151): f32 accumulation of products of the 16-bit
 // operands; the per-row int8 scale (colscale) multiplies the reduced sum.
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "kernels.cuh"
 #include "tc.cuh"
@@ -31,31 +36,39 @@ template <int NB> struct DCfg {
   static constexpr int W_BYTES = DBM * DBK * 2;
   static constexpr int X_BYTES = NB * DBK * 2;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
   static constexpr int RING = STAGES * STAGE_BYTES;
   static constexpr int SMEM = 1024 + RING + 256;
-  static_assert(NB * DP * 4 <= RING, "the partial tile must fit in the ring");
+  static constexpr int OUT_OFF = (NB * DP * 4 + 1023) / 1024 * 1024;  // SwiGLU output tile, after the partial
+  static_assert(OUT_OFF + NB * 64 * 2 <= RING, "the partial and SwiGLU tiles must fit in the ring");
+  static_assert(NB * DBM * 4 <= RING, "the f32 output tile must fit in the ring");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
+template <typename T> __device__ __forceinline__ T cvt16(float v);
+template <> __device__ __forceinline__ __nv_bfloat16 cvt16<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half cvt16<__half>(float v) { return __float2half_rn(v); }
+
 template <int NB, int EPI, bool F16>
 __global__ void __launch_bounds__(DTHREADS, 1)
-    gemm_dec_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x, int M,
-                    int N, int K, int kper, GemmEpiArgs ep, unsigned* fault) {
+    gemm_dec_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x,
+                    const __grid_constant__ CUtensorMap tma_c, int M, int N, int K, int kper, int direct,
+                    GemmEpiArgs ep, unsigned* fault) {
   using C = DCfg<NB>;
+  constexpr int CW = NB / 2;  // accumulator columns (X rows) drained per warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sw = smem;
   uint8_t* sx = smem + C::STAGES * C::W_BYTES;
-  float* part = reinterpret_cast<float*>(smem);  // [NB][DP], reuses the ring once every MMA has completed
+  float* part = reinterpret_cast<float*>(smem);  // epilogue tiles reuse the ring once every MMA has completed
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tmem_full = empty + C::STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * DBM;
-  const int ks = gridDim.y, z = blockIdx.y;
+  const int n0 = blockIdx.x * DBM, m0 = blockIdx.y * NB;
+  const int ks = gridDim.z, z = blockIdx.z;
   const int kb0 = z * kper;
   const int num_k = max(0, min(kper, K / DBK - kb0));
 
@@ -68,6 +81,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tma_w);
     tc::prefetch_tmap(&tma_x);
+    if (direct) tc::prefetch_tmap(&tma_c);
   }
   if (warp == 1) tc::tmem_alloc(tmem_slot, NB);
   tc::fence_before_sync();
@@ -75,16 +89,48 @@ __global__ void __launch_bounds__(DTHREADS, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  // Programmatic launch: constant weight tiles of the first stages stream in while the preceding kernel finishes.
+  // The weight slice is requested in full at once: the first ring stages by TMA loads, the rest as L2 prefetches,
+  // so HBM latency is paid about once rather than once per ring turn.  Programmatic launch: constant weights are
+  // requested while the preceding kernel finishes.
   const int pre = ep.b_const ? min(num_k, C::STAGES) : 0;
-  if (warp == 0 && lane == 0) {
-    for (int kb = 0; kb < pre; kb++) {
-      tc::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
-      tc::tma_load_2d(sw + kb * C::W_BYTES, &tma_w, (kb0 + kb) * DBK, n0, &full[kb]);
+  auto request_w = [&](int from) {
+    for (int kb = from; kb < num_k; kb++) {
+      if (kb < pre) {
+        tc::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+        tc::tma_load_2d(sw + kb * C::W_BYTES, &tma_w, (kb0 + kb) * DBK, n0, &full[kb]);
+      } else if (kb >= C::STAGES) {
+        tc::tma_prefetch_2d(&tma_w, (kb0 + kb) * DBK, n0);
+      }
     }
-  }
+  };
+  if (warp == 0 && lane == 0 && ep.b_const) request_w(0);
   pdl_wait();
   pdl_trigger();
+  if (warp == 0 && lane == 0 && !ep.b_const) request_w(C::STAGES);
+
+  // Rows [r_lo, r_hi) of the group are this CTA's in the reducing epilogue.  For the residual add with at most four
+  // rows per warp, each thread's residual (and vector) entries are loaded now and arrive while the mainloop runs (X
+  // is written only by kernels that have completed once pdl_wait returns).
+  constexpr int RB = 4;
+  const int R = (NB + ks - 1) / ks;
+  const int r_lo = z * R, r_hi = min(min(NB, r_lo + R), M - m0);
+  const int n4 = n0 + lane * 4;
+  const bool al = (reinterpret_cast<uintptr_t>(ep.c) & 15) == 0 && ep.ldc % 4 == 0 &&
+                  (ep.vec == nullptr || (reinterpret_cast<uintptr_t>(ep.vec) & 15) == 0);
+  const bool pre_x = EPI == EPI_ADD_F32 && R <= 8 * RB && al && n4 + 4 <= N;
+  float4 xold[RB], vold[RB];
+  if (pre_x) {
+#pragma unroll
+    for (int i = 0; i < RB; i++) {
+      const int cr = r_lo + warp + 8 * i;
+      if (cr < r_hi) {
+        const int m = m0 + cr;
+        xold[i] = *reinterpret_cast<const float4*>(static_cast<const float*>(ep.c) + (long)m * ep.ldc + n4);
+        vold[i] = ep.vec ? *reinterpret_cast<const float4*>(ep.vec + (long)(ep.row_base + m / ep.t) * ep.ldc + n4)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
 
   bool ok = true;
   if (warp == 0 && lane == 0) {
@@ -92,7 +138,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       const int s = kb % C::STAGES;
       const uint32_t ph = (kb / C::STAGES) & 1;
       if (kb < pre) {
-        tc::tma_load_2d(sx + s * C::X_BYTES, &tma_x, (kb0 + kb) * DBK, 0, &full[s]);
+        tc::tma_load_2d(sx + s * C::X_BYTES, &tma_x, (kb0 + kb) * DBK, m0, &full[s]);
         continue;
       }
       if (kb >= C::STAGES && !tc::mbar_wait(&empty[s], ph ^ 1)) {
@@ -101,7 +147,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       }
       tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
       tc::tma_load_2d(sw + s * C::W_BYTES, &tma_w, (kb0 + kb) * DBK, n0, &full[s]);
-      tc::tma_load_2d(sx + s * C::X_BYTES, &tma_x, (kb0 + kb) * DBK, 0, &full[s]);
+      tc::tma_load_2d(sx + s * C::X_BYTES, &tma_x, (kb0 + kb) * DBK, m0, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = tc::idesc_16_f32(DBM, NB, F16);
@@ -123,166 +169,239 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     }
     if (ok) tc::mma_commit(tmem_full);
   }
-  // partial tile TMEM -> shared memory, m-major, by all 8 warps once the MMAs are done: warp w holds weight rows
-  // 32 (w % 4) .. + 31 (its TMEM lane quarter) and columns [(w / 4) NB / 2, + NB / 2)
-  bool have = true;
-  {
-    __syncwarp();  // warps 0 and 1 reconverge after their single-lane roles (tcgen05.ld is warp-wide)
-    const int quad = warp & 3, half = warp >> 2;
-    const int n = quad * 32 + lane;
-    if (num_k > 0) {
-      have = tc::mbar_wait(tmem_full, 0);
-      if (!have) {
-        if (lane == 0) atomicOr(fault, 4u);
-      } else {
-        tc::fence_after_sync();
-        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-#pragma unroll 1
-        for (int c0 = half * (NB / 2); c0 < (half + 1) * (NB / 2); c0 += 32) {
-          uint32_t r[32];
-          tc::tmem_ld32_issue(trow + c0, r);
-          tc::tmem_ld_wait(r);
-#pragma unroll
-          for (int j = 0; j < 32; j++) part[(c0 + j) * DP + n] = __uint_as_float(r[j]);
-        }
-      }
-    } else {  // an empty K slice contributes zeros
-      for (int m = half * (NB / 2); m < (half + 1) * (NB / 2); m++) part[m * DP + n] = 0.f;
-    }
-  }
-  // every partial of the cluster is in shared memory
-  if (ks > 1) cg::this_cluster().sync();
-  else __syncthreads();
 
-  // reduce rows [z R, z R + R) over the cluster and run the epilogue; 8 warps, one or two rows per warp step
-  const int mrows = min(M, NB);
-  const int R = (mrows + ks - 1) / ks;
-  const int m_lo = z * R, m_hi = min(mrows, m_lo + R);
-  const bool v16 = (reinterpret_cast<uintptr_t>(ep.c) & 15) == 0 && ep.ldc % 4 == 0;
-  cg::cluster_group cluster = cg::this_cluster();
-  // Every partial of a batch of RB rows is loaded (distributed shared memory, all ranks unrolled) before any result
-  // is stored, so the remote-load latency is paid about once per batch rather than once per row and rank.
-  constexpr int RB = 4;
-  auto gather = [&](const int (&ms)[RB], int col, float4 (&out)[RB]) {  // out[i] = sum over ranks of part[ms[i]][col..]
+  // Drain: warp w holds TMEM lane quarter q = w % 4 (weight rows nl = 32 q + lane) and accumulator columns
+  // [h CW, h CW + CW), h = w / 4 (X rows m0 + c); every load of the warp is issued before the one wait.
+  __syncwarp();  // warps 0 and 1 reconverge after their single-lane roles (tcgen05.ld is warp-wide)
+  const int q = warp & 3, h = warp >> 2;
+  const int nl = q * 32 + lane, c_lo = h * CW;
+  uint32_t r[CW / 32][32];
+  if (num_k > 0) {
+    if (!tc::mbar_wait(tmem_full, 0)) {
+      if (lane == 0) atomicOr(fault, 4u);
+    }
+    tc::fence_after_sync();
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c_lo;
 #pragma unroll
-    for (int i = 0; i < RB; i++) out[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < CW / 32; j++) tc::tmem_ld32_issue(trow + 32 * j, r[j]);
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-      if (q < ks) {
-        const float* pq = ks > 1 ? cluster.map_shared_rank(part, q) : part;
-        float4 v[RB];
+    for (int j = 0; j < CW / 32; j++) tc::tmem_ld_wait(r[j]);
+  } else {  // an empty K slice contributes zeros
 #pragma unroll
-        for (int i = 0; i < RB; i++)
-          if (ms[i] >= 0) v[i] = *reinterpret_cast<const float4*>(pq + ms[i] * DP + col);
+    for (int j = 0; j < CW / 32; j++)
 #pragma unroll
-        for (int i = 0; i < RB; i++) {
-          if (ms[i] < 0) continue;
-          out[i].x += v[i].x; out[i].y += v[i].y; out[i].z += v[i].z; out[i].w += v[i].w;
+      for (int i = 0; i < 32; i++) r[j][i] = 0u;
+  }
+  auto acc = [&](int c) { return __uint_as_float(r[c >> 5][c & 31]); };  // accumulator column c_lo + c
+
+  if (direct) {
+    // no K split, store or SwiGLU: the output tile is assembled in shared memory and leaves by one TMA store
+    if (EPI == EPI_SWIGLU) {
+      // weight rows 0..63 of the block are gate rows, 64..127 the matching up rows (interleave_gate_up order): the
+      // scaled accumulators go to part[c][nl], then a rolled sweep (small code: each CTA runs it once, from a cold
+      // instruction cache) forms 4 outputs per step into the [NB][64] 16-bit tile that follows the partial
+      const float cs = ep.colscale ? ep.colscale[n0 + nl] : 1.f;
+#pragma unroll
+      for (int c = 0; c < CW; c++) part[(c_lo + c) * DP + nl] = acc(c) * cs;
+      __syncthreads();
+      uint8_t* tile = smem + C::OUT_OFF;
+#pragma unroll 1
+      for (int idx = threadIdx.x; idx < NB * 16; idx += DTHREADS) {
+        const int c = idx >> 4, j4 = (idx & 15) * 4, m = m0 + c;
+        const float4 g = *reinterpret_cast<const float4*>(part + c * DP + j4);
+        const float4 u = *reinterpret_cast<const float4*>(part + c * DP + 64 + j4);
+        float o[4] = {silu16_(g.x) * u.x, silu16_(g.y) * u.y, silu16_(g.z) * u.z, silu16_(g.w) * u.w};
+        if (ep.push.count && m < M) {
+          const int rw = ep.row_base + m / ep.t;
+#pragma unroll
+          for (int i = 0; i < 4; i++) o[i] = push_apply(ep.push, rw, n0 / 2 + j4 + i, o[i]);
         }
+        uint2 pk;
+        if (F16) {
+          const __half2 lo = __floats2half2_rn(o[0], o[1]), hi = __floats2half2_rn(o[2], o[3]);
+          pk = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+        } else {
+          const __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
+          pk = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+        }
+        *reinterpret_cast<uint2*>(tile + (c * 64 + j4) * 2) = pk;
       }
-    }
-  };
-  auto store4_16 = [&](long off, const float* o) {  // 4 consecutive 16-bit outputs, one 8-byte store when aligned
-    uint32_t w[2];
-    for (int i = 0; i < 2; i++) {
-      if (ep.c_dtype == DUO_BF16) {
-        const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
-        w[i] = *reinterpret_cast<const uint32_t*>(&h);
-      } else {
-        const __half2 h = __floats2half2_rn(o[2 * i], o[2 * i + 1]);
-        w[i] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-    }
-    uint8_t* base = static_cast<uint8_t*>(ep.c) + off * 2;
-    if ((reinterpret_cast<uintptr_t>(base) & 7) == 0) {
-      *reinterpret_cast<uint2*>(base) = make_uint2(w[0], w[1]);
     } else {
-      reinterpret_cast<uint32_t*>(base)[0] = w[0];
-      reinterpret_cast<uint32_t*>(base)[1] = w[1];
-    }
-  };
-  if (EPI == EPI_SWIGLU) {
-    // half-warp per row: lane & 15 -> output columns 4 (lane & 15) .. + 3 of the block's 64 neurons
-    const int j4 = (lane & 15) * 4;
-    const int nout = n0 / 2 + j4;  // first output column
-    float cg_[4] = {1.f, 1.f, 1.f, 1.f}, cu_[4] = {1.f, 1.f, 1.f, 1.f};
-    if (ep.colscale) {
-      for (int i = 0; i < 4; i++) {
-        cg_[i] = ep.colscale[n0 + j4 + i];
-        cu_[i] = ep.colscale[n0 + 64 + j4 + i];
+      const int n = n0 + nl;
+      const float cs = ep.colscale ? (n < N ? ep.colscale[n] : 0.f) : 1.f;
+      if (ep.c_dtype == DUO_F32) {
+        float* o = reinterpret_cast<float*>(smem);
+#pragma unroll
+        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = acc(c) * cs;
+      } else if (ep.c_dtype == DUO_F16) {
+        __half* o = reinterpret_cast<__half*>(smem);
+#pragma unroll
+        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = cvt16<__half>(acc(c) * cs);
+      } else {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(smem);
+#pragma unroll
+        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = cvt16<__nv_bfloat16>(acc(c) * cs);
       }
     }
-    for (int mb = m_lo + warp * 2 + (lane >> 4); mb < m_hi; mb += 16 * RB) {
-      int ms[RB];
-#pragma unroll
-      for (int i = 0; i < RB; i++) ms[i] = mb + 16 * i < m_hi ? mb + 16 * i : -1;
-      float4 g[RB], u[RB];
-      gather(ms, j4, g);
-      gather(ms, 64 + j4, u);
-#pragma unroll
-      for (int i = 0; i < RB; i++) {
-        const int m = mb + 16 * i;
-        if (m >= m_hi) break;
-        const float gv[4] = {g[i].x, g[i].y, g[i].z, g[i].w}, uv[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
-        const int r = ep.row_base + m / ep.t;
-        float o[4];
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          o[c] = siluf_(gv[c] * cg_[c]) * (uv[c] * cu_[c]);
-          if (ep.push.count) o[c] = push_apply(ep.push, r, nout + c, o[c]);
-        }
-        store4_16((long)m * ep.ldc + nout, o);
-      }
+    tc::fence_proxy_async();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (EPI == EPI_SWIGLU) tc::tma_store_2d(&tma_c, smem + C::OUT_OFF, n0 / 2, m0);
+      else tc::tma_store_2d(&tma_c, smem, n0, m0);
+      tc::bulk_commit();
+      tc::bulk_wait_read();  // the tile may be released; the grid's completion publishes the writes
     }
   } else {
-    // one row per warp step: lane -> weight rows n0 + 4 lane .. + 3
-    const int n = n0 + lane * 4;
-    float cs[4] = {1.f, 1.f, 1.f, 1.f};
-    if (ep.colscale) {
-      for (int i = 0; i < 4; i++) cs[i] = (n + i < N) ? ep.colscale[n + i] : 0.f;
-    }
-    for (int mb = m_lo + warp; mb < m_hi; mb += 8 * RB) {
-      if (n >= N) break;
-      int ms[RB];
+    // raw partial tile -> shared memory, m-major: part[c][nl]
 #pragma unroll
-      for (int i = 0; i < RB; i++) ms[i] = mb + 8 * i < m_hi ? mb + 8 * i : -1;
-      float4 a[RB];
-      gather(ms, lane * 4, a);
+    for (int c = 0; c < CW; c++) part[(c_lo + c) * DP + nl] = acc(c);
+    if (ks > 1) cg::this_cluster().sync();
+    else __syncthreads();
+
+    // reduce rows [r_lo, r_hi) of the group over the cluster and run the epilogue
+    cg::cluster_group cluster = cg::this_cluster();
+    // Every partial of a batch of RB rows is loaded (distributed shared memory, all ranks unrolled) before any result
+    // is stored, so the remote-load latency is paid about once per batch rather than once per row and rank.
+    auto gather = [&](const int (&cr)[RB], int col, float4 (&out)[RB]) {  // out[i] = sum over ranks of part[cr[i]][col..]
 #pragma unroll
-      for (int i = 0; i < RB; i++) {
-        const int m = mb + 8 * i;
-        if (m >= m_hi) break;
-        float x[4] = {a[i].x * cs[0], a[i].y * cs[1], a[i].z * cs[2], a[i].w * cs[3]};
-        const long off = (long)m * ep.ldc + n;
-        const bool full4 = v16 && n + 4 <= N;
-        if (ep.c_dtype == DUO_F32) {
-          float* Cp = static_cast<float*>(ep.c) + off;
-          if (full4) *reinterpret_cast<float4*>(Cp) = make_float4(x[0], x[1], x[2], x[3]);
-          else for (int c = 0; c < 4 && n + c < N; c++) Cp[c] = x[c];
-        } else if (n + 4 <= N) {
-          store4_16(off, x);
+      for (int i = 0; i < RB; i++) out[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int qq = 0; qq < 8; qq++) {
+        if (qq < ks) {
+          const float* pq = ks > 1 ? cluster.map_shared_rank(part, qq) : part;
+          float4 v[RB];
+#pragma unroll
+          for (int i = 0; i < RB; i++)
+            if (cr[i] >= 0) v[i] = *reinterpret_cast<const float4*>(pq + cr[i] * DP + col);
+#pragma unroll
+          for (int i = 0; i < RB; i++) {
+            if (cr[i] < 0) continue;
+            out[i].x += v[i].x; out[i].y += v[i].y; out[i].z += v[i].z; out[i].w += v[i].w;
+          }
+        }
+      }
+    };
+    auto store4_16 = [&](long off, const float* o) {  // 4 consecutive 16-bit outputs, one 8-byte store when aligned
+      uint32_t w[2];
+      for (int i = 0; i < 2; i++) {
+        if (ep.c_dtype == DUO_BF16) {
+          const __nv_bfloat162 hh = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+          w[i] = *reinterpret_cast<const uint32_t*>(&hh);
         } else {
-          for (int c = 0; c < 4 && n + c < N; c++) {
-            if (ep.c_dtype == DUO_BF16) static_cast<__nv_bfloat16*>(ep.c)[off + c] = __float2bfloat16_rn(x[c]);
-            else static_cast<__half*>(ep.c)[off + c] = __float2half_rn(x[c]);
+          const __half2 hh = __floats2half2_rn(o[2 * i], o[2 * i + 1]);
+          w[i] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+      }
+      uint8_t* base = static_cast<uint8_t*>(ep.c) + off * 2;
+      if ((reinterpret_cast<uintptr_t>(base) & 7) == 0) {
+        *reinterpret_cast<uint2*>(base) = make_uint2(w[0], w[1]);
+      } else {
+        reinterpret_cast<uint32_t*>(base)[0] = w[0];
+        reinterpret_cast<uint32_t*>(base)[1] = w[1];
+      }
+    };
+    if (EPI == EPI_SWIGLU) {
+      // half-warp per row: lane & 15 -> output columns 4 (lane & 15) .. + 3 of the block's 64 neurons
+      const int j4 = (lane & 15) * 4;
+      const int nout = n0 / 2 + j4;  // first output column
+      float cg_[4] = {1.f, 1.f, 1.f, 1.f}, cu_[4] = {1.f, 1.f, 1.f, 1.f};
+      if (ep.colscale) {
+        for (int i = 0; i < 4; i++) {
+          cg_[i] = ep.colscale[n0 + j4 + i];
+          cu_[i] = ep.colscale[n0 + 64 + j4 + i];
+        }
+      }
+      for (int cb = r_lo + warp * 2 + (lane >> 4); cb < r_hi; cb += 16 * RB) {
+        int cr[RB];
+#pragma unroll
+        for (int i = 0; i < RB; i++) cr[i] = cb + 16 * i < r_hi ? cb + 16 * i : -1;
+        float4 g[RB], u[RB];
+        gather(cr, j4, g);
+        gather(cr, 64 + j4, u);
+#pragma unroll
+        for (int i = 0; i < RB; i++) {
+          if (cr[i] < 0) break;
+          const int m = m0 + cr[i];
+          const float gv[4] = {g[i].x, g[i].y, g[i].z, g[i].w}, uv[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+          const int rw = ep.row_base + m / ep.t;
+          float o[4];
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            o[c] = silu16_(gv[c] * cg_[c]) * (uv[c] * cu_[c]);
+            if (ep.push.count) o[c] = push_apply(ep.push, rw, nout + c, o[c]);
+          }
+          store4_16((long)m * ep.ldc + nout, o);
+        }
+      }
+    } else {
+      // one row per warp step: lane -> weight rows n0 + 4 lane .. + 3
+      const int n = n4;
+      float csv[4] = {1.f, 1.f, 1.f, 1.f};
+      if (ep.colscale) {
+        for (int i = 0; i < 4; i++) csv[i] = (n + i < N) ? ep.colscale[n + i] : 0.f;
+      }
+      for (int cb = r_lo + warp; cb < r_hi && n < N; cb += 8 * RB) {
+        int cr[RB];
+#pragma unroll
+        for (int i = 0; i < RB; i++) cr[i] = cb + 8 * i < r_hi ? cb + 8 * i : -1;
+        float4 a[RB];
+        gather(cr, lane * 4, a);
+#pragma unroll
+        for (int i = 0; i < RB; i++) {
+          if (cr[i] < 0) break;
+          const int m = m0 + cr[i];
+          float x[4] = {a[i].x * csv[0], a[i].y * csv[1], a[i].z * csv[2], a[i].w * csv[3]};
+          const long off = (long)m * ep.ldc + n;
+          const bool full4 = al && n + 4 <= N;
+          if (EPI == EPI_ADD_F32) {
+            float* X = static_cast<float*>(ep.c) + off;
+            const float* vr = ep.vec ? ep.vec + (long)(ep.row_base + m / ep.t) * ep.ldc + n : nullptr;
+            if (pre_x) {  // one batch: i is the preload slot of this row
+              float4 o = xold[i];
+              o.x += x[0]; o.y += x[1]; o.z += x[2]; o.w += x[3];
+              if (ep.vec) { o.x += vold[i].x; o.y += vold[i].y; o.z += vold[i].z; o.w += vold[i].w; }
+              *reinterpret_cast<float4*>(X) = o;
+            } else if (full4) {
+              float4 o = *reinterpret_cast<float4*>(X);
+              o.x += x[0]; o.y += x[1]; o.z += x[2]; o.w += x[3];
+              if (vr) {
+                const float4 v4 = *reinterpret_cast<const float4*>(vr);
+                o.x += v4.x; o.y += v4.y; o.z += v4.z; o.w += v4.w;
+              }
+              *reinterpret_cast<float4*>(X) = o;
+            } else {
+              for (int c = 0; c < 4 && n + c < N; c++) X[c] += x[c] + (vr ? vr[c] : 0.f);
+            }
+          } else if (ep.c_dtype == DUO_F32) {
+            float* Cp = static_cast<float*>(ep.c) + off;
+            if (full4) *reinterpret_cast<float4*>(Cp) = make_float4(x[0], x[1], x[2], x[3]);
+            else for (int c = 0; c < 4 && n + c < N; c++) Cp[c] = x[c];
+          } else if (n + 4 <= N) {
+            store4_16(off, x);
+          } else {
+            for (int c = 0; c < 4 && n + c < N; c++) {
+              if (ep.c_dtype == DUO_BF16) static_cast<__nv_bfloat16*>(ep.c)[off + c] = __float2bfloat16_rn(x[c]);
+              else static_cast<__half*>(ep.c)[off + c] = __float2half_rn(x[c]);
+            }
           }
         }
       }
     }
+    // no CTA leaves while a peer may still read its partial: every remote load of this CTA has returned (its value
+    // was stored above), so a relaxed arrive suffices and the stores need not drain first
+    if (ks > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
   }
-  if (ks > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may still read its partial
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, NB);
   }
-  (void)have;
 }
 
 template <int NB, int EPI, bool F16>
-int run_dec(const CUtensorMap& tw, const CUtensorMap& tx, int m, int n, int k, const GemmEpiArgs& ep,
-            cudaStream_t st) {
+int run_dec(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tcm, int m, int n, int k, int groups,
+            int ks, int kper, int direct, const GemmEpiArgs& ep, cudaStream_t st) {
   using C = DCfg<NB>;
   static bool attr_set = false;
   auto kern = gemm_dec_kernel<NB, EPI, F16>;
@@ -292,14 +411,8 @@ int run_dec(const CUtensorMap& tw, const CUtensorMap& tx, int m, int n, int k, c
   }
   unsigned* fault = tc_fault_ptr();
   if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
-  const int nblocks = cdiv(n, DBM);
-  const int num_k = k / DBK;
-  // split K so that the grid roughly covers the SMs once (one CTA per SM), at most 8 ways (portable cluster size)
-  int ks = std::max(1, std::min({sm_count() / nblocks, 8, num_k}));
-  const int kper = cdiv(num_k, ks);
-  ks = cdiv(num_k, kper);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nblocks, ks);
+  cfg.gridDim = dim3(cdiv(n, DBM), groups, ks);
   cfg.blockDim = dim3(DTHREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
@@ -308,8 +421,8 @@ int run_dec(const CUtensorMap& tw, const CUtensorMap& tx, int m, int n, int k, c
   if (ks > 1) {
     attr[na].id = cudaLaunchAttributeClusterDimension;
     attr[na].val.clusterDim.x = 1;
-    attr[na].val.clusterDim.y = ks;
-    attr[na].val.clusterDim.z = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = ks;
     na++;
   }
   if (pdl_enabled()) {
@@ -319,16 +432,75 @@ int run_dec(const CUtensorMap& tw, const CUtensorMap& tx, int m, int n, int k, c
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  DUO_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tw, tx, m, n, k, kper, ep, fault));
+  DUO_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tw, tx, tcm, m, n, k, kper, direct, ep, fault));
   DUO_LAUNCH_CHECK("gemm_dec_kernel");
   return DUO_OK;
 }
 
 template <int NB, bool F16>
-int dispatch_dec(const CUtensorMap& tw, const CUtensorMap& tx, int m, int n, int k, const GemmEpiArgs& ep,
-                 cudaStream_t st) {
-  if (ep.epi == EPI_SWIGLU) return run_dec<NB, EPI_SWIGLU, F16>(tw, tx, m, n, k, ep, st);
-  return run_dec<NB, EPI_STORE, F16>(tw, tx, m, n, k, ep, st);
+int dispatch_dec(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tcm, int m, int n, int k,
+                 int groups, int ks, int kper, int direct, const GemmEpiArgs& ep, cudaStream_t st) {
+  if (ep.epi == EPI_SWIGLU)
+    return run_dec<NB, EPI_SWIGLU, F16>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, st);
+  if (ep.epi == EPI_ADD_F32)
+    return run_dec<NB, EPI_ADD_F32, F16>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, st);
+  return run_dec<NB, EPI_STORE, F16>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, st);
+}
+
+// Clusters of ks CTAs of the kernel that can be resident at once (one CTA per SM; a cluster must fit in one GPC).
+// The resources are those of every epilogue and operand type, so one instantiation answers for all.
+template <int NB> int max_clusters(int ks) {
+  static int cache[9] = {};
+  if (ks <= 1) return sm_count();
+  if (cache[ks]) return cache[ks];
+  auto kern = gemm_dec_kernel<NB, EPI_STORE, false>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DCfg<NB>::SMEM) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, ks);
+    cfg.blockDim = dim3(DTHREADS);
+    cfg.dynamicSmemBytes = DCfg<NB>::SMEM;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = ks;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  (void)cudaGetLastError();
+  if (n <= 0) n = sm_count() / ks;
+  cache[ks] = n;
+  return n;
+}
+
+// Launch plan: row-group size nb and K split ks, chosen to minimise waves x (a fixed cost per wave + the bytes each
+// CTA pulls in: its weight and X slices, plus the partials it reads back over the cluster).  The fixed cost (launch,
+// first-load latency, epilogue: ~4 us) is counted as the bytes a CTA streams in that time (~90 GB/s per SM when
+// every SM streams).
+constexpr double kWaveBytes = 360e3;
+struct DecPlan {
+  int nb = 0, groups = 0, ks = 1, kper = 0;
+  double cost = 0.0;
+};
+template <int NB> void plan_dec(int m, int n, int num_k, DecPlan& best) {
+  const long sms = sm_count();
+  const int groups = cdiv(m, NB);
+  const long base = (long)cdiv(n, DBM) * groups;
+  for (int want = 1; want <= std::min(8, num_k); want++) {
+    const int kper = cdiv(num_k, want);
+    const int ks = cdiv(num_k, kper);
+    if (ks != want) continue;  // the same split as a smaller want
+    const long slots = ks > 1 ? (long)max_clusters<NB>(ks) : sms;
+    const long waves = (base + slots - 1) / slots;
+    const double ingest = (double)(DBM + NB) * kper * DBK * 2;
+    const double reduce = ks > 1 ? (double)NB * DBM * 4 * (ks - 1) / ks : 0.0;
+    const double cost = (double)waves * (kWaveBytes + ingest + reduce);
+    if (best.nb == 0 || cost < best.cost) {
+      best.nb = NB; best.groups = groups; best.ks = ks; best.kper = kper; best.cost = cost;
+    }
+  }
 }
 
 }  // namespace
@@ -339,23 +511,36 @@ int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dt
   DUO_CHECK_ARG(m <= 256, "gemm_dec: at most 256 rows");
   DUO_CHECK_ARG(k % DBK == 0, "gemm_dec: k must be a multiple of 64");
   DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_dec: operands must be bf16 or f16");
-  DUO_CHECK_ARG(ep.epi == EPI_STORE || ep.epi == EPI_SWIGLU, "gemm_dec: store or SwiGLU epilogue only");
+  DUO_CHECK_ARG(ep.epi == EPI_STORE || ep.epi == EPI_SWIGLU || ep.epi == EPI_ADD_F32,
+                "gemm_dec: store, SwiGLU or residual-add epilogue");
   if (ep.epi == EPI_SWIGLU) {
     DUO_CHECK_ARG(n % 128 == 0, "gemm_dec: SwiGLU needs n a multiple of 128");
     DUO_CHECK_ARG(ep.c_dtype == ab_dtype, "gemm_dec: SwiGLU output is 16-bit");
   }
-  const int nb = m <= 64 ? 64 : m <= 128 ? 128 : 256;
-  CUtensorMap tw, tx;
+  if (ep.epi == EPI_ADD_F32) DUO_CHECK_ARG(ep.c_dtype == DUO_F32, "gemm_dec: the residual add is into f32");
+  const int num_k = k / DBK;
+  DecPlan p;
+  if (m > 64) plan_dec<128>(m, n, num_k, p);
+  plan_dec<64>(m, n, num_k, p);
+  // direct epilogue (TMA store of the finished tile): no K split, a store or SwiGLU, and an output whose base and
+  // rows are 16-byte aligned
+  const int es = ep.c_dtype == DUO_F32 ? 4 : 2;
+  const bool c_aligned = (reinterpret_cast<uintptr_t>(ep.c) & 15) == 0 && ((long)ep.ldc * es) % 16 == 0;
+  const int direct = p.ks == 1 && ep.epi != EPI_ADD_F32 && c_aligned;
+  CUtensorMap tw, tx, tcm;
+  std::memset(&tcm, 0, sizeof(tcm));
   DUO_TRY(make_tmap_16(&tw, w, ab_dtype, n, k, k, DBM, DBK));
-  DUO_TRY(make_tmap_16(&tx, x, ab_dtype, m, k, k, nb, DBK));
-  if (ab_dtype == DUO_F16) {
-    if (nb == 64) return dispatch_dec<64, true>(tw, tx, m, n, k, ep, st);
-    if (nb == 128) return dispatch_dec<128, true>(tw, tx, m, n, k, ep, st);
-    return dispatch_dec<256, true>(tw, tx, m, n, k, ep, st);
+  DUO_TRY(make_tmap_16(&tx, x, ab_dtype, m, k, k, p.nb, DBK));
+  if (direct) {
+    const bool sw = ep.epi == EPI_SWIGLU;
+    DUO_TRY(make_tmap_plain(&tcm, ep.c, ep.c_dtype, m, sw ? n / 2 : n, ep.ldc, p.nb, sw ? 64 : DBM));
   }
-  if (nb == 64) return dispatch_dec<64, false>(tw, tx, m, n, k, ep, st);
-  if (nb == 128) return dispatch_dec<128, false>(tw, tx, m, n, k, ep, st);
-  return dispatch_dec<256, false>(tw, tx, m, n, k, ep, st);
+  if (ab_dtype == DUO_F16) {
+    if (p.nb == 64) return dispatch_dec<64, true>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, st);
+    return dispatch_dec<128, true>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, st);
+  }
+  if (p.nb == 64) return dispatch_dec<64, false>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, st);
+  return dispatch_dec<128, false>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, st);
 }
 
 }  // namespace duo

@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
                 g *= ep.colscale[tile_n + gc + j];
                 u *= ep.colscale[tile_n + gc + 64 + j];
               }
-              v[j] = siluf_(g) * u;
+              v[j] = silu16_(g) * u;
             }
           } else {
             tc::tmem_ld32_issue(trow + c0, r0);

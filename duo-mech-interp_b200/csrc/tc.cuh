@@ -57,6 +57,25 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// 2D tiled TMA store of a shared-memory tile (rows and columns past the tensor's extent are not written); the
+// writing threads make their generic-proxy stores visible with fence_proxy_async() before the barrier that precedes
+// it.  bulk_commit() closes the group; bulk_wait_all() returns once its writes are done.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+// Prefetch a 2D tile of a tensor map into L2 (no shared-memory destination, no completion to wait for).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// returns once the source shared memory of every committed bulk store has been read
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -152,6 +171,9 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
 // elements) with a (box_cols x box_rows) box and 128-byte swizzle.  Out-of-range elements of a box read as zero.
 int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
                  int box_cols);
+// Host: the same over a 16-bit or f32 (DUO_F32) matrix without swizzle (a dense row-major box), for TMA stores.
+int make_tmap_plain(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
+                    int box_cols);
 
 // Device fault word shared by the tensor-core kernels: a bounded wait that gave up ORs a code into it.  tc_fault_ptr()
 // is its device address (kernels take it as a parameter); tc_fault_read_clear() synchronises the device, reads it

@@ -1,6 +1,7 @@
 """Op-level sweeps of the mixer kernels (BASELINE configs 2 and 3, and the projection GEMM) with CUDA-event timing.
 
     python duo-mech-interp_b200/sweep.py gemm [--m M --n N --k K] [--acc]
+    python duo-mech-interp_b200/sweep.py gemm-decode [--m M]                  # decode projection shapes, m <= 256
     python duo-mech-interp_b200/sweep.py gemv [--m M --n N --k K]             # int8 GEMV, m <= 8
     python duo-mech-interp_b200/sweep.py gdn-decode [--b B --steps S]      # config 2b
     python duo-mech-interp_b200/sweep.py gdn-prefill [--b B --t T]         # config 2a
@@ -96,6 +97,42 @@ def gemm(m, n, k, iters=10, compare=True, accumulate=False):
     return report("gemm_bf16", [m, n, k], ms, flops=2.0 * m * n * k, extra=extra)
 
 
+def gemm_decode(m=256, iters=8):
+    """The decode step's projection shapes at m rows (Qwen3.5-0.8B: DeltaNet in-projection, attention q|gate|k|v,
+    MLP gate|up + SwiGLU, and the three residual-add projections), each launch on its own weight copy so that the
+    weights stream from HBM as they do in a decode step; cuBLAS beside each on the same copies."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a16 = {kk: torch.randn(m, kk, device="cuda", generator=g).to(torch.bfloat16) for kk in (1024, 2048, 3584)}
+    for n, k, epi in [(8224, 1024, "store"), (5120, 1024, "store"), (7168, 1024, "swiglu"), (1024, 2048, "add"),
+                      (1024, 3584, "add")]:
+        ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.05).to(torch.bfloat16) for _ in range(iters)]
+        a = a16[k]
+        if epi == "add":
+            c = torch.zeros(m, n, device="cuda", dtype=torch.float32)
+            it = iter(range(1 << 30))
+            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], out=c, accumulate=True)
+            it2 = iter(range(1 << 30))
+            ref = lambda: c.add_(torch.matmul(a, ws[next(it2) % iters].T).float())
+        elif epi == "swiglu":
+            c = torch.empty(m, n // 2, device="cuda", dtype=torch.bfloat16)
+            it = iter(range(1 << 30))
+            run = lambda: ops.gemm_swiglu(a, ws[next(it) % iters])
+            it2 = iter(range(1 << 30))
+            ref = lambda: torch.matmul(a, ws[next(it2) % iters].T)
+        else:
+            c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            it = iter(range(1 << 30))
+            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], out=c)
+            it2 = iter(range(1 << 30))
+            ref = lambda: torch.matmul(a, ws[next(it2) % iters].T, out=c)
+        ms = timed(run, iters)
+        ms_ref = timed(ref, iters)
+        wbytes = n * k * 2
+        report("gemm_decode", [m, n, k], ms, flops=2.0 * m * n * k, bytes_=wbytes + m * k * 2,
+               extra={"epilogue": epi, "cublas_ms": ms_ref, "weights": "%d copies (from HBM)" % iters})
+        del ws
+
+
 def gemv(m, n, k, group=128):
     """The int8 GEMV of decode (m <= 8 rows): y = x . dequant(W)^T with int8 W [n, k] and one f32 scale per 128-group,
     bf16 x and y.  Weight copies are rotated so that every launch streams W from HBM."""
@@ -189,7 +226,7 @@ def attn_decode(b, length):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "gemv", "gdn-decode", "gdn-prefill", "attn-prefill", "attn-decode", "all"])
+    ap.add_argument("case", choices=["gemm", "gemm-decode", "gemv", "gdn-decode", "gdn-prefill", "attn-prefill", "attn-decode", "all"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=7168)
     ap.add_argument("--k", type=int, default=1024)
@@ -203,6 +240,8 @@ def main():
     a = ap.parse_args()
     if a.case == "gemm":
         gemm(a.m, a.n, a.k, a.iters, accumulate=a.acc)
+    elif a.case == "gemm-decode":
+        gemm_decode(a.m if a.m <= 256 else 256)
     elif a.case == "gemv":
         gemv(a.m if a.m <= 8 else 1, a.n, a.k)
     elif a.case == "gdn-decode":

@@ -100,8 +100,11 @@ def test_q8_gemv_streaming(ops, m, n, k, group):
 
 # small grids run the per-tile kernel (K split for the residual add); (4173, 1064, 1024) and (8269, 2088, 512) run the
 # persistent kernel with ragged edge tiles and one to four tiles per CTA
+# m <= 256 runs the decode kernel: (256, 8224, 1024) and (77, 5120, 1024) without a K split (TMA-store epilogue, a
+# ragged last weight block, a ragged row group), (100, 1024, 3584) and (256, 1024, 2048) with K split over a cluster
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (200, 300, 1024), (1024, 1024, 3584), (40, 7168, 1024),
-                                   (3000, 512, 2048), (4173, 1064, 1024), (8269, 2088, 512)])
+                                   (3000, 512, 2048), (4173, 1064, 1024), (8269, 2088, 512), (256, 8224, 1024),
+                                   (77, 5120, 1024), (100, 1024, 3584), (256, 1024, 2048)])
 def test_gemm_bf16(ops, m, n, k):
     a = (torch.randn(m, k, generator=_seed(m)) ).to(torch.bfloat16)
     b = (torch.randn(n, k, generator=_seed(n)) * 0.05).to(torch.bfloat16)
@@ -118,10 +121,12 @@ def test_gemm_bf16(ops, m, n, k):
 
 
 @pytest.mark.parametrize("m,inter,k,dt", [(37, 128, 256, torch.bfloat16), (100, 3584, 1024, torch.bfloat16),
+                                          (256, 3584, 1024, torch.bfloat16), (250, 3584, 1024, torch.float16),
                                           (1000, 3584, 1024, torch.bfloat16), (1000, 3584, 1024, torch.float16)])
 def test_gemm_swiglu(ops, m, inter, k, dt):
     """Fused gate|up GEMM + SwiGLU + neuron pushes (kernels_qwen35.js:250-280) against the oracle on the same 16-bit
-    operands; the 16-bit output rounding bounds the error (m = 1000 runs the persistent kernel)."""
+    operands; the 16-bit output rounding bounds the error (m = 1000 runs the persistent kernel, m = 250 / 256 the
+    decode kernel's TMA-store epilogue, m = 37 / 100 its cluster reduction)."""
     a = torch.randn(m, k, generator=_seed(m)).to(dt)
     wg = (torch.randn(inter, k, generator=_seed(inter)) * 0.05).to(dt)
     wu = (torch.randn(inter, k, generator=_seed(inter + 1)) * 0.05).to(dt)
