@@ -197,6 +197,11 @@ __device__ __forceinline__ float siluf_(float x) { return x / (1.f + expf(-x)); 
 // SiLU on the hardware exponential and the approximate divide (a few ulp; x -> -inf gives -0), for the SwiGLU
 // epilogues of the 16-bit GEMMs, whose result is rounded to bf16 / f16 right after
 __device__ __forceinline__ float silu16_(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+// SiLU for a result stored as T: the fast form when T is 16-bit, the accurate one for f32 (the f32 engine)
+template <typename T> __device__ __forceinline__ float silu_t(float x) {
+  if constexpr (sizeof(T) == 2) return silu16_(x);
+  else return siluf_(x);
+}
 // torch's softplus (beta 1, threshold 20) and the reference WGSL's (kernels_qwen35.js:11)
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 

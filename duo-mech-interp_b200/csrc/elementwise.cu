@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(256) swiglu_push_kernel(const T* __restrict__ 
   load8(gr + c0, g);
   load8(gr + inter + c0, u);
 #pragma unroll
-  for (int j = 0; j < 8; j++) v[j] = siluf_(g[j]) * u[j];
+  for (int j = 0; j < 8; j++) v[j] = silu_t<T>(g[j]) * u[j];
   const int r = row_base + m / t;
   for (int i = 0; i < pt.count; i++) {
     const int n = pt.neuron[i];

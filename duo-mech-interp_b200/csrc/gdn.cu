@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(256) gdn_conv_kernel(GdnConvArgs a) {
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         const float* wj = w[half * 4 + j];
-        v[half * 4 + j] = siluf_(wj[0] * xv[0][j] + wj[1] * xv[1][j] + wj[2] * xv[2][j] + wj[3] * xv[3][j]);
+        v[half * 4 + j] = silu_t<T>(wj[0] * xv[0][j] + wj[1] * xv[1][j] + wj[2] * xv[2][j] + wj[3] * xv[3][j]);
       }
     }
     if (norm) {
@@ -262,7 +262,7 @@ __global__ void __cluster_dims__(CS, 1, 1) __launch_bounds__(128) gdn_recurrent_
       if (rg == 0) {
         const float z = to_f(static_cast<const T*>(a.z)[m * a.z_stride + h * 128 + j]);
         const float hs = a.head_scale ? a.head_scale[h] : 1.f;
-        op[m * a.o_stride + h * 128 + j] = from_f<T>(o * rms * a.norm_w[j] * siluf_(z) * hs);
+        op[m * a.o_stride + h * 128 + j] = from_f<T>(o * rms * a.norm_w[j] * silu_t<T>(z) * hs);
       }
     } else if (rg == 0) {
       op[m * a.o_stride + h * 128 + j] = from_f<T>(o);
@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnCon
       const float x3 = to_f(y[yrow + ch]);
       const float4 w = *reinterpret_cast<const float4*>(ca.conv_w + (long)ch * 4);
       cs[0] = x1; cs[(long)conv_dim] = x2; cs[2L * conv_dim] = x3;
-      return siluf_(w.x * x0 + w.y * x1 + w.z * x2 + w.w * x3);
+      return silu_t<T>(w.x * x0 + w.y * x1 + w.z * x2 + w.w * x3);
     };
     const float qk = conv_ch((tid < 128 ? 0 : ca.hk * 128) + h * 128 + c);
     if (tid < 128) vs[c] = conv_ch(2 * ca.hk * 128 + h * 128 + c);
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnCon
       const float tot = red8[0] + red8[1] + red8[2] + red8[3];
       const float rms = rsqrtf(tot / 128.f + a.eps);
       const float hs = a.head_scale ? a.head_scale[h] : 1.f;
-      static_cast<T*>(a.o)[(long)b * a.o_stride + h * 128 + c] = from_f<T>(os[c] * rms * a.norm_w[c] * siluf_(z) * hs);
+      static_cast<T*>(a.o)[(long)b * a.o_stride + h * 128 + c] = from_f<T>(os[c] * rms * a.norm_w[c] * silu_t<T>(z) * hs);
     }
     __syncthreads();  // qs / ks / vs / os / red8 are rewritten by the next item
   }

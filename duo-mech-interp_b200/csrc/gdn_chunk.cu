@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(GdnScanArgs a) {
           for (int j = 0; j < 8; j++) {
             const int cc = wc + 8 * j + 2 * q4;
             float z0 = to_f(zp[m * a.z_stride + h * 128 + cc]), z1 = to_f(zp[m * a.z_stride + h * 128 + cc + 1]);
-            rz[half * 8 + j] = wm::pack_f16(siluf_(z0), siluf_(z1));
+            rz[half * 8 + j] = wm::pack_f16(silu16_(z0), silu16_(z1));
           }
         }
       }

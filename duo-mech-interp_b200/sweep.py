@@ -1,7 +1,7 @@
 """Op-level sweeps of the mixer kernels (BASELINE configs 2 and 3, and the projection GEMM) with CUDA-event timing.
 
     python duo-mech-interp_b200/sweep.py gemm [--m M --n N --k K] [--acc]
-    python duo-mech-interp_b200/sweep.py gemm-decode [--m M]                  # decode projection shapes, m <= 256
+    python duo-mech-interp_b200/sweep.py gemm-decode [--m M]                  # the projection shapes at m rows (256)
     python duo-mech-interp_b200/sweep.py gemv [--m M --n N --k K]             # int8 GEMV, m <= 8
     python duo-mech-interp_b200/sweep.py gdn-decode [--b B --steps S]      # config 2b
     python duo-mech-interp_b200/sweep.py gdn-prefill [--b B --t T]         # config 2a
@@ -98,9 +98,11 @@ def gemm(m, n, k, iters=10, compare=True, accumulate=False):
 
 
 def gemm_decode(m=256, iters=8):
-    """The decode step's projection shapes at m rows (Qwen3.5-0.8B: DeltaNet in-projection, attention q|gate|k|v,
-    MLP gate|up + SwiGLU, and the three residual-add projections), each launch on its own weight copy so that the
-    weights stream from HBM as they do in a decode step; cuBLAS beside each on the same copies."""
+    """The forward's projection shapes at m rows (Qwen3.5-0.8B: DeltaNet in-projection, attention q|gate|k|v,
+    MLP gate|up + SwiGLU, and the residual-add projections); at decode sizes (m <= 256) each launch reads its own
+    weight copy so that the weights stream from HBM as they do in a decode step; cuBLAS beside each."""
+    if m > 256:
+        iters = 3
     g = torch.Generator(device="cuda").manual_seed(0)
     a16 = {kk: torch.randn(m, kk, device="cuda", generator=g).to(torch.bfloat16) for kk in (1024, 2048, 3584)}
     for n, k, epi in [(8224, 1024, "store"), (5120, 1024, "store"), (7168, 1024, "swiglu"), (1024, 2048, "add"),
@@ -241,7 +243,7 @@ def main():
     if a.case == "gemm":
         gemm(a.m, a.n, a.k, a.iters, accumulate=a.acc)
     elif a.case == "gemm-decode":
-        gemm_decode(a.m if a.m <= 256 else 256)
+        gemm_decode(a.m if a.m != 8192 else 256)
     elif a.case == "gemv":
         gemv(a.m if a.m <= 8 else 1, a.n, a.k)
     elif a.case == "gdn-decode":
