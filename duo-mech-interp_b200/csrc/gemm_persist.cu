@@ -211,12 +211,14 @@ __global__ void __launch_bounds__(PTHREADS, 1)
         for (int c0 = 0; c0 < BN; c0 += 32) {
           uint32_t r0[32];
           tc::tmem_ld32_issue(trow + c0, r0);
+          // column scales of the chunk: one coalesced load (lane j holds column c0 + j), broadcast by shuffles
+          const float csl = ep.colscale ? (tile_n + c0 + lane < N ? ep.colscale[tile_n + c0 + lane] : 0.f) : 1.f;
           tc::tmem_ld_wait(r0);
 #pragma unroll
           for (int j = 0; j < 32; j++) {
             const int n = tile_n + c0 + j;
             float x = __uint_as_float(r0[j]);
-            if (ep.colscale) x *= n < N ? ep.colscale[n] : 0.f;
+            if (ep.colscale) x *= __shfl_sync(0xffffffffu, csl, j);
             if (n < N && x > best) {
               best = x;
               bidx = n;
@@ -245,25 +247,38 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             uint32_t r1[32];
             tc::tmem_ld32_issue(trow + gc, r0);
             tc::tmem_ld32_issue(trow + gc + 64, r1);
+            // the 32 gate and 32 up column scales, as 16-byte loads issued while the TMEM loads are in flight (a
+            // ragged last tile, N % 256 == 128, ends at column N: its scales past N read as 1)
+            float cg[32], cu[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) cg[j] = cu[j] = 1.f;
+            if (ep.colscale) {
+              const int c0g = tile_n + gc;
+              if (c0g + 96 <= N) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                  const float4 a4 = *reinterpret_cast<const float4*>(ep.colscale + c0g + j);
+                  const float4 b4 = *reinterpret_cast<const float4*>(ep.colscale + c0g + 64 + j);
+                  cg[j] = a4.x; cg[j + 1] = a4.y; cg[j + 2] = a4.z; cg[j + 3] = a4.w;
+                  cu[j] = b4.x; cu[j + 1] = b4.y; cu[j + 2] = b4.z; cu[j + 3] = b4.w;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                  if (c0g + j < N) cg[j] = ep.colscale[c0g + j];
+                  if (c0g + 64 + j < N) cu[j] = ep.colscale[c0g + 64 + j];
+                }
+              }
+            }
             tc::tmem_ld_wait(r0);
             tc::tmem_ld_wait(r1);
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-              float g = __uint_as_float(r0[j]), u = __uint_as_float(r1[j]);
-              if (ep.colscale) {
-                g *= ep.colscale[tile_n + gc + j];
-                u *= ep.colscale[tile_n + gc + 64 + j];
-              }
-              v[j] = silu16_(g) * u;
-            }
+            for (int j = 0; j < 32; j++) v[j] = silu16_(__uint_as_float(r0[j]) * cg[j]) * (__uint_as_float(r1[j]) * cu[j]);
           } else {
             tc::tmem_ld32_issue(trow + c0, r0);
             tc::tmem_ld_wait(r0);
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-              v[j] = __uint_as_float(r0[j]);
-              if (ep.colscale) v[j] *= (tile_n + c0 + j < N) ? ep.colscale[tile_n + c0 + j] : 0.f;
-            }
+            for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r0[j]);  // scaled after the transpose
           }
         }
         if (c0 + 32 >= NC) {  // every TMEM read of this tile is done: hand the accumulator back to the MMA warp
@@ -280,6 +295,12 @@ __global__ void __launch_bounds__(PTHREADS, 1)
         if (f32_out) {
           // 8 lanes x 4 columns per row, 4 rows per step; every load of the residual is issued before any store
           const int cq = (lane & 7) * 4, n = nb + cq;
+          // this lane's 4 column scales (store / residual add; SwiGLU values are scaled already)
+          float cs4[4] = {1.f, 1.f, 1.f, 1.f};
+          if (EPI != EPI_SWIGLU && ep.colscale) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) cs4[i] = n + i < ncols ? ep.colscale[n + i] : 0.f;
+          }
           float4 old[8], add[8];
 #pragma unroll
           for (int s8 = 0; s8 < 8; s8++) {
@@ -308,7 +329,8 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             const int row = s8 * 4 + (lane >> 3);
             const int m = row0 + row;
             if (m >= M || n >= ncols) continue;
-            const float4 x = *reinterpret_cast<const float4*>(wb + row * PEPI_PITCH + cq);
+            float4 x = *reinterpret_cast<const float4*>(wb + row * PEPI_PITCH + cq);
+            x.x *= cs4[0]; x.y *= cs4[1]; x.z *= cs4[2]; x.w *= cs4[3];
             float o[4] = {old[s8].x + x.x + add[s8].x, old[s8].y + x.y + add[s8].y, old[s8].z + x.z + add[s8].z,
                           old[s8].w + x.w + add[s8].w};
             if (EPI == EPI_SWIGLU && ep.push.count) {
@@ -322,6 +344,12 @@ __global__ void __launch_bounds__(PTHREADS, 1)
         } else {
           // 16-bit output: 4 lanes x 8 columns (16 bytes) per row, 8 rows per step
           const int c8 = (lane & 3) * 8, n = nb + c8;
+          // this lane's 8 column scales (store; SwiGLU values are scaled already)
+          float cs8[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+          if (EPI != EPI_SWIGLU && ep.colscale) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) cs8[i] = n + i < ncols ? ep.colscale[n + i] : 0.f;
+          }
 #pragma unroll
           for (int s4 = 0; s4 < 4; s4++) {
             const int row = s4 * 8 + (lane >> 2);
@@ -329,7 +357,8 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             if (m >= M || n >= ncols) continue;
             const float4 lo = *reinterpret_cast<const float4*>(wb + row * PEPI_PITCH + c8);
             const float4 hi = *reinterpret_cast<const float4*>(wb + row * PEPI_PITCH + c8 + 4);
-            float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            float x[8] = {lo.x * cs8[0], lo.y * cs8[1], lo.z * cs8[2], lo.w * cs8[3],
+                          hi.x * cs8[4], hi.y * cs8[5], hi.z * cs8[6], hi.w * cs8[7]};
             if (EPI == EPI_SWIGLU && ep.push.count) {
               const int r = ep.row_base + m / ep.t;
               for (int i = 0; i < 8 && n + i < ncols; i++) x[i] = push_apply(ep.push, r, n + i, x[i]);

@@ -97,7 +97,7 @@ def gemm(m, n, k, iters=10, compare=True, accumulate=False):
     return report("gemm_bf16", [m, n, k], ms, flops=2.0 * m * n * k, extra=extra)
 
 
-def gemm_decode(m=256, iters=8):
+def gemm_decode(m=256, iters=8, colscale=False, intw=False):
     """The forward's projection shapes at m rows (Qwen3.5-0.8B: DeltaNet in-projection, attention q|gate|k|v,
     MLP gate|up + SwiGLU, and the residual-add projections); at decode sizes (m <= 256) each launch reads its own
     weight copy so that the weights stream from HBM as they do in a decode step; cuBLAS beside each."""
@@ -107,31 +107,36 @@ def gemm_decode(m=256, iters=8):
     a16 = {kk: torch.randn(m, kk, device="cuda", generator=g).to(torch.bfloat16) for kk in (1024, 2048, 3584)}
     for n, k, epi in [(8224, 1024, "store"), (5120, 1024, "store"), (7168, 1024, "swiglu"), (1024, 2048, "add"),
                       (1024, 3584, "add")]:
-        ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.05).to(torch.bfloat16) for _ in range(iters)]
+        if intw:  # int8-valued weights, as the engine's packs hold them (the row scale goes to col_scale)
+            ws = [torch.randint(-127, 128, (n, k), device="cuda", generator=g).to(torch.bfloat16) for _ in range(iters)]
+        else:
+            ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.05).to(torch.bfloat16) for _ in range(iters)]
+        cs = (torch.rand(n, device="cuda", generator=g) * 1e-3 + 1e-4) if colscale else None
         a = a16[k]
         if epi == "add":
             c = torch.zeros(m, n, device="cuda", dtype=torch.float32)
             it = iter(range(1 << 30))
-            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], out=c, accumulate=True)
+            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], col_scale=cs, out=c, accumulate=True)
             it2 = iter(range(1 << 30))
             ref = lambda: c.add_(torch.matmul(a, ws[next(it2) % iters].T).float())
         elif epi == "swiglu":
             c = torch.empty(m, n // 2, device="cuda", dtype=torch.bfloat16)
             it = iter(range(1 << 30))
-            run = lambda: ops.gemm_swiglu(a, ws[next(it) % iters])
+            run = lambda: ops.gemm_swiglu(a, ws[next(it) % iters], col_scale=cs)
             it2 = iter(range(1 << 30))
             ref = lambda: torch.matmul(a, ws[next(it2) % iters].T)
         else:
             c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
             it = iter(range(1 << 30))
-            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], out=c)
+            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], col_scale=cs, out=c)
             it2 = iter(range(1 << 30))
             ref = lambda: torch.matmul(a, ws[next(it2) % iters].T, out=c)
         ms = timed(run, iters)
         ms_ref = timed(ref, iters)
         wbytes = n * k * 2
         report("gemm_decode", [m, n, k], ms, flops=2.0 * m * n * k, bytes_=wbytes + m * k * 2,
-               extra={"epilogue": epi, "cublas_ms": ms_ref, "weights": "%d copies (from HBM)" % iters})
+               extra={"epilogue": epi, "cublas_ms": ms_ref, "weights": "%d copies" % iters,
+                      "col_scale": colscale, "int_weights": intw})
         del ws
 
 
@@ -239,11 +244,13 @@ def main():
     ap.add_argument("--fn", default="gdn_chunk")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--acc", action="store_true", help="gemm: residual-add epilogue into f32")
+    ap.add_argument("--colscale", action="store_true", help="gemm-decode: per-row weight scale in the epilogue")
+    ap.add_argument("--intw", action="store_true", help="gemm-decode: int8-valued weights (the engine's packs)")
     a = ap.parse_args()
     if a.case == "gemm":
         gemm(a.m, a.n, a.k, a.iters, accumulate=a.acc)
     elif a.case == "gemm-decode":
-        gemm_decode(a.m if a.m != 8192 else 256)
+        gemm_decode(a.m if a.m != 8192 else 256, colscale=a.colscale, intw=a.intw)
     elif a.case == "gemv":
         gemv(a.m if a.m <= 8 else 1, a.n, a.k)
     elif a.case == "gdn-decode":
