@@ -346,30 +346,55 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnCon
   // which never touches the recurrent state) finishes; the conv inputs, conv state and outputs wait for it.
   pdl_enter();
 
+  // The conv inputs of an item (its channels' carried conv state and new input, z, the gate inputs) are loaded one
+  // item ahead, so their latency hides behind the previous item's state slices.  Items own disjoint channels, and
+  // the projection output is read only after the programmatic-launch wait.
+  const int c = tid & 127;
+  struct ConvIn {
+    float xq[4], xv[4], z, yb, ya;
+  };
+  auto fetch = [&](int j, ConvIn& in) {
+    if (j >= my_items) return;
+    const int item = blockIdx.x + j * gridDim.x;
+    const int b = item / H, h = item % H;
+    const long yrow = (long)b * ca.w;
+    const float* cs = ca.conv_state + ((long)(a.state_row0 + b) * 3) * conv_dim;
+    const int chq = (tid < 128 ? 0 : ca.hk * 128) + h * 128 + c;
+    in.xq[0] = cs[chq]; in.xq[1] = cs[conv_dim + chq]; in.xq[2] = cs[2L * conv_dim + chq];
+    in.xq[3] = to_f(y[yrow + chq]);
+    if (tid < 128) {
+      const int chv = 2 * ca.hk * 128 + h * 128 + c;
+      in.xv[0] = cs[chv]; in.xv[1] = cs[conv_dim + chv]; in.xv[2] = cs[2L * conv_dim + chv];
+      in.xv[3] = to_f(y[yrow + chv]);
+      in.z = to_f(static_cast<const T*>(a.z)[(long)b * a.z_stride + h * 128 + c]);
+    }
+    const long gb = yrow + conv_dim + ca.hv * 128;
+    in.yb = to_f(y[gb + h]);
+    in.ya = to_f(y[gb + ca.hv + h]);
+  };
+  ConvIn nxt{};
+  fetch(0, nxt);
+
   for (int j = 0; j < my_items; j++) {
     const int item = blockIdx.x + j * gridDim.x;
     const int b = item / H, h = item % H;
     const int R = a.state_row0 + b;
-    const long yrow = (long)b * ca.w;
+    const ConvIn cur = nxt;
+    fetch(j + 1, nxt);
     // 1. conv + SiLU of the head's q (threads 0..127, also v) and k (128..255) channels, shifting their conv state
-    const int c = tid & 127;
-    float z = 0.f;
-    if (tid < 128) z = to_f(static_cast<const T*>(a.z)[(long)b * a.z_stride + h * 128 + c]);
-    auto conv_ch = [&](int ch) {
+    const float z = cur.z;
+    auto conv_ch = [&](int ch, const float (&x)[4]) {
       float* cs = ca.conv_state + ((long)R * 3) * conv_dim + ch;
-      const float x0 = cs[0], x1 = cs[(long)conv_dim], x2 = cs[2L * conv_dim];
-      const float x3 = to_f(y[yrow + ch]);
       const float4 w = *reinterpret_cast<const float4*>(ca.conv_w + (long)ch * 4);
-      cs[0] = x1; cs[(long)conv_dim] = x2; cs[2L * conv_dim] = x3;
-      return silu_t<T>(w.x * x0 + w.y * x1 + w.z * x2 + w.w * x3);
+      cs[0] = x[1]; cs[(long)conv_dim] = x[2]; cs[2L * conv_dim] = x[3];
+      return silu_t<T>(w.x * x[0] + w.y * x[1] + w.z * x[2] + w.w * x[3]);
     };
-    const float qk = conv_ch((tid < 128 ? 0 : ca.hk * 128) + h * 128 + c);
-    if (tid < 128) vs[c] = conv_ch(2 * ca.hk * 128 + h * 128 + c);
+    const float qk = conv_ch((tid < 128 ? 0 : ca.hk * 128) + h * 128 + c, cur.xq);
+    if (tid < 128) vs[c] = conv_ch(2 * ca.hk * 128 + h * 128 + c, cur.xv);
     const float ssq = warp_sum(qk * qk);
     if (lane == 0) red8[warp] = ssq;
-    const long gb = yrow + conv_dim + ca.hv * 128;
-    const float beta = sigmoidf_(to_f(y[gb + h]));
-    const float gdec = expf(-expf(ca.a_log[h]) * softplusf_(to_f(y[gb + ca.hv + h]) + ca.dt_bias[h]));
+    const float beta = sigmoidf_(cur.yb);
+    const float gdec = expf(-expf(ca.a_log[h]) * softplusf_(cur.ya + ca.dt_bias[h]));
     __syncthreads();
     {
       const int w0 = tid < 128 ? 0 : 4;
