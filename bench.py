@@ -35,7 +35,7 @@ def parse():
     ap.add_argument("--rows", type=int, default=256)
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--decode", type=int, default=512)
-    ap.add_argument("--max-tokens", type=int, default=65536, help="tokens per prefill forward call")
+    ap.add_argument("--max-tokens", type=int, default=131072, help="tokens per prefill forward call")
     ap.add_argument("--vec-layer", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
