@@ -6,6 +6,7 @@
 #include <cooperative_groups.h>
 
 #include "kernels.cuh"
+#include "tc.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -164,10 +165,177 @@ __global__ void __launch_bounds__(256) gdn_conv_kernel(GdnConvArgs a) {
   }
 }
 
+// TMA-fed form of the conv prologue (16-bit projections whose rows are 16-byte aligned).  Block = (128-channel group,
+// row, CONV_TPC consecutive 64-token tiles).  Thread 0 streams the tiles' raw [64 tokens][128 channels] inputs into a
+// CONV_NS-deep shared-memory ring by 2D TMA loads, so two tiles are in flight while one is processed; a tile's 3-token
+// halo is the previous tile's last 3 rows, kept in f32 (the block's first tile takes it from the carried conv state
+// or from the projection).  Per tile the arithmetic is that of gdn_conv_kernel: half-warp h takes tokens h, h + 16, ..,
+// thread c channels 4c .. 4c + 3 and 64 + 4c .. 64 + 4c + 3.
+constexpr int CONV_NS = 3, CONV_TPC = 8;
+constexpr int CONV_TMA_SMEM = 1024 + CONV_NS * CONV_TT * 128 * 2 + 3 * 128 * 4 + 64;
+
+template <typename T>
+__global__ void __launch_bounds__(256) gdn_conv_tma_kernel(const __grid_constant__ CUtensorMap tmy, GdnConvArgs a,
+                                                           unsigned* fault) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  T* ring = reinterpret_cast<T*>(smem);                                                // [NS][64][128]
+  float* halo = reinterpret_cast<float*>(smem + CONV_NS * CONV_TT * 128 * sizeof(T));  // [3][128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(halo + 3 * 128);                        // [NS]
+  constexpr uint32_t TILE_BYTES = CONV_TT * 128 * sizeof(T);
+  const int cgp = blockIdx.x, rr = blockIdx.y;
+  const int tiles = (a.t + CONV_TT - 1) / CONV_TT;
+  const int j0 = blockIdx.z * CONV_TPC, j1 = min(tiles, j0 + CONV_TPC);
+  const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
+  const int tid = threadIdx.x, c = tid & 15, hw = tid >> 4;
+  const int R = a.row_base + rr;
+  const long m0 = (long)rr * a.t;
+  const T* y = static_cast<const T*>(a.y);
+  float* st = a.conv_state + ((long)R * (CONV_KS - 1)) * conv_dim + cgp * 128;  // st[j * conv_dim + ch]
+
+  if (tid == 0) {
+    for (int s2 = 0; s2 < CONV_NS; s2++) tc::mbar_init(&full[s2], 1);
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmy);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0) {
+    for (int s2 = 0; s2 < CONV_NS && j0 + s2 < j1; s2++) {
+      tc::mbar_arrive_expect_tx(&full[s2], TILE_BYTES);
+      tc::tma_load_2d(ring + s2 * CONV_TT * 128, &tmy, cgp * 128, (int)(m0 + (long)(j0 + s2) * CONV_TT), &full[s2]);
+    }
+  }
+  // halo of the first tile; the new conv state = the last KS-1 inputs of (old state ++ this call's inputs), written by
+  // the block of tile 0 (the only reader of the old state) once every read of it is done
+  float ns[CONV_KS - 1];
+  if (tid < 128) {
+#pragma unroll
+    for (int d = 0; d < CONV_KS - 1; d++) {
+      const int tt = j0 * CONV_TT - (CONV_KS - 1) + d;
+      halo[d * 128 + tid] = tt < 0 ? st[(long)((CONV_KS - 1) + tt) * conv_dim + tid]
+                                   : to_f(y[(m0 + tt) * a.w + cgp * 128 + tid]);
+    }
+    if (blockIdx.z == 0) {
+#pragma unroll
+      for (int d = 0; d < CONV_KS - 1; d++) {
+        const int idx = a.t + d;  // index into old ++ new
+        ns[d] = idx < CONV_KS - 1 ? st[(long)idx * conv_dim + tid]
+                                  : to_f(y[(m0 + idx - (CONV_KS - 1)) * a.w + cgp * 128 + tid]);
+      }
+    }
+  }
+  __syncthreads();
+  if (blockIdx.z == 0 && tid < 128) {
+#pragma unroll
+    for (int d = 0; d < CONV_KS - 1; d++) st[(long)d * conv_dim + tid] = ns[d];
+  }
+
+  const bool norm = cgp < 2 * a.hk;  // q and k heads are l2-normalised; v heads pass through
+  float w[8][CONV_KS];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int ch = cgp * 128 + (j < 4 ? 4 * c + j : 64 + 4 * c + j - 4);
+    const float4 ww = *reinterpret_cast<const float4*>(a.conv_w + (long)ch * CONV_KS);
+    w[j][0] = ww.x; w[j][1] = ww.y; w[j][2] = ww.z; w[j][3] = ww.w;
+  }
+  T* out = static_cast<T*>(a.qkv_out);
+  for (int j = j0; j < j1; j++) {
+    const int s2 = (j - j0) % CONV_NS;
+    const uint32_t ph = (uint32_t)(((j - j0) / CONV_NS) & 1);
+    const bool ok = tc::mbar_wait(&full[s2], ph);
+    if (__syncthreads_or(!ok)) {  // a load that never landed: give up (the fault word says so)
+      if (tid == 0) atomicOr(fault, 16u);
+      return;
+    }
+    const T* tile = ring + s2 * CONV_TT * 128;
+    const int t0 = j * CONV_TT, tn = min(CONV_TT, a.t - t0);
+    for (int i = hw; i < tn; i += 16) {
+      float v[8];
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+        const int col = half * 64 + 4 * c;
+        float x[CONV_KS][4];
+#pragma unroll
+        for (int d = 0; d < CONV_KS; d++) {
+          const int row = i - (CONV_KS - 1) + d;
+          if (row >= 0) {
+            const uint2 u = *reinterpret_cast<const uint2*>(tile + row * 128 + col);
+            const T* hh = reinterpret_cast<const T*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; e++) x[d][e] = to_f(hh[e]);
+          } else {
+            const float4 f = *reinterpret_cast<const float4*>(halo + (row + CONV_KS - 1) * 128 + col);
+            x[d][0] = f.x; x[d][1] = f.y; x[d][2] = f.z; x[d][3] = f.w;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float* wj = w[half * 4 + e];
+          v[half * 4 + e] = silu_t<T>(wj[0] * x[0][e] + wj[1] * x[1][e] + wj[2] * x[2][e] + wj[3] * x[3][e]);
+        }
+      }
+      if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss += v[e] * v[e];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = rsqrtf(ss + 1e-6f);
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] *= inv;
+      }
+      T* o = out + (m0 + t0 + i) * conv_dim + cgp * 128;
+      store4<T>(o + 4 * c, v);
+      store4<T>(o + 64 + 4 * c, v + 4);
+    }
+    if (!norm && tid < tn) {
+      const int hh = cgp - 2 * a.hk;
+      const long m = m0 + t0 + tid;
+      const long base = m * a.w + conv_dim + a.hv * a.dv;
+      a.beta_out[m * a.hv + hh] = sigmoidf_(to_f(y[base + hh]));
+      a.g_out[m * a.hv + hh] = -expf(a.a_log[hh]) * softplusf_(to_f(y[base + a.hv + hh]) + a.dt_bias[hh]);
+    }
+    __syncthreads();  // every read of this slot and of the halo is done
+    if (j + 1 < j1 && tid < 128) {
+#pragma unroll
+      for (int d = 0; d < CONV_KS - 1; d++) halo[d * 128 + tid] = to_f(tile[(CONV_TT - (CONV_KS - 1) + d) * 128 + tid]);
+    }
+    __syncthreads();  // the next tile's halo is in place; this slot may be refilled
+    if (tid == 0 && j + CONV_NS < j1) {
+      tc::fence_proxy_async();
+      tc::mbar_arrive_expect_tx(&full[s2], TILE_BYTES);
+      tc::tma_load_2d(ring + s2 * CONV_TT * 128, &tmy, cgp * 128, (int)(m0 + (long)(j + CONV_NS) * CONV_TT), &full[s2]);
+    }
+  }
+}
+
 int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
   if (a.rows == 0 || a.t == 0) return DUO_OK;
   if (a.dk != 128 || a.dv != 128 || a.ks != CONV_KS) return fail(DUO_EINVAL, "gdn_conv: needs dk = dv = 128, ks = 4");
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
+  if (dtype != DUO_F32 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.w % 8 == 0) {
+    CUtensorMap tmy;
+    DUO_TRY(make_tmap_plain(&tmy, a.y, dtype, (long)a.rows * a.t, a.w, a.w, CONV_TT, 128));
+    unsigned* fault = tc_fault_ptr();
+    if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
+    dim3 grid(conv_dim / 128, a.rows, cdiv(cdiv(a.t, CONV_TT), CONV_TPC));
+    return with_act(dtype, [&](auto tag) -> int {
+      using T = decltype(tag);
+      if constexpr (sizeof(T) == 2) {
+        static bool attr_set = false;
+        if (!attr_set) {
+          DUO_CUDA_TRY(cudaFuncSetAttribute(gdn_conv_tma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            CONV_TMA_SMEM));
+          attr_set = true;
+        }
+        DUO_CUDA_TRY(::duo::launch_kernel(gdn_conv_tma_kernel<T>, grid, 256, CONV_TMA_SMEM, st, tmy, a, fault));
+        DUO_LAUNCH_CHECK("gdn_conv_tma_kernel");
+      }
+      return DUO_OK;
+    });
+  }
   dim3 grid(conv_dim / 128, a.rows, cdiv(a.t, CONV_TT));
   return with_act(dtype, [&](auto tag) -> int {
     DUO_CUDA_TRY(::duo::launch_kernel(gdn_conv_kernel<decltype(tag)>, grid, 256, 0, st, a));
