@@ -19,9 +19,9 @@ namespace cg = cooperative_groups;
 __device__ unsigned g_tc_fault;
 
 // ---------------------------------------------------------------------------------------------------------------
-// tcgen05 GEMM for small grids (decode-sized M): one CTA per 128 x BN tile (x a K range), K step 64 (one 128-byte
-// swizzle row of 16-bit values), a ~96 KB TMA ring so that two CTAs share an SM.  Large grids go to the persistent
-// kernel (gemm_persist.cu).  Warp 0: TMA producer (one lane).  Warp 1: TMEM allocator and MMA issuer (one lane).
+// tcgen05 GEMM for small grids with more than 256 rows (decode-sized row counts go to gemm_dec.cu): one CTA per
+// 128 x BN tile (x a K range), K step 64 (one 128-byte swizzle row of 16-bit values), a ~96 KB TMA ring so that two
+// CTAs share an SM.  Large grids go to the persistent kernel (gemm_persist.cu).  Warp 0: TMA producer (one lane).  Warp 1: TMEM allocator and MMA issuer (one lane).
 // Warps 2-5: epilogue, one accumulator row (TMEM lane) per thread, read 32 columns at a time.
 
 constexpr int TC_BM = 128, TC_BK = 64, TC_THREADS = 192;

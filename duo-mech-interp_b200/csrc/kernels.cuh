@@ -52,7 +52,8 @@ struct GemmEpiArgs {
                                 // tiles may be fetched before the programmatic-launch wait
 };
 
-// decode-sized tcgen05 GEMM (m <= 256 rows; weights on the MMA's M side, K split over a cluster): y = x . w^T
+// decode-sized tcgen05 GEMM (m <= 256 rows; weights on the MMA's M side, grid = weight blocks x row groups x K
+// slices, K split over a cluster where the SMs need it): y = x . w^T
 int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dtype, const GemmEpiArgs& ep,
                     cudaStream_t st);
 
