@@ -315,7 +315,8 @@ int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
   if (a.rows == 0 || a.t == 0) return DUO_OK;
   if (a.dk != 128 || a.dv != 128 || a.ks != CONV_KS) return fail(DUO_EINVAL, "gdn_conv: needs dk = dv = 128, ks = 4");
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
-  if (dtype != DUO_F32 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.w % 8 == 0) {
+  // the TMA-fed form for 16-bit projections whose rows are 16-byte aligned and at least one box (64 token rows) tall
+  if (dtype != DUO_F32 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.w % 8 == 0 && (long)a.rows * a.t >= CONV_TT) {
     CUtensorMap tmy;
     DUO_TRY(make_tmap_plain(&tmy, a.y, dtype, (long)a.rows * a.t, a.w, a.w, CONV_TT, 128));
     unsigned* fault = tc_fault_ptr();
