@@ -1,7 +1,9 @@
 """Op-level sweeps of the mixer kernels (BASELINE configs 2 and 3, and the projection GEMM) with CUDA-event timing.
 
     python duo-mech-interp_b200/sweep.py gemm [--m M --n N --k K] [--acc]
-    python duo-mech-interp_b200/sweep.py gemm-decode [--m M]                  # the projection shapes at m rows (256)
+    python duo-mech-interp_b200/sweep.py gemm-decode [--m M] [--colscale] [--intw]
+                                           # the projection shapes at m rows (256), optionally with per-row weight
+                                           # scales in the epilogue and int8-valued weights as the engine runs them
     python duo-mech-interp_b200/sweep.py gemv [--m M --n N --k K]             # int8 GEMV, m <= 8
     python duo-mech-interp_b200/sweep.py gdn-decode [--b B --steps S]      # config 2b
     python duo-mech-interp_b200/sweep.py gdn-prefill [--b B --t T]         # config 2a
