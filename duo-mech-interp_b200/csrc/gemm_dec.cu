@@ -522,11 +522,11 @@ int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dt
   DecPlan p;
   if (m > 64) plan_dec<128>(m, n, num_k, p);
   plan_dec<64>(m, n, num_k, p);
-  // direct epilogue (TMA store of the finished tile): no K split, a store or SwiGLU, and an output whose base and
-  // rows are 16-byte aligned
+  // direct epilogue (TMA store of the finished tile): no K split, a store or SwiGLU, an output whose base and rows
+  // are 16-byte aligned, and at least one row group of rows (the store box is never taller than the whole output)
   const int es = ep.c_dtype == DUO_F32 ? 4 : 2;
   const bool c_aligned = (reinterpret_cast<uintptr_t>(ep.c) & 15) == 0 && ((long)ep.ldc * es) % 16 == 0;
-  const int direct = p.ks == 1 && ep.epi != EPI_ADD_F32 && c_aligned;
+  const int direct = p.ks == 1 && ep.epi != EPI_ADD_F32 && c_aligned && m >= p.nb;
   CUtensorMap tw, tx, tcm;
   std::memset(&tcm, 0, sizeof(tcm));
   DUO_TRY(make_tmap_16(&tw, w, ab_dtype, n, k, k, DBM, DBK));
