@@ -54,6 +54,38 @@ def test_bad_arguments_return_status_and_message(L):
     assert st == L.DUO_EINVAL
 
 
+def test_projection_and_scan_arguments_are_checked_first(L):
+    """Shape, dtype and table checks of the projection and scan entry points return a status before any device work."""
+    lib = L.lib()
+    # fused gate|up + SwiGLU: inter a multiple of 64, ldo >= inter, a push table when there are pushes, rows in it
+    st = lib.duo_gemm_swiglu(None, 4, 64, None, 100, L.DUO_BF16, None, None, 100, None, None, None, 0, 0, 1, 0, None)
+    assert st == L.DUO_EINVAL and b"64" in lib.duo_last_error()
+    st = lib.duo_gemm_swiglu(None, 4, 64, None, 128, L.DUO_F32, None, None, 128, None, None, None, 0, 0, 1, 0, None)
+    assert st == L.DUO_EINVAL and b"bf16 or f16" in lib.duo_last_error()
+    st = lib.duo_gemm_swiglu(None, 4, 64, None, 128, L.DUO_BF16, None, None, 128, None, None, None, 0, 0, 1, 0, None)
+    assert st == L.DUO_EINVAL and b"null" in lib.duo_last_error()
+    sentinel = C.c_void_p(16)  # never dereferenced: the checks fail first
+    st = lib.duo_gemm_swiglu(sentinel, 4, 64, sentinel, 128, L.DUO_BF16, None, sentinel, 64, None, None, None, 0, 0,
+                             1, 0, None)
+    assert st == L.DUO_EINVAL and b"ldo" in lib.duo_last_error()
+    st = lib.duo_gemm_swiglu(sentinel, 4, 64, sentinel, 128, L.DUO_BF16, None, sentinel, 128, None, None, None, 2, 4,
+                             1, 0, None)
+    assert st == L.DUO_EINVAL and b"push table" in lib.duo_last_error()
+    st = lib.duo_gemm_swiglu(sentinel, 4, 64, sentinel, 128, L.DUO_BF16, None, sentinel, 128, sentinel, sentinel,
+                             sentinel, 1, 2, 1, 0, None)  # 4 rows of A, 2 rows in the push table
+    assert st == L.DUO_EINVAL and b"push table" in lib.duo_last_error()
+    # the residual-add GEMM accumulates into f32 only
+    st = lib.duo_gemm_bf16(sentinel, 4, 64, sentinel, 4, None, sentinel, L.DUO_BF16, 4, 1, None)
+    assert st == L.DUO_EINVAL and b"f32" in lib.duo_last_error()
+    # chunked scan: head dims 128, one dtype for q/k/v/o
+    st = lib.duo_gdn_chunk_fwd(None, None, None, L.DUO_BF16, None, None, None, None, L.DUO_BF16, 1, 64, 1, 64, 128, 1,
+                               None)
+    assert st == L.DUO_EINVAL and b"128" in lib.duo_last_error()
+    st = lib.duo_gdn_chunk_fwd(None, None, None, L.DUO_BF16, None, None, None, None, L.DUO_F32, 1, 64, 1, 128, 128, 1,
+                               None)
+    assert st == L.DUO_EINVAL and b"dtype" in lib.duo_last_error()
+
+
 def test_engine_rejects_bad_config_and_null_handle(L):
     lib = L.lib()
     full = (C.c_uint8 * 4)(0, 0, 0, 1)
