@@ -373,11 +373,7 @@ static int run_attention(const AttnArgs& a, cudaStream_t st) {
     return DUO_OK;
   }
   constexpr size_t smem = sizeof(float) * (AP_BQ * (AP_HD + 1) + AP_BK * (AP_HD + 1) + AP_BK * AP_HD + AP_BQ * (AP_BK + 1));
-  static bool attr = false;
-  if (!attr) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr = true;
-  }
+  DUO_TRY(ensure_smem_attr(attn_prefill_kernel<T>, (int)smem));
   DUO_CUDA_TRY(::duo::launch_kernel(attn_prefill_kernel<T>, dim3(cdiv(a.t, AP_BQ), a.nh, a.b), 256, smem, st, a));
   DUO_LAUNCH_CHECK("attn_prefill_kernel");
   return DUO_OK;

@@ -216,12 +216,7 @@ int launch_attn_decode_mma(const AttnArgs& a, int dtype, cudaStream_t st) {
   auto run = [&](auto rep_c, auto t_c) -> int {
     constexpr int RP = decltype(rep_c)::value;
     using T16 = decltype(t_c);
-    static bool attr = false;
-    if (!attr) {
-      DUO_CUDA_TRY(cudaFuncSetAttribute(attn_decode_mma_kernel<RP, T16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        kDecodeSmem));
-      attr = true;
-    }
+    DUO_TRY(ensure_smem_attr(attn_decode_mma_kernel<RP, T16>, kDecodeSmem));
     DUO_CUDA_TRY(::duo::launch_kernel(attn_decode_mma_kernel<RP, T16>, dim3(ns, a.nkv, a.b), 128, kDecodeSmem, st, a, ns, split_len));
     DUO_LAUNCH_CHECK("attn_decode_mma_kernel");
     return DUO_OK;

@@ -60,7 +60,7 @@ extern "C" int duo_attention_noalloc(const void* q, const void* kc, const void* 
                                      const void* gate, int gate_stride, void* o, int dtype, int b, int t, int nh,
                                      int nkv, int hd, int max_len, float scale, duo_stream stream) {
   DUO_CHECK_ARG(b >= 0 && t >= 0 && nh > 0 && nkv > 0 && max_len > 0, "attention_noalloc: bad shape");
-  DUO_CHECK_ARG(valid_act(dtype), "attention_noalloc: dtype must be f32 or bf16");
+  DUO_CHECK_ARG(valid_act(dtype), "attention_noalloc: dtype must be f32, bf16 or f16");
   DUO_CHECK_ARG(b == 0 || t == 0 || (q && kc && vc && start && o), "attention_noalloc: null pointer");
   AttnArgs a{};
   a.q = q; a.kc = kc; a.vc = vc; a.cache_row0 = 0; a.start = start; a.len = nullptr;

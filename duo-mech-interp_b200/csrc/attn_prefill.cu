@@ -184,11 +184,7 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_mma_kernel(AttnArgs a) {
 template <int REP, typename T16>
 static int run_prefill_mma(const AttnArgs& a, cudaStream_t st) {
   constexpr int smem = (128 + 4 * BKEY) * PQ * 2;
-  static bool attr = false;
-  if (!attr) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_mma_kernel<REP, T16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  DUO_TRY(ensure_smem_attr(attn_prefill_mma_kernel<REP, T16>, smem));
   DUO_CUDA_TRY(::duo::launch_kernel(attn_prefill_mma_kernel<REP, T16>, dim3(cdiv(a.t, 128 / REP), a.nkv, a.b), 256, smem, st, a));
   DUO_LAUNCH_CHECK("attn_prefill_mma_kernel");
   return DUO_OK;

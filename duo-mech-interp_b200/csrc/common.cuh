@@ -96,8 +96,14 @@ template <typename F> int with_act(int dt, F&& f) {
   }
 }
 
-// number of SMs of the current device (cached per process; one device per process in this library's model)
+// number of SMs of the current device (looked up once per device)
 int sm_count();
+
+// cudaFuncAttributeMaxDynamicSharedMemorySize = bytes for `func` on the current device, set once per (device, func)
+int ensure_smem_attr_fn(const void* func, int bytes);
+template <typename K> int ensure_smem_attr(K* kernel, int bytes) {
+  return ensure_smem_attr_fn(reinterpret_cast<const void*>(kernel), bytes);
+}
 
 // ---------------------------------------------------------------------------------------------------------------
 // device helpers

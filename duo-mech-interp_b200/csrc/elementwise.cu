@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tc.cuh"
 
 namespace duo {
 
@@ -159,8 +160,15 @@ int launch_argmax(const float* logits, int m, int v, int32_t* out, cudaStream_t 
 // ---------------------------------------------------------------------------------------------------------------
 // bookkeeping: last token of each row -> last[row], row lengths += t
 
-__global__ void copy_last_kernel(const float* __restrict__ x, int h, int t, int row_base, float* __restrict__ last) {
+// The last kernel of a forward also copies the fault word of the bounded-wait kernels into its host-mapped mirror
+// (plain stores to pinned memory), where the engine's next call sees it without synchronising.
+__global__ void copy_last_kernel(const float* __restrict__ x, int h, int t, int row_base, float* __restrict__ last,
+                                 const unsigned* fault, unsigned* mirror) {
   pdl_enter();
+  if (blockIdx.x == 0 && threadIdx.x == 0 && fault && mirror) {
+    const unsigned f = *reinterpret_cast<const volatile unsigned*>(fault);
+    if (f) *reinterpret_cast<volatile unsigned*>(mirror) = f;
+  }
   const int r = blockIdx.x;
   const float* src = x + ((long)r * t + t - 1) * h;
   float* dst = last + (long)(row_base + r) * h;
@@ -177,7 +185,9 @@ __global__ void advance_len_kernel(int32_t* len, int row_base, int rows, int t) 
 int launch_finish_rows(const float* x, int h, int t, int row_base, int rows, float* last, int32_t* len,
                        cudaStream_t st) {
   if (rows == 0) return DUO_OK;
-  DUO_CUDA_TRY(::duo::launch_kernel(copy_last_kernel, rows, 256, 0, st, x, h, t, row_base, last));
+  const unsigned* fault = tc_fault_ptr();
+  unsigned* mirror = fault_mirror_dev();
+  DUO_CUDA_TRY(::duo::launch_kernel(copy_last_kernel, rows, 256, 0, st, x, h, t, row_base, last, fault, mirror));
   DUO_LAUNCH_CHECK("copy_last_kernel");
   DUO_CUDA_TRY(::duo::launch_kernel(advance_len_kernel, cdiv(rows, 256), 256, 0, st, len, row_base, rows, t));
   DUO_LAUNCH_CHECK("advance_len_kernel");
@@ -210,6 +220,6 @@ extern "C" int duo_rmsnorm(const float* x, int m, int d, const float* w, float e
                            duo_stream stream) {
   DUO_CHECK_ARG(m >= 0 && d > 0 && d % 8 == 0, "rmsnorm: d must be a positive multiple of 8");
   DUO_CHECK_ARG(m == 0 || (x && w && y), "rmsnorm: null pointer");
-  DUO_CHECK_ARG(valid_act(y_dtype), "rmsnorm: y dtype must be f32 or bf16");
+  DUO_CHECK_ARG(valid_act(y_dtype), "rmsnorm: y dtype must be f32, bf16 or f16");
   return launch_rmsnorm(x, m, d, w, eps, offset, y, y_dtype, as_stream(stream));
 }

@@ -363,6 +363,10 @@ extern "C" int duo_engine_create(const duo_config* cfg, duo_engine** out) {
                 "engine_create: group must be 0 or a multiple of 16 dividing hidden and inter");
   DUO_CHECK_ARG(valid_act(c.act_dtype), "engine_create: act_dtype must be DUO_F32, DUO_BF16 or DUO_F16");
   DUO_CHECK_ARG(c.full_attention_host, "engine_create: null layer type array");
+  {
+    const int fs = fault_mirror_init();  // the host-mapped fault word the forward's last kernel writes
+    if (fs != DUO_OK) return fs;
+  }
   duo_engine* e = new duo_engine();
   e->cfg = c;
   e->full.assign(c.full_attention_host, c.full_attention_host + c.layers);
@@ -585,6 +589,7 @@ extern "C" int duo_engine_set_pushes(duo_engine* e, int layer, int n, const int3
 
 extern "C" int duo_engine_forward_device(duo_engine* e, const int32_t* ids, int row_base, int rows, int t,
                                          int vec_layer, duo_stream stream) {
+  DUO_TRY(fault_gate("forward"));
   DUO_TRY(check_engine(e, true, true));
   DUO_CHECK_ARG(ids, "forward: null ids");
   DUO_CHECK_ARG(vec_layer >= -1 && vec_layer < e->cfg.layers, "forward: vec_layer out of range");
@@ -596,6 +601,7 @@ extern "C" int duo_engine_forward_device(duo_engine* e, const int32_t* ids, int 
 
 extern "C" int duo_engine_forward(duo_engine* e, const int32_t* ids_host, int row_base, int rows, int t,
                                   int vec_layer, duo_stream stream) {
+  DUO_TRY(fault_gate("forward"));
   DUO_TRY(check_engine(e, true, true));
   DUO_CHECK_ARG(ids_host, "forward: null ids");
   DUO_TRY(check_rows(e, row_base, rows, t));
@@ -604,12 +610,14 @@ extern "C" int duo_engine_forward(duo_engine* e, const int32_t* ids_host, int ro
 }
 
 extern "C" int duo_engine_logits(duo_engine* e, int row0, int n, float* out, duo_stream stream) {
+  DUO_TRY(fault_gate("logits"));
   DUO_TRY(check_engine(e, true, true));
   DUO_CHECK_ARG(out && n >= 1 && row0 >= 0 && row0 + n <= e->rows, "logits: bad rows");
   return logits_impl(e, row0, n, out, as_stream(stream));
 }
 
 extern "C" int duo_engine_argmax(duo_engine* e, int row0, int n, int32_t* out, duo_stream stream) {
+  DUO_TRY(fault_gate("argmax"));
   DUO_TRY(check_engine(e, true, true));
   DUO_CHECK_ARG(out && n >= 1 && row0 >= 0 && row0 + n <= e->rows, "argmax: bad rows");
   cudaStream_t st = as_stream(stream);
@@ -625,6 +633,7 @@ int generate_step(duo_engine* e, int vec_layer, int32_t* tokens_out, int n_steps
 }  // namespace
 
 extern "C" int duo_engine_generate(duo_engine* e, int n_steps, int vec_layer, int32_t* tokens_out, duo_stream stream) {
+  DUO_TRY(fault_gate("generate"));
   DUO_TRY(check_engine(e, true, true));
   DUO_CHECK_ARG(n_steps >= 0 && (n_steps == 0 || tokens_out), "generate: bad arguments");
   DUO_CHECK_ARG(vec_layer >= -1 && vec_layer < e->cfg.layers, "generate: vec_layer out of range");
@@ -633,6 +642,7 @@ extern "C" int duo_engine_generate(duo_engine* e, int n_steps, int vec_layer, in
     if (e->len[r] + n_steps > e->max_len) return fail(DUO_ESTATE, "generate: a row would exceed max_len");
   cudaStream_t st = as_stream(stream);
   for (int s = 0; s < n_steps; s++) {
+    DUO_TRY(fault_gate("generate"));  // a fault seen by an earlier step's last kernel stops the loop
     DUO_TRY(generate_step(e, vec_layer, tokens_out, n_steps, s, st));
     for (int r = 0; r < e->rows; r++) e->len[r] += 1;
   }

@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(256) gdn_conv_kernel(GdnConvArgs a) {
 
   // 2. conv + SiLU (+ l2norm) per token, half-warp per token
   const int c = tid & 15, hw = tid >> 4;
+  const unsigned hmask = 0xFFFFu << (tid & 16);  // the lanes of this thread's half-warp
   const bool norm = cgp < 2 * a.hk;  // q and k heads are l2-normalised; v heads pass through
   float w[8][CONV_KS];
 #pragma unroll
@@ -141,11 +142,13 @@ __global__ void __launch_bounds__(256) gdn_conv_kernel(GdnConvArgs a) {
       }
     }
     if (norm) {
+      // the two half-warps of a warp may be on different tokens, or one of them past the last token (tn mod 16
+      // odd): the reduction names only this half-warp's lanes
       float ss = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; j++) ss += v[j] * v[j];
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(hmask, ss, o);
       const float inv = rsqrtf(ss + 1e-6f);
 #pragma unroll
       for (int j = 0; j < 8; j++) v[j] *= inv;
@@ -188,11 +191,16 @@ __global__ void __launch_bounds__(256) gdn_conv_tma_kernel(const __grid_constant
   const int j0 = blockIdx.z * CONV_TPC, j1 = min(tiles, j0 + CONV_TPC);
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
   const int tid = threadIdx.x, c = tid & 15, hw = tid >> 4;
+  const unsigned hmask = 0xFFFFu << (tid & 16);  // the lanes of this thread's half-warp
   const int R = a.row_base + rr;
   const long m0 = (long)rr * a.t;
   const T* y = static_cast<const T*>(a.y);
   float* st = a.conv_state + ((long)R * (CONV_KS - 1)) * conv_dim + cgp * 128;  // st[j * conv_dim + ch]
 
+  if (tc::fault_pending(fault)) {  // an earlier kernel gave up a wait
+    pdl_wait();
+    return;
+  }
   if (tid == 0) {
     for (int s2 = 0; s2 < CONV_NS; s2++) tc::mbar_init(&full[s2], 1);
     tc::fence_mbar_init();
@@ -246,7 +254,14 @@ __global__ void __launch_bounds__(256) gdn_conv_tma_kernel(const __grid_constant
     const uint32_t ph = (uint32_t)(((j - j0) / CONV_NS) & 1);
     const bool ok = tc::mbar_wait(&full[s2], ph);
     if (__syncthreads_or(!ok)) {  // a load that never landed: give up (the fault word says so)
-      if (tid == 0) atomicOr(fault, 16u);
+      if (tid == 0) {
+        atomicOr(fault, 16u);
+        // tiles j .. j + NS - 1 may still be in flight into this CTA's ring: wait for them (bounded) before the CTA
+        // and its shared memory go away
+        for (int jj = j; jj < j1 && jj < j + CONV_NS; jj++)
+          tc::mbar_wait(&full[(jj - j0) % CONV_NS], (uint32_t)(((jj - j0) / CONV_NS) & 1));
+      }
+      __syncthreads();
       return;
     }
     const T* tile = ring + s2 * CONV_TT * 128;
@@ -277,11 +292,13 @@ __global__ void __launch_bounds__(256) gdn_conv_tma_kernel(const __grid_constant
         }
       }
       if (norm) {
+        // half-warp reduction: when tn mod 16 is odd the other half-warp of this warp has left the loop and waits
+        // at the block barrier below, so a full-warp mask would never complete
         float ss = 0.f;
 #pragma unroll
         for (int e = 0; e < 8; e++) ss += v[e] * v[e];
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(hmask, ss, o);
         const float inv = rsqrtf(ss + 1e-6f);
 #pragma unroll
         for (int e = 0; e < 8; e++) v[e] *= inv;
@@ -325,12 +342,7 @@ int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
     return with_act(dtype, [&](auto tag) -> int {
       using T = decltype(tag);
       if constexpr (sizeof(T) == 2) {
-        static bool attr_set = false;
-        if (!attr_set) {
-          DUO_CUDA_TRY(cudaFuncSetAttribute(gdn_conv_tma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            CONV_TMA_SMEM));
-          attr_set = true;
-        }
+        DUO_TRY(ensure_smem_attr(gdn_conv_tma_kernel<T>, CONV_TMA_SMEM));
         DUO_CUDA_TRY(::duo::launch_kernel(gdn_conv_tma_kernel<T>, grid, 256, CONV_TMA_SMEM, st, tmy, a, fault));
         DUO_LAUNCH_CHECK("gdn_conv_tma_kernel");
       }
@@ -659,11 +671,7 @@ int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cu
   const int grid = cdiv(items, per);
   return with_act(dtype, [&](auto tag) -> int {
     using T = decltype(tag);
-    static bool attr_set = false;
-    if (!attr_set) {
-      DUO_CUDA_TRY(cudaFuncSetAttribute(gdn_decode_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM));
-      attr_set = true;
-    }
+    DUO_TRY(ensure_smem_attr(gdn_decode_kernel<T>, DEC_SMEM));
     DUO_CUDA_TRY(::duo::launch_kernel(gdn_decode_kernel<T>, grid, DEC_THREADS, DEC_SMEM, st, ca, a));
     DUO_LAUNCH_CHECK("gdn_decode_kernel");
     return DUO_OK;

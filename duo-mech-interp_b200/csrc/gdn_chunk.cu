@@ -590,14 +590,9 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(GdnScanArgs a) {
 
 template <typename TI, bool NORM>
 static int run_chunk(const GdnScanArgs& a, cudaStream_t st) {
-  static bool attr = false;
   const int smem_p = (int)sizeof(PrepSmem), smem_s = (int)sizeof(ScanSmem);
-  if (!attr) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(gdn_chunk_prep_kernel<TI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_p));
-    DUO_CUDA_TRY(
-        cudaFuncSetAttribute(gdn_chunk_scan_kernel<TI, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_s));
-    attr = true;
-  }
+  DUO_TRY(ensure_smem_attr(gdn_chunk_prep_kernel<TI>, smem_p));
+  DUO_TRY(ensure_smem_attr(gdn_chunk_scan_kernel<TI, NORM>, smem_s));
   const int nch = (a.t + CK - 1) / CK;
   DUO_CUDA_TRY(::duo::launch_kernel(gdn_chunk_prep_kernel<TI>, dim3(nch, a.h, a.b), 256, smem_p, st, a));
   DUO_LAUNCH_CHECK("gdn_chunk_prep_kernel");

@@ -16,8 +16,6 @@ namespace duo {
 
 namespace cg = cooperative_groups;
 
-__device__ unsigned g_tc_fault;
-
 // ---------------------------------------------------------------------------------------------------------------
 // tcgen05 GEMM for small grids with more than 256 rows (decode-sized row counts go to gemm_dec.cu): one CTA per
 // 128 x BN tile (x a K range), K step 64 (one 128-byte swizzle row of 16-bit values), a ~96 KB TMA ring so that two
@@ -45,6 +43,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   static_assert(C::STAGES >= 2, "ring too small");
   static_assert(TC_BM * ((EPI == EPI_SWIGLU ? BN / 2 : BN) + 4) * 4 <= C::STAGES * C::STAGE_BYTES,
                 "the epilogue tile must fit in the ring");
+  if (gridDim.z == 1 && tc::fault_pending(fault)) {  // an earlier kernel gave up a wait (no cluster when z == 1)
+    pdl_wait();
+    return;
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
@@ -346,35 +348,11 @@ int make_tmap_plain(CUtensorMap* map, const void* base, int dtype, long rows, lo
   return DUO_OK;
 }
 
-unsigned* tc_fault_ptr() {
-  static unsigned* ptr = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_tc_fault) == cudaSuccess) ptr = static_cast<unsigned*>(p);
-  });
-  return ptr;
-}
-
-int tc_fault_read_clear(unsigned* out) {
-  unsigned v = 0, zero = 0;
-  DUO_CUDA_TRY(cudaDeviceSynchronize());
-  DUO_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tc_fault, sizeof(v)));
-  DUO_CUDA_TRY(cudaMemcpyToSymbol(g_tc_fault, &zero, sizeof(zero)));
-  *out = v;
-  return DUO_OK;
-}
-
 template <int BN, int EPI, bool F16>
 static int run_tc(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, int k, int ksplit,
                   const GemmEpiArgs& ep, cudaStream_t st) {
   using C = TcCfg<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      C::SMEM));
-    attr_set = true;
-  }
+  DUO_TRY(ensure_smem_attr(gemm_tc_kernel<BN, EPI, F16>, C::SMEM));
   unsigned* fault = tc_fault_ptr();
   if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
   const int num_k = k / TC_BK;
@@ -521,7 +499,7 @@ extern "C" int duo_gemm_bf16(const void* a, int m, int k, const void* b, int n, 
   DUO_CHECK_ARG(m >= 0 && n >= 0 && k > 0, "gemm_bf16: bad shape");
   DUO_CHECK_ARG(k % 64 == 0, "gemm_bf16: k must be a multiple of 64");
   DUO_CHECK_ARG(m == 0 || n == 0 || (a && b && c), "gemm_bf16: null pointer");
-  DUO_CHECK_ARG(valid_act(c_dtype), "gemm_bf16: c dtype must be f32 or bf16");
+  DUO_CHECK_ARG(valid_act(c_dtype), "gemm_bf16: c dtype must be f32, bf16 or f16");
   DUO_CHECK_ARG(ldc >= n, "gemm_bf16: ldc < n");
   DUO_CHECK_ARG(!accumulate || c_dtype == DUO_F32, "gemm_bf16: accumulate needs an f32 C");
   GemmEpiArgs ep;
@@ -558,7 +536,3 @@ extern "C" int duo_gemm_swiglu(const void* a, int m, int k, const void* b, int i
   return launch_gemm_tc(a, m, k, b, 2 * inter, ab_dtype, ep, as_stream(stream));
 }
 
-extern "C" int duo_fault_status(unsigned* out) {
-  DUO_CHECK_ARG(out, "fault_status: null pointer");
-  return tc_fault_read_clear(out);
-}

@@ -56,6 +56,10 @@ __global__ void __launch_bounds__(DTHREADS, 1)
                     GemmEpiArgs ep, unsigned* fault) {
   using C = DCfg<NB>;
   constexpr int CW = NB / 2;  // accumulator columns (X rows) drained per warp
+  if (gridDim.z == 1 && tc::fault_pending(fault)) {  // an earlier kernel gave up a wait (no cluster when z == 1)
+    pdl_wait();
+    return;
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sw = smem;
@@ -403,12 +407,8 @@ template <int NB, int EPI, bool F16>
 int run_dec(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tcm, int m, int n, int k, int groups,
             int ks, int kper, int direct, const GemmEpiArgs& ep, cudaStream_t st) {
   using C = DCfg<NB>;
-  static bool attr_set = false;
   auto kern = gemm_dec_kernel<NB, EPI, F16>;
-  if (!attr_set) {
-    DUO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    attr_set = true;
-  }
+  DUO_TRY(ensure_smem_attr(kern, C::SMEM));
   unsigned* fault = tc_fault_ptr();
   if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
   cudaLaunchConfig_t cfg = {};

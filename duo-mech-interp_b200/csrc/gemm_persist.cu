@@ -65,6 +65,10 @@ __global__ void __launch_bounds__(PTHREADS, 1)
     gemm_persist_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, int M,
                         int N, int K, int m_fast, GemmEpiArgs ep, unsigned* fault) {
   using C = PCfg<BN>;
+  if (tc::fault_pending(fault)) {  // an earlier kernel gave up a wait
+    pdl_wait();
+    return;
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
@@ -398,12 +402,7 @@ template <int BN, int EPI, bool F16>
 int run_persist(const CUtensorMap& ta, const CUtensorMap& tb, int m, int n, int k, const GemmEpiArgs& ep,
                 cudaStream_t st) {
   using C = PCfg<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    DUO_CUDA_TRY(
-        cudaFuncSetAttribute(gemm_persist_kernel<BN, EPI, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    attr_set = true;
-  }
+  DUO_TRY(ensure_smem_attr(gemm_persist_kernel<BN, EPI, F16>, C::SMEM));
   unsigned* fault = tc_fault_ptr();
   if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
   const long tiles = (long)cdiv(n, BN) * cdiv(m, PBM);

@@ -311,7 +311,7 @@ extern "C" int duo_q8_dequantize(const int8_t* q, const float* s, int n, int k, 
                                  duo_stream stream) {
   DUO_TRY(check_q8_shape(n, k, group));
   DUO_CHECK_ARG(q && s && out, "q8_dequantize: null pointer");
-  DUO_CHECK_ARG(valid_act(out_dtype), "q8_dequantize: out dtype must be f32 or bf16");
+  DUO_CHECK_ARG(valid_act(out_dtype), "q8_dequantize: out dtype must be f32, bf16 or f16");
   return launch_dequant(q, s, n, k, group, out, out_dtype, as_stream(stream));
 }
 

@@ -3,6 +3,8 @@
 #include <atomic>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include "common.cuh"
 
@@ -30,17 +32,33 @@ bool pdl_enabled() {
 }
 
 int sm_count() {
-  static int cached = 0;
+  constexpr int kMaxDev = 64;
+  static int cached[kMaxDev] = {};
   static std::mutex mu;
-  std::lock_guard<std::mutex> lock(mu);
-  if (cached == 0) {
-    int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
-      cached = n;
-    else
-      cached = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+    cudaGetLastError();
+    return 148;
   }
-  return cached;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    int n = 0;
+    cached[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+int ensure_smem_attr_fn(const void* func, int bytes) {
+  int dev = 0;
+  DUO_CUDA_TRY(cudaGetDevice(&dev));
+  static std::mutex mu;
+  static std::set<std::tuple<int, const void*, int>> done;
+  const auto key = std::make_tuple(dev, func, bytes);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return DUO_OK;
+  DUO_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert(key);
+  return DUO_OK;
 }
 
 }  // namespace duo

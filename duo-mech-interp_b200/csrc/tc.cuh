@@ -38,6 +38,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Device-side fail-fast of a kernel launched without a cluster: true for every thread of the CTA when an earlier
+// kernel has recorded a fault.  Call it first thing (every thread); a CTA that skips calls pdl_wait() before it
+// returns, so the kernels after it still wait for the ones before it.  Kernels launched as clusters do not use it:
+// their CTAs could read different values and the ones that stay would wait at a cluster barrier for the others.
+__device__ __forceinline__ bool fault_pending(const unsigned* fault) {
+  return __syncthreads_or(threadIdx.x == 0 && *reinterpret_cast<const volatile unsigned*>(fault) != 0u) != 0;
+}
+
 // Wait for the phase of `parity` to complete, giving up after `limit_ns` of wall time (the caller records a fault
 // and unwinds instead of hanging the GPU).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
@@ -175,10 +183,13 @@ int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long 
 int make_tmap_plain(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
                     int box_cols);
 
-// Device fault word shared by the tensor-core kernels: a bounded wait that gave up ORs a code into it.  tc_fault_ptr()
-// is its device address (kernels take it as a parameter); tc_fault_read_clear() synchronises the device, reads it
-// and clears it.
+// Device fault word shared by the bounded-wait kernels (fault.cu): a wait that gave up ORs a code into it.
+// tc_fault_ptr() is its address on the current device (kernels take it as a parameter).  fault_mirror_init() creates
+// the device's host-mapped copy, fault_mirror_dev() is that copy's device address (the engine's last kernel of a
+// forward writes it), and fault_gate(where) returns DUO_ECUDA once a fault is visible on the host.
 unsigned* tc_fault_ptr();
-int tc_fault_read_clear(unsigned* out);
+int fault_mirror_init();
+unsigned* fault_mirror_dev();
+int fault_gate(const char* where);
 
 }  // namespace duo

@@ -53,6 +53,7 @@ SIGNATURES = {
     "duo_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
     "duo_attention_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
     "duo_fault_status": (_i, [C.POINTER(_u)]),
+    "duo_fault_raise": (_i, [_u]),
     "duo_engine_create": (_i, [C.POINTER(duo_config), C.POINTER(_vp)]),
     "duo_engine_destroy": (None, [_vp]),
     "duo_engine_load": (_i, [_vp, C.POINTER(duo_weights_view), _vp]),

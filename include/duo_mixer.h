@@ -47,10 +47,18 @@ const char* duo_last_error(void);
 int duo_abi_version(void);
 /* Number of kernels this library has launched in this process (every entry point counts its launches). */
 unsigned long long duo_launch_count(void);
-/* Synchronise the device and read-and-clear the fault word of the tensor-core kernels: non-zero means a bounded
- * wait inside a kernel gave up (the kernel unwound instead of hanging).  The reference's analogue is its
- * device-lost check, engine/gpu.js:38, 151. */
+/* Synchronise the current device and read-and-clear the fault word of the bounded-wait kernels (TMA / tcgen05 /
+ * TMA-fed conv), its host-mapped mirror and the word set by duo_fault_raise: non-zero means a wait inside a kernel
+ * gave up (the kernel unwound instead of hanging; codes 1, 2, 4, 8 tensor-core pipeline, 16 conv prologue).  While the
+ * word is set, the tensor-core kernels launched without a cluster skip their work, and every duo_engine_forward /
+ * _forward_device / _logits / _argmax / _generate (and each step of _generate) returns DUO_ECUDA before launching
+ * anything once the fault is visible on the host (the last kernel of each forward mirrors it there).  Without a CUDA
+ * device only the duo_fault_raise word exists.  The reference's analogue is its device-lost check, engine/gpu.js:38,
+ * 151. */
 int duo_fault_status(unsigned* out);
+/* OR `code` into the host-side fault word that the engine calls check, exactly as a mirrored device fault would be
+ * seen: exercises the engine's error path without any device fault.  duo_fault_status clears it. */
+int duo_fault_raise(unsigned code);
 
 /* ============================================================================================================
  * Op-level entry points (the per-kernel sweeps and the parity tests call these; the engine uses the same kernels)

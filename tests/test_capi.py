@@ -105,3 +105,31 @@ def test_engine_rejects_bad_config_and_null_handle(L):
 def test_python_errors_raise(L):
     with pytest.raises(L.DuoError):
         L.call("duo_q8_quantize", None, L.DUO_F32, 4, 100, 128, None, None, None)
+
+
+def test_engine_calls_refuse_work_after_a_fault(L):
+    """A bounded wait that gave up inside a kernel reaches the host through a mirrored fault word; every engine call
+    reads it before anything else and returns DUO_ECUDA without launching a kernel, until duo_fault_status reads and
+    clears it.  Here the word is set from the host (duo_fault_raise), the way a mirrored device fault would appear:
+    no device fault is involved."""
+    lib = L.lib()
+    n0 = lib.duo_launch_count()
+    assert lib.duo_fault_raise(16) == L.DUO_OK
+    calls = {
+        "forward": lambda: lib.duo_engine_forward(None, None, 0, 1, 1, -1, None),
+        "forward_device": lambda: lib.duo_engine_forward_device(None, None, 0, 1, 1, -1, None),
+        "logits": lambda: lib.duo_engine_logits(None, 0, 1, None, None),
+        "argmax": lambda: lib.duo_engine_argmax(None, 0, 1, None, None),
+        "generate": lambda: lib.duo_engine_generate(None, 4, -1, None, None),
+    }
+    for name, call in calls.items():
+        assert call() == L.DUO_ECUDA, name
+        msg = lib.duo_last_error()
+        assert b"gave up" in msg and b"fault code 16" in msg, (name, msg)
+    assert lib.duo_launch_count() == n0  # nothing was launched
+    code = C.c_uint(0)
+    assert lib.duo_fault_status(C.byref(code)) == L.DUO_OK
+    assert code.value == 16
+    assert lib.duo_fault_status(C.byref(code)) == L.DUO_OK and code.value == 0  # read and cleared
+    # the gate is open again: what fails now is the null handle
+    assert lib.duo_engine_forward(None, None, 0, 1, 1, -1, None) == L.DUO_EINVAL
