@@ -709,3 +709,21 @@ extern "C" int duo_gdn_recurrent_fwd(const void* q, const void* k, const void* v
   return launch_gdn_recurrent(op_scan_args(q, k, v, g, beta, state, o, b, t, h, l2norm_qk), in_dtype,
                               as_stream(stream));
 }
+
+extern "C" int duo_gdn_conv_fwd(const void* y, int dtype, int w, const float* conv_w, float* conv_state,
+                                const float* a_log, const float* dt_bias, void* qkv, float* g, float* beta, int b,
+                                int t, int hk, int hv, int dk, int dv, duo_stream stream) {
+  DUO_CHECK_ARG(valid_act(dtype), "gdn_conv: dtype must be f32, bf16 or f16");
+  DUO_CHECK_ARG(dk == 128 && dv == 128, "gdn_conv: dk and dv must be 128");
+  DUO_CHECK_ARG(b >= 0 && t >= 0 && hk > 0 && hv > 0 && hv % hk == 0, "gdn_conv: bad shape");
+  const long conv_dim = 2L * hk * dk + (long)hv * dv;
+  DUO_CHECK_ARG(w >= conv_dim + (long)hv * dv + 2L * hv, "gdn_conv: w must hold [q k v | z | b | a]");
+  if (b == 0 || t == 0) return DUO_OK;
+  DUO_CHECK_ARG(y && conv_w && conv_state && a_log && dt_bias && qkv && g && beta, "gdn_conv: null pointer");
+  GdnConvArgs a{};
+  a.y = y; a.w = w; a.conv_w = conv_w; a.conv_state = conv_state; a.a_log = a_log; a.dt_bias = dt_bias;
+  a.qkv_out = qkv; a.g_out = g; a.beta_out = beta;
+  a.hk = hk; a.hv = hv; a.dk = dk; a.dv = dv; a.ks = CONV_KS;
+  a.rows = b; a.t = t; a.row_base = 0;
+  return launch_gdn_conv(a, dtype, as_stream(stream));
+}

@@ -117,6 +117,21 @@ def _gdn(name, q, k, v, g, beta, state, l2norm_qk, stream):
     return o
 
 
+def gdn_conv(y, conv_w, conv_state, a_log, dt_bias, hk, hv, stream=None):
+    """DeltaNet prologue of the fused projection y [b, t, w]: causal conv + SiLU + q/k l2norm with the carried
+    conv_state [b, 3, conv_dim] (f32, updated in place), gates beta / g (kernels_qwen35.js:129-178, 208-229).
+    Returns qkv [b, t, conv_dim] (y's dtype), g, beta [b, t, hv] f32."""
+    _dev(y, conv_w, conv_state, a_log, dt_bias)
+    b, t, w = y.shape
+    conv_dim = 2 * hk * 128 + hv * 128
+    qkv = torch.empty(b, t, conv_dim, dtype=y.dtype, device=y.device)
+    g = torch.empty(b, t, hv, dtype=torch.float32, device=y.device)
+    beta = torch.empty_like(g)
+    call("duo_gdn_conv_fwd", ptr(y), dtype_code(y.dtype), w, ptr(conv_w), ptr(conv_state), ptr(a_log), ptr(dt_bias),
+         ptr(qkv), ptr(g), ptr(beta), b, t, hk, hv, 128, 128, stream_ptr(stream))
+    return qkv, g, beta
+
+
 def gdn_recurrent(q, k, v, g, beta, state, l2norm_qk=True, stream=None):
     """Token-by-token gated delta rule; `state` [b, h, 128, 128] f32 is updated in place (kernels_qwen35.js:209-236)."""
     return _gdn("duo_gdn_recurrent_fwd", q, k, v, g, beta, state, l2norm_qk, stream)

@@ -106,6 +106,19 @@ int duo_gemm_swiglu(const void* a, int m, int k, const void* b, int inter, int a
 int duo_rmsnorm(const float* x, int m, int d, const float* w, float eps, int offset, void* y, int y_dtype,
                 duo_stream stream);
 
+/* The Gated DeltaNet prologue of a linear-attention layer over b rows x t tokens of its fused projection
+ * y [b * t, w] (f32, bf16 or f16; w >= conv_dim + hv dv + 2 hv) = [q k v (conv_dim = 2 hk dk + hv dv) | z (hv dv) |
+ * b (hv) | a (hv)]: causal depthwise conv (kernel 4, weights conv_w [conv_dim, 4] f32) over the conv_dim channels,
+ * continuing from conv_state [b, 3, conv_dim] (f32, the last 3 inputs of earlier calls, oldest first; updated in
+ * place), then SiLU and the l2norm (eps 1e-6) of every q and k head -> qkv [b * t, conv_dim] (same dtype as y);
+ * beta = sigmoid(b), g = -exp(a_log) * softplus(a + dt_bias) -> beta, g [b * t, hv] f32.  dk = dv = 128.
+ * Replaces `conv` + `convState` (engine/kernels_qwen35.js:129-178) and the gate and l2norm prep of `delta`
+ * (kernels_qwen35.js:208-229).  16-bit projections whose rows are 16-byte aligned and that span at least 64 token
+ * rows take the TMA-fed kernel, the rest the register-staged one. */
+int duo_gdn_conv_fwd(const void* y, int dtype, int w, const float* conv_w, float* conv_state, const float* a_log,
+                     const float* dt_bias, void* qkv, float* g, float* beta, int b, int t, int hk, int hv, int dk,
+                     int dv, duo_stream stream);
+
 /* Gated DeltaNet scan computed token by token (the recurrent form; t = 1 is one decode step) over b rows x t tokens
  * x h heads:  q, k [b, t, h, dk], v [b, t, h, dv] (f32 or bf16, token-major), g (log decay), beta [b, t, h] f32,
  * state [b, h, dk, dv] f32 read as the initial state and overwritten with the final one, o [b, t, h, dv].

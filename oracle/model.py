@@ -42,8 +42,21 @@ class Cfg:
 class OracleModel:
     """CPU restatement of the engine's Model with its per-row state (model.js:308-360)."""
 
-    def __init__(self, cfg, weights, rows, max_len, dtype=torch.float32):
+    # Where the 16-bit engines round an intermediate to bf16 / f16 (everything else stays f32): each name marks one
+    # such point in forward() / logits().  round_points maps names to a rounding function (empty: pure f32).
+    ROUND_POINTS = ("norm_in", "proj", "conv", "scan_out", "attn_q", "kv", "attn_out", "norm_post", "mlp_act",
+                    "final")
+
+    def __init__(self, cfg, weights, rows, max_len, dtype=torch.float32, round_points=None, gemm_weights=None,
+                 gemv_max=8):
         self.cfg, self.w, self.rows, self.max_len, self.dt = cfg, weights, rows, max_len, dtype
+        self.round_points = dict(round_points or {})
+        # the matrices a forward of more than gemv_max token rows multiplies with (the 16-bit engines' tensor-core
+        # pack, bf16(q * s) for G = 128); forwards of up to gemv_max rows use `weights` (the int8 GEMV's f32(q) * s)
+        self.w_gemm, self.gemv_max = gemm_weights, gemv_max
+        unknown = set(self.round_points) - set(self.ROUND_POINTS) - {"proj_gates"}
+        if unknown:
+            raise ValueError(f"unknown rounding points {sorted(unknown)}")
         c = cfg
         self.inv_freq = mixer.rope_inv_freq(c.rot, c.theta)
         self.conv = {}
@@ -61,6 +74,10 @@ class OracleModel:
         self.vectors = torch.zeros(rows, c.hidden, dtype=dtype)
         self.head_scales = {l: torch.ones(c.hv, dtype=dtype) for l in self.conv}
         self.last = torch.zeros(rows, c.hidden, dtype=dtype)
+
+    def _r(self, name, x):
+        fn = self.round_points.get(name)
+        return x if fn is None else fn(x)
 
     # -- state (model.js:352-376)
     def reset(self, r):
@@ -82,24 +99,25 @@ class OracleModel:
 
     # -- forward (model.js:404-466)
     def forward(self, ids, row_base, rows, T, pushes=None, vec=None, capture_resid=False):
-        c, w, dt = self.cfg, self.w, self.dt
+        c, dt = self.cfg, self.dt
         M = rows * T
+        w = self.w_gemm if (self.w_gemm is not None and M > self.gemv_max) else self.w
         ids = torch.as_tensor(ids, dtype=torch.int64).reshape(M)
-        x = w["embed"][ids].to(dt)  # kernels.js:205-221 gather (weights given already dequantised)
+        x = self.w["embed"][ids].to(dt)  # kernels.js:205-221 gather (weights given already dequantised)
         pos = torch.tensor([self.len[row_base + i] + t for i in range(rows) for t in range(T)])
         row_of = torch.tensor([row_base + i for i in range(rows) for _ in range(T)])
         pushes = pushes or {}
         resid = []
         for l, lt in enumerate(c.layer_types):
             L = w["layers"][l]
-            xn = mixer.rmsnorm(x, L["in_norm"], c.eps).to(dt)
-            y = xn @ L["proj"].to(dt).T
+            xn = self._r("norm_in", mixer.rmsnorm(x, L["in_norm"], c.eps).to(dt))
+            y = self._r("proj", xn @ L["proj"].to(dt).T)
             if lt == "linear_attention":
                 o = self._deltanet(l, L, y, row_base, rows, T)
             else:
                 o = self._attention(l, L, y, row_base, rows, T, pos)
             x = x + o @ L["out"].to(dt).T
-            xn = mixer.rmsnorm(x, L["post_norm"], c.eps).to(dt)
+            xn = self._r("norm_post", mixer.rmsnorm(x, L["post_norm"], c.eps).to(dt))
             gu = xn @ L["gu"].to(dt).T
             a = F.silu(gu[:, : c.inter]) * gu[:, c.inter:]
             for rec in pushes.get(l, []):  # kernels_qwen35.js:270-276, in record order
@@ -110,6 +128,7 @@ class OracleModel:
                     a[:, cols] = a[:, cols] * (vals[:, None] if rec.get("n") is None else vals)
                 else:
                     a[:, cols] = a[:, cols] + (vals[:, None] if rec.get("n") is None else vals)
+            a = self._r("mlp_act", a)
             x = x + a @ L["down"].to(dt).T
             if vec == l:  # kernels.js:190-203, one vector per absolute row
                 x = x + self.vectors[row_of]
@@ -125,30 +144,32 @@ class OracleModel:
         M = rows * T
         qkv = y[:, : c.conv_dim].reshape(rows, T, c.conv_dim)
         z = y[:, c.conv_dim: c.conv_dim + c.vd].reshape(rows, T, c.hv, c.dv)
-        b = y[:, c.conv_dim + c.vd: c.conv_dim + c.vd + c.hv].reshape(rows, T, c.hv)
-        a = y[:, c.conv_dim + c.vd + c.hv:].reshape(rows, T, c.hv)
+        b = self._r("proj_gates", y[:, c.conv_dim + c.vd: c.conv_dim + c.vd + c.hv]).reshape(rows, T, c.hv)
+        a = self._r("proj_gates", y[:, c.conv_dim + c.vd + c.hv:]).reshape(rows, T, c.hv)
         rs = slice(row_base, row_base + rows)
         conv_out, new_state = mixer.causal_conv1d(qkv, L["conv"], self.conv[l][rs])
         self.conv[l][rs] = new_state.to(dt)
         conv_out = conv_out.to(dt)
         q = conv_out[..., : c.kd].reshape(rows, T, c.hk, c.dk)
         k = conv_out[..., c.kd: 2 * c.kd].reshape(rows, T, c.hk, c.dk)
-        v = conv_out[..., 2 * c.kd:].reshape(rows, T, c.hv, c.dv)
+        v = self._r("conv", conv_out[..., 2 * c.kd:].reshape(rows, T, c.hv, c.dv))
+        if "conv" in self.round_points:  # the engine's conv writes q and k already l2-normalised
+            q, k = self._r("conv", mixer.l2norm(q)), self._r("conv", mixer.l2norm(k))
         if c.hv // c.hk > 1:
             q = q.repeat_interleave(c.hv // c.hk, dim=2)
             k = k.repeat_interleave(c.hv // c.hk, dim=2)
         beta, g = mixer.gdn_gates(a, b, L["alog"], L["dtb"])
         rule = mixer.recurrent_gated_delta_rule if T == 1 else mixer.chunk_gated_delta_rule
-        o, s = rule(q, k, v, g.to(dt), beta.to(dt), state=self.S[l][rs])
+        o, s = rule(q, k, v, g.to(dt), beta.to(dt), state=self.S[l][rs], l2norm_qk="conv" not in self.round_points)
         self.S[l][rs] = s.to(dt)
         o = mixer.gated_rmsnorm(o, z, L["gnorm"], c.eps).to(dt)
         o = o * self.head_scales[l][None, None, :, None]
-        return o.reshape(M, c.vd)
+        return self._r("scan_out", o.reshape(M, c.vd))
 
     def _attention(self, l, L, y, row_base, rows, T, pos):
         c, dt = self.cfg, self.dt
         q, k, v, gate = mixer.attn_prep(y, L["qnorm"], L["knorm"], pos, c.nh, c.nkv, c.hd, self.inv_freq, c.eps)
-        q, k, v = q.to(dt), k.to(dt), v.to(dt)
+        q, k, v = self._r("attn_q", q.to(dt)), self._r("kv", k.to(dt)), self._r("kv", v.to(dt))
         out = torch.zeros(rows * T, c.nh, c.hd, dtype=dt)
         for i in range(rows):
             r = row_base + i
@@ -161,13 +182,14 @@ class OracleModel:
             out[i * T:(i + 1) * T] = mixer.cached_attention(q[i * T:(i + 1) * T], self.kc[l][r], self.vc[l][r],
                                                             n_keys, 1.0 / math.sqrt(c.hd)).to(dt)
         out = out.reshape(rows * T, c.nh * c.hd) * torch.sigmoid(gate.to(dt))
-        return out
+        return self._r("attn_out", out)
 
     # -- heads (model.js:472-500)
     def logits(self, rows=None):
         rows = list(range(self.rows)) if rows is None else rows
-        h = mixer.rmsnorm(self.last[rows], self.w["final_norm"], self.cfg.eps).to(self.dt)
-        return h @ self.w["embed"].to(self.dt).T
+        w = self.w_gemm if (self.w_gemm is not None and len(rows) > self.gemv_max) else self.w
+        h = self._r("final", mixer.rmsnorm(self.last[rows], self.w["final_norm"], self.cfg.eps).to(self.dt))
+        return h @ w["embed"].to(self.dt).T
 
     def argmax(self, rows=None):
         # kernels.js:261-284: ties go to the lower index, which torch.argmax also does on the CPU

@@ -2,21 +2,57 @@
 int8 weights: the method of the reference's tests/engine_ref.py + tests/engine.mjs (same inputs; logits, greedy
 tokens; pushes and the residual vector) and steerfind.html (batched rows == single rows).
 
-Tolerances: f32 engine 1e-4 max relative logit error and identical greedy tokens for 32 steps (north_star's
-fp32-accumulation check, config 1); 16-bit tensor-core engine with f16 activations 2e-2 (north_star's 16-bit bound).
-bf16 activations: the bf16 format alone, rounded at the engine's rounding points with everything else exact, puts
-config 1's logits 3.3% (max relative) off the f32 oracle on this random-init model, and transformers' own bf16 model
-is 6.6% off its fp32 logits on the same workload (both measured with the oracle).  2e-2 is below that floor, so the
-bf16 engine is held to BF16_TOL = 6e-2: no worse than the reference's own PyTorch path in bf16."""
+Tolerances (max relative logit error, north_star):
+  * f32 engine: 1e-4 against the f32 oracle and identical greedy tokens for 32 steps (config 1);
+  * 16-bit engines (f16 / bf16 activations): TOL16 = 2e-2 against the oracle run with the engine's own rounding points
+    (OracleModel.ROUND_POINTS: the intermediates the engine stores in 16 bits, and for G = 128 the tensor-core pack's
+    16-bit q * s), i.e. on identical arithmetic up to summation order and the chunk scan's f16 internals;
+  * and against the pure f32 oracle: 2e-2, or 1.3 x the error the rounding points alone cause if that is larger.
+    For f16 that is 2e-2.  For bf16 it is not: rounding only the projection GEMMs' A operands to bf16 already puts
+    config 1's logits 2.5% off f32, all of the engine's points 3.5% (tests/test_bf16_floor.py), so no bf16 engine
+    can meet 2e-2 against f32 on this model.
+Greedy tokens of a 16-bit engine may differ from the f32 oracle's only where the oracle's top-2 logit gap is within
+twice the logit error measured at that step."""
 import numpy as np
 import pytest
 import torch
 
 from conftest import rel_max
-from oracle.model import Cfg, OracleModel
+from oracle.model import Cfg, OracleModel, map_weights
 from tiny import TINY, tiny_state_dict, tiny_workload
 
-BF16_TOL = 6e-2
+TOL16 = 2e-2
+RND16 = {"bf16": lambda x: x.to(torch.bfloat16).float(), "f16": lambda x: x.to(torch.float16).float()}
+
+
+def make_oracle(cfg, Wd, act, group, rows, max_len, emulate):
+    """The f32 oracle, or (emulate, 16-bit act) the oracle that rounds where the engine does."""
+    if not emulate or act == "f32":
+        return OracleModel(cfg, Wd, rows=rows, max_len=max_len)
+    rnd = RND16[act]
+    wg = map_weights(Wd, rnd) if group else None  # G = 128: the tensor-core pack holds 16-bit(q * s)
+    return OracleModel(cfg, Wd, rows=rows, max_len=max_len, round_points={p: rnd for p in OracleModel.ROUND_POINTS},
+                       gemm_weights=wg)
+
+
+def check_16bit(eng, ref, emu, what=""):
+    """eng / ref / emu: per-step logits of the engine, the f32 oracle and the emulating oracle."""
+    e_emu = max(rel_max(a, b) for a, b in zip(eng, emu))
+    e_ref = max(rel_max(a, b) for a, b in zip(eng, ref))
+    floor = max(rel_max(b, r) for b, r in zip(emu, ref))
+    assert e_emu < TOL16, (what, "vs emulating oracle", e_emu)
+    assert e_ref < max(TOL16, 1.3 * floor), (what, "vs f32 oracle", e_ref, "floor", floor)
+    return e_emu, e_ref, floor
+
+
+def check_greedy_near_ties(toks, ref_toks, eng, ref):
+    """Tokens may differ only where the reference's top-2 gap is within twice the measured logit error of the step."""
+    same = torch.stack(toks) == torch.stack(ref_toks)
+    for s, r in zip(*torch.nonzero(~same, as_tuple=True)):
+        s, r = int(s), int(r)
+        top2 = ref[s][r].topk(2).values
+        err = float((eng[s][r].double() - ref[s][r].double()).abs().max())
+        assert float(top2[0] - top2[1]) <= 2 * err, ("divergence away from a near-tie", s, r)
 
 pytestmark = pytest.mark.gpu
 
@@ -76,8 +112,8 @@ def run_engine(types, W, act, ids, push, vec_layer, vecs, steps, group=128, max_
     return logits, toks
 
 
-def run_oracle(types, Wd, ids, push, vec_layer, vecs, steps, forced=None):
-    om = OracleModel(oracle_cfg(types), Wd, rows=3, max_len=64)
+def run_oracle(types, Wd, ids, push, vec_layer, vecs, steps, forced=None, act="f32", group=128, emulate=False):
+    om = make_oracle(oracle_cfg(types), Wd, act, group, 3, 64, emulate)
     if vecs is not None:
         om.set_vectors(list(vecs))
     om.forward(ids.reshape(-1), 0, 3, ids.shape[1], pushes=push, vec=vec_layer)
@@ -89,19 +125,23 @@ def run_oracle(types, Wd, ids, push, vec_layer, vecs, steps, forced=None):
     return logits
 
 
-@pytest.mark.parametrize("act,tol", [("f32", 1e-4), ("f16", 2e-2), ("bf16", BF16_TOL)])
+@pytest.mark.parametrize("act", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("group", [128, 0])
-def test_tiny_model_parity(tiny, act, tol, group):
+def test_tiny_model_parity(tiny, act, group):
     types, packs = tiny
     W, Wd = packs[group]
     ids, push, vec_layer, vecs = tiny_workload()
     eng, toks = run_engine(types, W, act, ids, push, vec_layer, vecs, 6, group)
     ref = run_oracle(types, Wd, ids, push, vec_layer, vecs, 6, forced=toks)
-    for s, (a, b) in enumerate(zip(eng, ref)):
-        assert rel_max(a, b) < tol, f"step {s}"
+    ref_toks = [r.argmax(-1) for r in ref[:-1]]
     if act == "f32":
-        ref_toks = [r.argmax(-1) for r in ref[:-1]]
+        for s, (a, b) in enumerate(zip(eng, ref)):
+            assert rel_max(a, b) < 1e-4, f"step {s}"
         assert torch.equal(torch.stack(toks), torch.stack(ref_toks))
+    else:
+        emu = run_oracle(types, Wd, ids, push, vec_layer, vecs, 6, forced=toks, act=act, group=group, emulate=True)
+        check_16bit(eng, ref, emu, f"tiny {act} G={group}")
+        check_greedy_near_ties(toks, ref_toks, eng, ref)
 
 
 @pytest.mark.parametrize("act", ["f32", "f16", "bf16"])
@@ -134,10 +174,18 @@ def test_chunked_prefill_and_row_lengths(tiny, act):
     m = Model(cfg, W).alloc(rows=3, max_len=64, max_t=7)
     m.prefill(1, ids[1].tolist())
     assert m.row_len(1) == 20 and m.row_len(0) == 0
-    om = OracleModel(oracle_cfg(types), Wd, rows=3, max_len=64)
-    om.forward(ids[1], 1, 1, 20)
-    tol = {"f32": 1e-4, "f16": 2e-2, "bf16": BF16_TOL}[act]
-    assert rel_max(m.logits_row(1).cpu(), om.logits([1])[0]) < tol
+    out = {}
+    for emulate in ((False,) if act == "f32" else (False, True)):
+        om = make_oracle(oracle_cfg(types), Wd, act, 128, 3, 64, emulate)
+        for i in range(0, 20, 7):  # the same 7-token calls as the engine's prefill
+            chunk = ids[1][i:i + 7]
+            om.forward(chunk, 1, 1, len(chunk))
+        out[emulate] = om.logits([1])[0]
+    eng = m.logits_row(1).cpu()
+    if act == "f32":
+        assert rel_max(eng, out[False]) < 1e-4
+    else:
+        check_16bit([eng], [out[False]], [out[True]], f"chunked prefill {act}")
 
 
 @pytest.mark.parametrize("act", ["f32", "f16", "bf16"])
@@ -150,11 +198,16 @@ def test_long_prefill(tiny, act):
     ids = torch.randint(0, TINY["vocab"], (2, 187), generator=torch.Generator().manual_seed(11))
     m = Model(duo_cfg_from_tiny(types, act), W).alloc(rows=2, max_len=200, max_t=150, max_tokens=300)
     om = OracleModel(oracle_cfg(types), Wd, rows=2, max_len=200)
-    tol = {"f32": 1e-4, "f16": 2e-2, "bf16": BF16_TOL}[act]
+    emu = make_oracle(oracle_cfg(types), Wd, act, 128, 2, 200, True)
     for a, b in ((0, 150), (150, 187)):
         m.forward(ids[:, a:b].reshape(-1), 0, 2, b - a)
         om.forward(ids[:, a:b].reshape(-1), 0, 2, b - a)
-        assert rel_max(m.logits_all().cpu(), om.logits()) < tol, (a, b)
+        emu.forward(ids[:, a:b].reshape(-1), 0, 2, b - a)
+        eng = m.logits_all().cpu()
+        if act == "f32":
+            assert rel_max(eng, om.logits()) < 1e-4, (a, b)
+        else:
+            check_16bit([eng], [om.logits()], [emu.logits()], f"long prefill {act} {a}:{b}")
 
 
 def test_generate_matches_step_loop(tiny):
@@ -198,6 +251,59 @@ def test_greedy_from_lm_head_epilogue(tiny, act):
         loop.append(nxt.cpu())
         m2.step(nxt.tolist())
     assert torch.equal(gen.long(), torch.stack(loop, 1))
+
+
+def test_head_scales(tiny):
+    """setHeadScales (model.js:362-369; applied after the gated norm, kernels_qwen35.js:243): per-head output scales
+    of linear-attention layers, for prefill and decode; None restores ones."""
+    from duo import Model
+    types, packs = tiny
+    W, Wd = packs[128]
+    lin = [l for l, t in enumerate(types) if t == "linear_attention"]
+    hv = TINY["hv"]
+    scales = {lin[0]: [0.5 + 0.25 * i for i in range(hv)], lin[-1]: [2.0 - 0.3 * i for i in range(hv)]}
+    ids, _, _, _ = tiny_workload()
+    m = Model(duo_cfg_from_tiny(types, "f32"), W).alloc(rows=3, max_len=64, max_t=64, max_tokens=64)
+    om = OracleModel(oracle_cfg(types), Wd, rows=3, max_len=64)
+    plain = OracleModel(oracle_cfg(types), Wd, rows=3, max_len=64)
+    m.set_head_scales(scales)
+    om.set_head_scales(scales)
+    m.forward(ids.reshape(-1), 0, 3, ids.shape[1])
+    om.forward(ids.reshape(-1), 0, 3, ids.shape[1])
+    plain.forward(ids.reshape(-1), 0, 3, ids.shape[1])
+    assert rel_max(m.logits_all().cpu(), om.logits()) < 1e-4
+    assert rel_max(om.logits(), plain.logits()) > 1e-3  # the scales change the result
+    m.step([1, 2, 3])
+    om.forward([1, 2, 3], 0, 3, 1)
+    assert rel_max(m.logits_all().cpu(), om.logits()) < 1e-4
+    m.set_head_scales(None)
+    m.reset_all()
+    m.forward(ids.reshape(-1), 0, 3, ids.shape[1])
+    assert rel_max(m.logits_all().cpu(), plain.logits()) < 1e-4
+
+
+def test_engine_stops_after_a_fault(tiny):
+    """With the fault word set (from the host here, as a mirrored device fault would be), engine calls return an error
+    before launching anything; once duo_fault_status has read and cleared it, the engine runs again."""
+    from duo import DuoError, Model, lib as L, ops
+    types, packs = tiny
+    W, _ = packs[128]
+    m = Model(duo_cfg_from_tiny(types, "bf16"), W).alloc(rows=2, max_len=32, max_t=8)
+    m.prefill(0, list(range(5)))
+    before = m.logits_row(0).cpu()
+    assert ops.fault_status() == 0
+    L.lib().duo_fault_raise(2)
+    n0 = L.lib().duo_launch_count()
+    with pytest.raises(DuoError, match="gave up"):
+        m.step([1, 2])
+    with pytest.raises(DuoError, match="gave up"):
+        m.generate(3)
+    assert L.lib().duo_launch_count() == n0
+    assert m.row_len(0) == 5
+    assert ops.fault_status() == 2
+    assert torch.equal(m.logits_row(0).cpu(), before)
+    m.step([1, 2])
+    assert m.row_len(0) == 6
 
 
 def test_engine_errors(tiny):
@@ -263,22 +369,81 @@ def test_config1_full_model(config1, act):
         toks.append(nxt)
         m.step(nxt.tolist(), opts)
         eng.append(m.logits_all().cpu())
-    om = OracleModel(ocfg, Wd, rows=3, max_len=128)
-    om.forward(ids.reshape(-1), 0, 3, 64, pushes=push)
-    ref = [om.logits()]
-    ref_toks = []
-    for s in range(32):
-        ref_toks.append(ref[-1].argmax(-1))
-        om.forward(toks[s].tolist(), 0, 3, 1, pushes=push)  # teacher-forced on the engine's tokens
-        ref.append(om.logits())
-    tol = {"f32": 1e-4, "f16": 2e-2, "bf16": BF16_TOL}[act]
-    errs = [rel_max(a, b) for a, b in zip(eng, ref)]
-    assert max(errs) < tol, errs
-    same = torch.stack(toks) == torch.stack(ref_toks)
+    runs = {}
+    for emulate in ((False,) if act == "f32" else (False, True)):
+        om = make_oracle(ocfg, Wd, act, 128, 3, 128, emulate)
+        om.forward(ids.reshape(-1), 0, 3, 64, pushes=push)
+        lg = [om.logits()]
+        for s in range(32):
+            om.forward(toks[s].tolist(), 0, 3, 1, pushes=push)  # teacher-forced on the engine's tokens
+            lg.append(om.logits())
+        runs[emulate] = lg
+    ref = runs[False]
+    ref_toks = [r.argmax(-1) for r in ref[:-1]]
     if act == "f32":
-        assert bool(same.all())
+        errs = [rel_max(a, b) for a, b in zip(eng, ref)]
+        assert max(errs) < 1e-4, errs
+        assert torch.equal(torch.stack(toks), torch.stack(ref_toks))
     else:
-        # bf16: report (not fail on) greedy divergences at near-ties of the reference
-        for s, r in zip(*torch.nonzero(~same, as_tuple=True)):
-            top2 = ref[int(s)][int(r)].topk(2).values
-            assert float(top2[0] - top2[1]) < 0.05 * float(top2[0].abs()), "divergence away from a near-tie"
+        check_16bit(eng, ref, runs[True], f"config 1 {act}")
+        check_greedy_near_ties(toks, ref_toks, eng, ref)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# the configuration bench.py times: full shape, int8 weights with one scale per output row, bf16 activations, prompts
+# prefilled in groups of 2 rows, long enough for the TMA-fed conv's multi-block path, lengths not multiples of 64;
+# more than 8 rows, so decode runs the decode GEMM and greedy tokens come from the LM head's argmax epilogue
+
+
+@pytest.mark.slow
+def test_bench_configuration_parity(cuda):
+    from duo import Model, qwen35_0p8b
+    from duo.weights import random_weights
+    cfg = qwen35_0p8b(group=0, act_dtype="bf16")
+    W = random_weights(cfg, seed=5)
+    Wd = to_cpu(W.dequantized())
+    ocfg = Cfg()
+    rows, T1, T2, steps, vec_layer = 12, 601, 37, 8, 12
+    gen = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, ocfg.vocab, (rows, T1 + T2), generator=gen)
+    # steering vectors on the first half of the rows, N(0, 1) * 0.5 * the median residual norm after layer 12 of a
+    # calibration prompt (token 0 skipped), as bench.py sets them
+    cal = OracleModel(ocfg, Wd, rows=1, max_len=64)
+    resid = cal.forward(torch.randint(0, ocfg.vocab, (64,), generator=gen), 0, 1, 64, capture_resid=True)
+    p50 = float(resid[vec_layer][1:].norm(dim=-1).median())
+    vecs = [torch.randn(ocfg.hidden, generator=gen) * 0.5 * p50 if r < rows // 2 else None for r in range(rows)]
+
+    m = Model(cfg, W).alloc(rows=rows, max_len=T1 + T2 + steps + 1, max_t=T1, max_tokens=2 * T1)
+    m.set_vectors(vecs)
+    opts = {"vec": vec_layer}
+    for a, b in ((0, T1), (T1, T1 + T2)):
+        for g0 in range(0, rows, 2):  # row groups of 2, as the bench's max_tokens gives
+            m.forward(ids[g0:g0 + 2, a:b].reshape(-1), g0, 2, b - a, opts)
+    eng = [m.logits_all().cpu()]
+    gen_toks = m.generate(steps, vec=vec_layer).cpu().long()  # [rows, steps]: first = argmax of the prefill state
+    eng.append(m.logits_all().cpu())
+    assert m.row_len(0) == T1 + T2 + steps
+
+    runs = {}
+    for emulate in (False, True):
+        om = make_oracle(ocfg, Wd, "bf16", 0, rows, T1 + T2 + steps + 1, emulate)
+        om.set_vectors(vecs)
+        for a, b in ((0, T1), (T1, T1 + T2)):
+            for g0 in range(0, rows, 2):
+                om.forward(ids[g0:g0 + 2, a:b].reshape(-1), g0, 2, b - a, vec=vec_layer)
+        lg = [om.logits()]
+        for s in range(steps):
+            om.forward(gen_toks[:, s].tolist(), 0, rows, 1, vec=vec_layer)  # teacher-forced on the engine's tokens
+            lg.append(om.logits())
+        runs[emulate] = lg
+    ref, emu = runs[False], runs[True]
+    check_16bit(eng, [ref[0], ref[-1]], [emu[0], emu[-1]], "bench configuration")
+    # the engine's greedy tokens against the oracle's logits at every step (near-ties within the measured error)
+    err = max(float((a.double() - b.double()).abs().max()) for a, b in zip(eng, [ref[0], ref[-1]]))
+    for s in range(steps):
+        ref_tok = ref[s].argmax(-1)
+        for r in torch.nonzero(gen_toks[:, s] != ref_tok).flatten().tolist():
+            top2 = ref[s][r].topk(2).values
+            assert float(top2[0] - top2[1]) <= 2 * err, ("divergence away from a near-tie", s, r)
+    from duo import ops
+    assert ops.fault_status() == 0

@@ -266,3 +266,111 @@ def test_attention(ops, dtype, tol, b, t, starts, max_len, nh, nkv):
     ref = _attn_ref(q.float(), kc.float(), vc.float(), start, gate.float())
     o = ops.attention(q.cuda(), kc.cuda(), vc.cuda(), start.cuda(), gate=gate.cuda())
     assert rel_max(o.float(), ref) < tol
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# DeltaNet conv prologue (kernels_qwen35.js:129-178, 208-229): causal conv + SiLU + q/k l2norm + gates, state carried
+# across calls.  Call sequences mix the register-staged kernel (f32, or fewer than 64 token rows) and the TMA-fed one
+# (16-bit, >= 64 token rows), several 64-token tiles per block and several blocks per row (> 512 tokens), and token
+# counts whose last tile has an odd number of tokens modulo 16 (37, 3, 129).
+
+
+def _conv_ref(y, conv_w, state, a_log, dt_bias, hk, hv):
+    b, t, _ = y.shape
+    kd, vd = hk * 128, hv * 128
+    cd = 2 * kd + vd
+    out, new_state = mixer.causal_conv1d(y[..., :cd].float(), conv_w, state)
+    q = mixer.l2norm(out[..., :kd].reshape(b, t, hk, 128)).reshape(b, t, kd)
+    k = mixer.l2norm(out[..., kd:2 * kd].reshape(b, t, hk, 128)).reshape(b, t, kd)
+    beta, g = mixer.gdn_gates(y[..., cd + vd + hv:cd + vd + 2 * hv].float(), y[..., cd + vd:cd + vd + hv].float(),
+                              a_log, dt_bias)
+    return torch.cat([q, k, out[..., 2 * kd:]], -1), g, beta, new_state
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2), (torch.float16, 2e-3)])
+@pytest.mark.parametrize("b,calls,hk,hv", [(2, [700, 3, 37, 1, 2], 4, 4), (1, [1100], 16, 16),
+                                           (3, [17, 64, 129], 2, 4), (8, [37], 16, 16)])
+def test_gdn_conv(ops, dtype, tol, b, calls, hk, hv):
+    gen = _seed(sum(calls) + 31 * b + hk)
+    cd = 2 * hk * 128 + hv * 128
+    w = cd + hv * 128 + 2 * hv
+    conv_w = torch.randn(cd, 4, generator=gen) * 0.3
+    a_log = torch.empty(hv).uniform_(0, 16, generator=gen).log()
+    dt_bias = torch.ones(hv)
+    state = torch.randn(b, 3, cd, generator=gen) * 0.5
+    st_gpu = state.clone().cuda()
+    for t in calls:
+        y = torch.randn(b, t, w, generator=gen).to(dtype)
+        qkv, g, beta = ops.gdn_conv(y.cuda(), conv_w.cuda(), st_gpu, a_log.cuda(), dt_bias.cuda(), hk, hv)
+        rq, rg, rb, state = _conv_ref(y, conv_w, state, a_log, dt_bias, hk, hv)
+        assert rel_max(qkv.float(), rq) < tol, t
+        assert rel_max(g, rg) < 1e-5 and rel_max(beta, rb) < 1e-5, t
+        assert torch.equal(st_gpu.cpu(), state.float()), t  # the carried inputs, exactly
+    assert ops.fault_status() == 0
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# config 2's chunked-scan shapes (B in {1, 8}, T in {512, 4096, 16384}, H = 16, chunk 64, bf16 inputs, f32 state),
+# checked against the oracle's chunk rule on three of the sixteen heads (the CPU cost of all heads is large)
+
+
+@pytest.mark.parametrize("b,t", [(1, 512), (8, 512), (1, 4096), (8, 4096), (1, 16384), (8, 16384)])
+def test_gdn_chunk_config2_shapes(ops, b, t):
+    h, heads = 16, [0, 9, 15]
+    gen = torch.Generator(device="cuda").manual_seed(b * 100003 + t)
+    rn = lambda *s: torch.randn(*s, generator=gen, device="cuda")
+    q, k = mixer.l2norm(rn(b, t, h, 128)), mixer.l2norm(rn(b, t, h, 128))
+    v = rn(b, t, h, 128)
+    beta = torch.sigmoid(rn(b, t, h))
+    g = -torch.nn.functional.softplus(rn(b, t, h))
+    qb, kb, vb = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
+    st = torch.zeros(b, h, 128, 128, device="cuda")
+    o = ops.gdn_chunk(qb, kb, vb, g.contiguous(), beta.contiguous(), st, l2norm_qk=False)
+    sl = lambda x: x[:, :, heads].float().cpu()
+    ro, rs = mixer.chunk_gated_delta_rule(sl(qb), sl(kb), sl(vb), sl(g), sl(beta), state=None, l2norm_qk=False)
+    assert rel_max(o[:, :, heads].float(), ro) < 2e-2
+    assert rel_max(st[:, heads], rs) < 2e-2
+    assert not torch.isnan(o.float()).any()
+    assert ops.fault_status() == 0
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# config 3's attention shapes: prefill at B = 4, T in {1024, 4096, 16384} (8 q / 2 kv heads, hd 256, sigmoid gate)
+# checked on sampled query positions; decode at B = 32 against an 8192-token cache, checked in full
+
+
+@pytest.mark.parametrize("t", [1024, 4096, 16384])
+def test_attention_prefill_config3(ops, t):
+    b, nh, nkv, hd = 4, 8, 2, 256
+    gen = torch.Generator(device="cuda").manual_seed(t)
+    rn = lambda *s: torch.randn(*s, generator=gen, device="cuda").to(torch.bfloat16)
+    q, gate = rn(b, t, nh, hd), rn(b, t, nh, hd)
+    kc, vc = rn(b, t, nkv, hd), rn(b, t, nkv, hd)
+    start = torch.zeros(b, dtype=torch.int32, device="cuda")
+    o = ops.attention(q, kc, vc, start, gate=gate)
+    pos = sorted(set([0, 1, 63, 64, 127, 128, t // 2, t - 65, t - 2, t - 1] +
+                     torch.randint(0, t, (6,), generator=_seed(t)).tolist()))
+    kf, vf = kc.float().cpu(), vc.float().cpu()
+    for r in range(b):
+        qs = q[r, pos].float().cpu()
+        ref = torch.stack([mixer.cached_attention(qs[i:i + 1], kf[r], vf[r], [p + 1], hd ** -0.5)[0]
+                           for i, p in enumerate(pos)])
+        ref = ref * torch.sigmoid(gate[r, pos].float().cpu())
+        assert rel_max(o[r, pos].float(), ref) < 2e-2, r
+    assert not torch.isnan(o.float()).any()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("ragged", [False, True])
+def test_attention_decode_config3(ops, dtype, ragged):
+    b, nh, nkv, hd, max_len = 32, 8, 2, 256, 8192
+    gen = torch.Generator(device="cuda").manual_seed(32 + ragged)
+    rn = lambda *s: torch.randn(*s, generator=gen, device="cuda").to(dtype)
+    q, gate = rn(b, 1, nh, hd), rn(b, 1, nh, hd)
+    kc, vc = rn(b, max_len, nkv, hd), rn(b, max_len, nkv, hd)
+    starts = (torch.randint(0, max_len, (b,), generator=_seed(5)) if ragged else torch.full((b,), max_len - 1))
+    starts[0] = max_len - 1
+    start = starts.to(torch.int32).cuda()
+    o = ops.attention(q, kc, vc, start, gate=gate)
+    ref = _attn_ref(q.float().cpu(), kc.float().cpu(), vc.float().cpu(), starts, gate.float().cpu())
+    assert rel_max(o.float(), ref) < 2e-2

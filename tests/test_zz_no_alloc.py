@@ -16,9 +16,9 @@ from conftest import rel_max
 pytestmark = pytest.mark.gpu
 
 
-def _inputs(b, max_len, starts, seed, nh=8, nkv=2, hd=256):
+def _inputs(b, max_len, starts, seed, nh=8, nkv=2, hd=256, dtype=torch.bfloat16):
     g = torch.Generator(device="cpu").manual_seed(seed)
-    mk = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16).cuda()
+    mk = lambda *s: torch.randn(*s, generator=g).to(dtype).cuda()
     q, gate = mk(b, 1, nh, hd), mk(b, 1, nh, hd)
     kc, vc = mk(b, max_len, nkv, hd), mk(b, max_len, nkv, hd)
     return q, kc, vc, torch.tensor(starts, dtype=torch.int32).cuda(), gate
@@ -29,17 +29,21 @@ def _call(name, q, kc, vc, start, gate):
     b, t, nh, hd = q.shape
     _, max_len, nkv, _ = kc.shape
     o = torch.full_like(q, float("nan"))
+    code = {torch.float32: L.DUO_F32, torch.bfloat16: L.DUO_BF16, torch.float16: L.DUO_F16}[q.dtype]
     st = L.lib().__getattr__(name)(L.ptr(q), L.ptr(kc), L.ptr(vc), L.ptr(start), L.ptr(gate), nh * hd, L.ptr(o),
-                                   L.DUO_BF16, b, t, nh, nkv, hd, max_len, C.c_float(hd ** -0.5),
+                                   code, b, t, nh, nkv, hd, max_len, C.c_float(hd ** -0.5),
                                    L.stream_ptr())
     return st, o
 
 
-def test_noalloc_matches_allocating_entry_point_twice(cuda):
+# bf16 and f16 take the tensor-core decode kernel and its split plan, f32 the CUDA-core kernel and its own plan: the
+# scratch size the entry point checks must follow each of them
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_noalloc_matches_allocating_entry_point_twice(cuda, dtype):
     from duo import lib as L
     cases = [(4, 4096, [4095, 17, 2048, 3000], 1), (2, 2048, [2047, 100], 2)]
     for b, max_len, starts, seed in cases:  # two calls in a row on the shared static scratch
-        q, kc, vc, start, gate = _inputs(b, max_len, starts, seed)
+        q, kc, vc, start, gate = _inputs(b, max_len, starts, seed, dtype=dtype)
         st, o_na = _call("duo_attention_noalloc", q, kc, vc, start, gate)
         assert st == L.DUO_OK, L.lib().duo_last_error()
         st, o_ref = _call("duo_attention", q, kc, vc, start, gate)
