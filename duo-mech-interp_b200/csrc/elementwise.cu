@@ -212,6 +212,52 @@ int launch_feed_tokens(const int32_t* am, int rows, int32_t* ids, int32_t* log, 
   return DUO_OK;
 }
 
+// 16-bit -> f32 copy (the capture hooks of the 16-bit engines), 8 values per thread
+template <typename T>
+__global__ void to_f32_kernel(const T* __restrict__ src, long n8, float* __restrict__ dst) {
+  pdl_enter();
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    float v[8];
+    load8(src + 8 * i, v);
+    store8(dst + 8 * i, v);
+  }
+}
+
+int launch_to_f32(const void* src, int dtype, long n, float* dst, cudaStream_t st) {
+  if (n == 0) return DUO_OK;
+  if (n % 8 || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 31))
+    return fail(DUO_EINVAL, "to_f32: n must be a multiple of 8 and the buffers 16 / 32-byte aligned");
+  const int grid = (int)std::min<long>((n / 8 + 255) / 256, (long)sm_count() * 8);
+  if (dtype == DUO_BF16)
+    DUO_CUDA_TRY(::duo::launch_kernel(to_f32_kernel<__nv_bfloat16>, grid, 256, 0, st,
+                                      static_cast<const __nv_bfloat16*>(src), n / 8, dst));
+  else if (dtype == DUO_F16)
+    DUO_CUDA_TRY(::duo::launch_kernel(to_f32_kernel<__half>, grid, 256, 0, st, static_cast<const __half*>(src), n / 8, dst));
+  else
+    return fail(DUO_EINVAL, "to_f32: source must be bf16 or f16");
+  DUO_LAUNCH_CHECK("to_f32_kernel");
+  return DUO_OK;
+}
+
+// Per (layer, neuron) of a capture [L, T, I] over tokens t0 .. T-1: max, its first token, min, its first token
+// (engine/kernels.js:288-306).  Thread per neuron, consecutive threads on consecutive neurons (coalesced rows).
+__global__ void token_extremes_kernel(const float* __restrict__ cap, int L, int T, int I, int t0,
+                                      float* __restrict__ out) {
+  pdl_enter();
+  const int n = blockIdx.x * blockDim.x + threadIdx.x, l = blockIdx.y;
+  if (n >= I || l >= L) return;
+  float mx = -3.4e38f, mn = 3.4e38f;
+  int amx = 0, amn = 0;
+  const float* c = cap + (long)l * T * I + n;
+  for (int t = t0; t < T; t++) {
+    const float v = c[(long)t * I];
+    if (v > mx) { mx = v; amx = t; }
+    if (v < mn) { mn = v; amn = t; }
+  }
+  float4* o = reinterpret_cast<float4*>(out + ((long)l * I + n) * 4);
+  *o = make_float4(mx, (float)amx, mn, (float)amn);
+}
+
 }  // namespace duo
 
 using namespace duo;
@@ -222,4 +268,16 @@ extern "C" int duo_rmsnorm(const float* x, int m, int d, const float* w, float e
   DUO_CHECK_ARG(m == 0 || (x && w && y), "rmsnorm: null pointer");
   DUO_CHECK_ARG(valid_act(y_dtype), "rmsnorm: y dtype must be f32, bf16 or f16");
   return launch_rmsnorm(x, m, d, w, eps, offset, y, y_dtype, as_stream(stream));
+}
+
+extern "C" int duo_token_extremes(const float* cap, int layers, int t, int inter, int t0, float* out,
+                                  duo_stream stream) {
+  DUO_CHECK_ARG(layers >= 0 && t >= 0 && inter >= 0 && t0 >= 0, "token_extremes: bad sizes");
+  if (layers == 0 || inter == 0) return DUO_OK;
+  DUO_CHECK_ARG(cap && out, "token_extremes: null pointer");
+  DUO_CHECK_ARG((reinterpret_cast<uintptr_t>(out) & 15) == 0, "token_extremes: out must be 16-byte aligned");
+  DUO_CUDA_TRY(::duo::launch_kernel(token_extremes_kernel, dim3(cdiv(inter, 256), layers), 256, 0, as_stream(stream),
+                                    cap, layers, t, inter, t0, out));
+  DUO_LAUNCH_CHECK("token_extremes_kernel");
+  return DUO_OK;
 }

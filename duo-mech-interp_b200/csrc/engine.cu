@@ -16,6 +16,7 @@ using namespace duo;
 namespace {
 
 constexpr int kMaxPush = 16;  // push records per layer (the reference allows 8, model.js:415)
+constexpr int kStage = 3;     // pinned staging slots for host token ids (duo_engine_forward)
 constexpr int kGemvMax = 8;   // rows up to which projections stream int8 weights through the GEMV
 
 struct Pack {
@@ -77,9 +78,22 @@ struct duo_engine {
   std::vector<int> len;
   std::vector<LayerState> ls;
   std::vector<void*> state_owned;
-  // residual capture (model.js `resid`): copy of x after layer `cap_layer` of each forward into cap_out[M, hidden]
-  int cap_layer = -1;
-  float* cap_out = nullptr;
+  // host token ids are copied into one of kStage pinned slots and from there to the device; a slot is reused only
+  // after the copy that last read it has run (its event), so the caller's array is free when the call returns
+  int32_t* ids_stage = nullptr;
+  cudaEvent_t stage_ev[kStage] = {};
+  int stage_next = 0;
+  // capture hooks (model.js:7-12, 445-461): per kind, the slot of each layer in `out` (-1: not captured); a forward
+  // of M token rows writes its rows to out[(slot * cap_t + t0 + m) * width] (f32) and then advances t0 by M when
+  // `advance` (prefill chunks, model.js:486-491)
+  struct Capture {
+    std::vector<int> slot;
+    float* out = nullptr;
+    long cap_t = 0, t0 = 0;
+    bool advance = true;
+    bool on() const { return out != nullptr; }
+  } cap[DUO_CAP_KINDS];
+  int stop_after = -1;  // last layer a forward runs (-1: all; model.js `stopAfter`)
   // live profiling: per kind, a pool of (start, stop) event pairs recorded around launches on the stream
   unsigned prof_mask = 0;
   struct ProfKind {
@@ -113,6 +127,14 @@ struct duo_engine {
     if (i >= 0) cudaEventRecord(prof[kind].ev[i + 1], st);
   }
   void free_state() {
+    for (cudaEvent_t& ev : stage_ev)
+      if (ev) {
+        cudaEventSynchronize(ev);
+        cudaEventDestroy(ev);
+        ev = nullptr;
+      }
+    if (ids_stage) cudaFreeHost(ids_stage);
+    ids_stage = nullptr;
     for (void* p : state_owned) cudaFree(p);
     state_owned.clear();
     ls.clear();
@@ -179,6 +201,19 @@ int build_pack(duo_engine* e, const duo_q8_view& v, int n, int k, int interleave
     out->colscale = static_cast<float*>(cs);
   }
   return launch_pack16(v.q, v.s, n, k, e->gsize(k), interleave, per_row ? 0 : 1, e->act, out->w, out->colscale, st);
+}
+
+// rows [0, M) of src (dtype, row width `width`) -> the capture of `kind` for layer l, as f32
+int capture_rows(duo_engine* e, int kind, int l, const void* src, int dtype, int M, int width, cudaStream_t st) {
+  const duo_engine::Capture& k = e->cap[kind];
+  if (!k.on() || k.slot[l] < 0) return DUO_OK;
+  float* dst = k.out + ((long)k.slot[l] * k.cap_t + k.t0) * width;
+  if (dtype == DUO_F32) {
+    DUO_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)M * width * 4, cudaMemcpyDeviceToDevice, st));
+    return DUO_OK;
+  }
+  PROF_TRY(DUO_PROF_OTHER, launch_to_f32(src, dtype, (long)M * width, dst, st));
+  return DUO_OK;
 }
 
 int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, int T, int vec_layer,
@@ -263,6 +298,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.ldc = H;
       PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->o, M, out_k, L.out, e->p_out[l], H, ep, st));
     }
+    DUO_TRY(capture_rows(e, DUO_CAP_RESID_ATTN, l, e->x, DUO_F32, M, H, st));
     PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->x, M, H, L.post_norm, c.eps, 1, e->xn, act, st));
     PushTable pt{S.push_neuron, S.push_mode, S.push_vals, S.push_count, e->rows};
     if (M > kGemvMax && act != DUO_F32) {
@@ -286,6 +322,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->xn, M, H, L.gu, Pack{}, 2 * c.inter, ep, st));
       PROF_TRY(DUO_PROF_SWIGLU, launch_swiglu_push(e->y, M, c.inter, T, row_base, pt, e->a, act, st));
     }
+    DUO_TRY(capture_rows(e, DUO_CAP_ACT, l, e->a, act, M, c.inter, st));
     {
       GemmEpiArgs ep;
       ep.epi = EPI_ADD_F32;
@@ -297,10 +334,12 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.row_base = row_base;
       PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->a, M, c.inter, L.down, e->p_down[l], H, ep, st));
     }
-    if (l == e->cap_layer && e->cap_out)
-      DUO_CUDA_TRY(cudaMemcpyAsync(e->cap_out, e->x, (size_t)M * H * 4, cudaMemcpyDeviceToDevice, st));
+    DUO_TRY(capture_rows(e, DUO_CAP_RESID, l, e->x, DUO_F32, M, H, st));
+    if (l == e->stop_after) break;
   }
   PROF_TRY(DUO_PROF_OTHER, launch_finish_rows(e->x, H, T, row_base, rows, e->last, e->len_dev, st));
+  for (auto& k : e->cap)
+    if (k.on() && k.advance) k.t0 += M;
   return DUO_OK;
 }
 
@@ -342,6 +381,10 @@ int check_rows(duo_engine* e, int row_base, int rows, int T) {
   for (int r = row_base; r < row_base + rows; r++)
     if (e->len[r] + T > e->max_len)
       return fail(DUO_ESTATE, "forward: row " + std::to_string(r) + " would exceed max_len " + std::to_string(e->max_len));
+  for (const auto& k : e->cap)
+    if (k.on() && k.t0 + (long)rows * T > k.cap_t)
+      return fail(DUO_EINVAL, "forward: the capture holds " + std::to_string(k.cap_t) + " token rows per layer; this "
+                              "call would write rows " + std::to_string(k.t0) + " .. " + std::to_string(k.t0 + (long)rows * T - 1));
   return DUO_OK;
 }
 
@@ -493,6 +536,16 @@ extern "C" int duo_engine_alloc(duo_engine* e, int rows, int max_len, int max_to
     DUO_TRY(A(&p, kMaxPush * 4)); S.push_mode = (int32_t*)p;
     DUO_TRY(A(&p, (size_t)kMaxPush * rows * 4)); S.push_vals = (float*)p;
   }
+  {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, (size_t)kStage * Mx * 4, cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(DUO_ENOMEM, "engine_alloc: pinned staging of the token ids");
+    }
+    e->ids_stage = static_cast<int32_t*>(h);
+    for (cudaEvent_t& ev : e->stage_ev) DUO_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    e->stage_next = 0;
+  }
   DUO_CUDA_TRY(cudaMemset(e->len_dev, 0, rows * 4));
   DUO_CUDA_TRY(cudaMemset(e->vec, 0, (size_t)rows * c.hidden * 4));
   DUO_CUDA_TRY(cudaMemset(e->last, 0, (size_t)rows * c.hidden * 4));
@@ -518,12 +571,55 @@ extern "C" int duo_engine_reset_all(duo_engine* e, duo_stream stream) {
   return DUO_OK;
 }
 
+extern "C" int duo_engine_set_capture(duo_engine* e, int kind, int n_layers, const int32_t* layers_host, float* out,
+                                      int cap_t) {
+  DUO_CHECK_ARG(e, "null engine");
+  DUO_CHECK_ARG(kind >= 0 && kind < DUO_CAP_KINDS, "set_capture: bad kind");
+  const int L = e->cfg.layers;
+  DUO_CHECK_ARG(n_layers >= 0 && n_layers <= L, "set_capture: bad layer count");
+  duo_engine::Capture& k = e->cap[kind];
+  if (n_layers == 0) {
+    k = duo_engine::Capture{};
+    return DUO_OK;
+  }
+  DUO_CHECK_ARG(out && cap_t >= 1, "set_capture: null output or cap_t < 1");
+  std::vector<int> slot(L, -1);
+  for (int i = 0; i < n_layers; i++) {
+    const int l = layers_host ? layers_host[i] : i;
+    DUO_CHECK_ARG(l >= 0 && l < L && slot[l] < 0, "set_capture: layer out of range or listed twice");
+    slot[l] = i;
+  }
+  k.slot = std::move(slot);
+  k.out = out;
+  k.cap_t = cap_t;
+  k.t0 = 0;
+  k.advance = true;
+  return DUO_OK;
+}
+
+extern "C" int duo_engine_set_capture_t0(duo_engine* e, int kind, int t0) {
+  DUO_CHECK_ARG(e, "null engine");
+  DUO_CHECK_ARG(kind >= 0 && kind < DUO_CAP_KINDS && e->cap[kind].on(), "set_capture_t0: that capture is off");
+  DUO_CHECK_ARG(t0 >= 0 && t0 < e->cap[kind].cap_t, "set_capture_t0: t0 out of range");
+  e->cap[kind].t0 = t0;
+  return DUO_OK;
+}
+
+extern "C" int duo_engine_set_stop_after(duo_engine* e, int layer) {
+  DUO_CHECK_ARG(e, "null engine");
+  DUO_CHECK_ARG(layer >= -1 && layer < e->cfg.layers, "set_stop_after: layer out of range");
+  e->stop_after = layer == e->cfg.layers - 1 ? -1 : layer;
+  return DUO_OK;
+}
+
 extern "C" int duo_engine_capture_resid(duo_engine* e, int layer, float* out) {
   DUO_CHECK_ARG(e, "null engine");
   DUO_CHECK_ARG(layer >= -1 && layer < e->cfg.layers, "capture_resid: layer out of range");
   DUO_CHECK_ARG(layer == -1 || out, "capture_resid: null output");
-  e->cap_layer = layer;
-  e->cap_out = layer >= 0 ? out : nullptr;
+  if (layer < 0) return duo_engine_set_capture(e, DUO_CAP_RESID, 0, nullptr, nullptr, 0);
+  const int32_t one = layer;
+  DUO_TRY(duo_engine_set_capture(e, DUO_CAP_RESID, 1, &one, out, 1 << 30));
+  e->cap[DUO_CAP_RESID].advance = false;  // every forward writes its rows from row 0
   return DUO_OK;
 }
 
@@ -551,6 +647,7 @@ extern "C" int duo_engine_set_vectors(duo_engine* e, const float* vecs_host, int
   cudaStream_t st = as_stream(stream);
   DUO_CUDA_TRY(cudaMemsetAsync(e->vec, 0, (size_t)e->rows * H * 4, st));
   if (n_rows) DUO_CUDA_TRY(cudaMemcpyAsync(e->vec, vecs_host, (size_t)n_rows * H * 4, cudaMemcpyHostToDevice, st));
+  DUO_CUDA_TRY(cudaStreamSynchronize(st));  // the host array may be freed when this returns
   return DUO_OK;
 }
 
@@ -605,7 +702,14 @@ extern "C" int duo_engine_forward(duo_engine* e, const int32_t* ids_host, int ro
   DUO_TRY(check_engine(e, true, true));
   DUO_CHECK_ARG(ids_host, "forward: null ids");
   DUO_TRY(check_rows(e, row_base, rows, t));
-  DUO_CUDA_TRY(cudaMemcpyAsync(e->ids, ids_host, (size_t)rows * t * 4, cudaMemcpyHostToDevice, as_stream(stream)));
+  cudaStream_t st = as_stream(stream);
+  const int s = e->stage_next;
+  e->stage_next = (s + 1) % kStage;
+  DUO_CUDA_TRY(cudaEventSynchronize(e->stage_ev[s]));  // the copy that last read this slot has run
+  int32_t* stage = e->ids_stage + (size_t)s * std::max<long>(e->max_tokens, e->rows);
+  std::memcpy(stage, ids_host, (size_t)rows * t * 4);
+  DUO_CUDA_TRY(cudaMemcpyAsync(e->ids, stage, (size_t)rows * t * 4, cudaMemcpyHostToDevice, st));
+  DUO_CUDA_TRY(cudaEventRecord(e->stage_ev[s], st));
   return duo_engine_forward_device(e, e->ids, row_base, rows, t, vec_layer, stream);
 }
 

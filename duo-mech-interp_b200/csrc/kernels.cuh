@@ -88,6 +88,11 @@ int launch_swiglu_push(const void* gu, int m, int inter, int t, int row_base, co
                        cudaStream_t st);
 int launch_vec_add(float* x, int m, int h, int t, int row_base, const float* vec, cudaStream_t st);
 int launch_argmax(const float* logits, int m, int v, int32_t* out, cudaStream_t st);
+// 16-bit (bf16 / f16) -> f32 copy of n values (n a multiple of 8)
+int launch_to_f32(const void* src, int dtype, long n, float* dst, cudaStream_t st);
+// push-probe statistics (stats.cu): stats [n, DUO_STATS_COLS]; d [n, ldd] accumulated when not null
+int launch_push_stats(const float* logits, int n, int vocab, long ld, const int32_t* base, const int32_t* tid,
+                      const float* tlw, int nt, float* stats, float* d, long ldd, cudaStream_t st);
 int launch_finish_rows(const float* x, int h, int t, int row_base, int rows, float* last, int32_t* len,
                        cudaStream_t st);
 int launch_feed_tokens(const int32_t* am, int rows, int32_t* ids, int32_t* log, int n_steps, int step,

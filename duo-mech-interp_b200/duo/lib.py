@@ -13,6 +13,8 @@ DUO_OK, DUO_EINVAL, DUO_ECUDA, DUO_ESTATE, DUO_ENOMEM = 0, -1, -2, -3, -4
 DUO_F32, DUO_BF16, DUO_F16, DUO_I8, DUO_I32 = 0, 1, 2, 3, 4
 DUO_PUSH_ADD, DUO_PUSH_MUL = 0, 1
 DUO_ALL_NEURONS = -1
+DUO_CAP_RESID, DUO_CAP_RESID_ATTN, DUO_CAP_ACT = 0, 1, 2
+DUO_STATS_COLS = 6
 
 # every symbol the header declares, with (restype, argtypes)
 _vp, _i, _f, _u = C.c_void_p, C.c_int, C.c_float, C.c_uint
@@ -53,6 +55,11 @@ SIGNATURES = {
     "duo_gdn_chunk_fwd": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "duo_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
     "duo_attention_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp]),
+    "duo_token_extremes": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
+    "duo_engine_set_capture": (_i, [_vp, _i, _i, _vp, _vp, _i]),
+    "duo_engine_set_capture_t0": (_i, [_vp, _i, _i]),
+    "duo_engine_set_stop_after": (_i, [_vp, _i]),
+    "duo_push_stats": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "duo_fault_status": (_i, [C.POINTER(_u)]),
     "duo_fault_raise": (_i, [_u]),
     "duo_engine_create": (_i, [C.POINTER(duo_config), C.POINTER(_vp)]),

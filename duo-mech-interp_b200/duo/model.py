@@ -1,8 +1,10 @@
 """`Model`: the host-side mirror of the reference engine's Model class (engine/model.js:26-509).
 
 Same operations and argument meaning: alloc(rows, maxLen, maxT), reset(r), setVectors(rows), setHeadScales,
-_forward(ids, rowBase, rows, T, opts) with opts = {pushes: {layer: [{n, mode, vals}]}, vec: layer}, prefill(r, ids,
-opts) chunked by maxT, step(ids, opts), logitsRow(r), logitsAll(), argmaxAll().  Names are snake_case; errors raise
+_forward(ids, rowBase, rows, T, opts) with opts = {pushes: {layer: [{n, mode, vals}]}, vec: layer, resid: true |
+"attn", residBuf, capture, capLayers, capT, capT0, stopAfter} (model.js:7-12, 404-466; the buffers are CUDA f32
+tensors [layers, capT, hidden] and [len(capLayers), capT, inter]), prefill(r, ids, opts) chunked by maxT with capT0
+advancing per chunk, step(ids, opts), logitsRow(r), logitsAll(), argmaxAll().  Names are snake_case; errors raise
 (the reference throws, model.js:52, 406, 418).  All compute runs in libduo_mixer.so; this file only moves arguments.
 """
 import ctypes as C
@@ -62,7 +64,6 @@ class Model:
         L.call("duo_engine_alloc", self._h, rows, max_len, self.max_tokens)
         self.rows = rows
         self._pushes = {}
-        self._ids_pinned = torch.empty(self.max_tokens, dtype=torch.int32, pin_memory=True)
         return self
 
     def reset(self, r):
@@ -123,29 +124,68 @@ class Model:
             self._pushes[l] = key
 
     # ---- forward (model.js:404-508)
+    def _set_hooks(self, opts):
+        """The per-call capture / stopAfter options (model.js:427, 445-461); returns the kinds it turned on."""
+        on = []
+        cap_t = opts.get("capT")
+        t0 = int(opts.get("capT0", 0) or 0)
+        if opts.get("resid"):
+            kind = L.DUO_CAP_RESID_ATTN if opts["resid"] == "attn" else L.DUO_CAP_RESID
+            buf = opts["residBuf"]
+            L.call("duo_engine_set_capture", self._h, kind, self.cfg.num_hidden_layers, None, L.ptr(buf),
+                   int(cap_t or buf.shape[1]))
+            on.append(kind)
+        if opts.get("capture") is not None:
+            buf = opts["capture"]
+            layers = opts.get("capLayers")
+            arr = None if layers is None else np.ascontiguousarray(np.asarray(layers, dtype=np.int32))
+            n = self.cfg.num_hidden_layers if layers is None else len(layers)
+            L.call("duo_engine_set_capture", self._h, L.DUO_CAP_ACT, n,
+                   None if arr is None else arr.ctypes.data_as(C.c_void_p), L.ptr(buf), int(cap_t or buf.shape[1]))
+            on.append(L.DUO_CAP_ACT)
+        for kind in on:
+            if t0:
+                L.call("duo_engine_set_capture_t0", self._h, kind, t0)
+        if opts.get("stopAfter") is not None:
+            L.call("duo_engine_set_stop_after", self._h, int(opts["stopAfter"]))
+        return on
+
+    def _clear_hooks(self, on, opts):
+        for kind in on:
+            L.call("duo_engine_set_capture", self._h, kind, 0, None, None, 0)
+        if opts.get("stopAfter") is not None:
+            L.call("duo_engine_set_stop_after", self._h, -1)
+
     def forward(self, ids, row_base, rows, T, opts=None):
         """_forward: rows consecutive sequences from row_base, T new tokens each (ids token-major, len rows * T)."""
         opts = opts or {}
         self._set_pushes(opts.get("pushes"))
+        hooks = self._set_hooks(opts)
+        try:
+            self._forward(ids, row_base, rows, T, opts)
+        finally:
+            self._clear_hooks(hooks, opts)
+
+    def _forward(self, ids, row_base, rows, T, opts):
         vec = opts.get("vec")
         vec = -1 if vec is None else int(vec)
         if torch.is_tensor(ids) and ids.is_cuda:
             ids = ids.to(torch.int32).contiguous()
             L.call("duo_engine_forward_device", self._h, L.ptr(ids), row_base, rows, T, vec, self._s())
             return
-        n = rows * T
-        if n > self._ids_pinned.numel():
-            raise L.DuoError(L.DUO_EINVAL, f"forward: rows * T = {n} exceeds max_tokens {self._ids_pinned.numel()}")
-        host = self._ids_pinned[:n]
-        host.copy_(torch.as_tensor(np.asarray(ids, dtype=np.int32).reshape(-1)))
-        L.call("duo_engine_forward", self._h, L.ptr(host), row_base, rows, T, vec, self._s())
+        host = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        if host.size != rows * T:
+            raise L.DuoError(L.DUO_EINVAL, f"forward: {host.size} ids for rows * T = {rows * T}")
+        # the engine copies the ids into its own pinned staging before returning: `host` may go away after the call
+        L.call("duo_engine_forward", self._h, host.ctypes.data_as(C.c_void_p), row_base, rows, T, vec, self._s())
 
     def prefill(self, r, ids, opts=None):
         """Prefill row r with ids from its current length, in chunks of max_t tokens (model.js:486-491)."""
         ids = list(ids) if not torch.is_tensor(ids) else ids
+        opts = opts or {}
         for i in range(0, len(ids), self.max_t):
             chunk = ids[i:i + self.max_t]
-            self.forward(chunk, r, 1, len(chunk), opts)
+            self.forward(chunk, r, 1, len(chunk), {**opts, "capT0": int(opts.get("capT0", 0) or 0) + i})
 
     def step(self, ids, opts=None):
         """Decode one token for every row (ids[r] for row r) (model.js:508)."""

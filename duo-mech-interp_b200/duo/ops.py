@@ -162,3 +162,15 @@ def fault_status():
     v = C.c_uint(0)
     call("duo_fault_status", C.byref(v))
     return v.value
+
+
+def push_stats(logits, base, targets, target_logw=None, d=None, stream=None):
+    """Next-token statistics of the push probe (engine/analysis.js:480-537) over logits [n, vocab] f32: returns stats
+    [n, 6] = (lse, mass, tlse, kl, dp, gain); kl / dp / gain against row base[r] (-1: none); d [n, vocab] (optional)
+    is accumulated with lp - lp[base] in place."""
+    _dev(logits, base, targets, target_logw, d)
+    n, vocab = logits.shape
+    stats = torch.empty(n, 6, dtype=torch.float32, device=logits.device)
+    call("duo_push_stats", ptr(logits), n, vocab, ptr(base), ptr(targets), ptr(target_logw), targets.numel(),
+         ptr(stats), ptr(d), stream_ptr(stream))
+    return stats, d

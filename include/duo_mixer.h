@@ -157,6 +157,29 @@ int duo_attention_noalloc(const void* q, const void* kc, const void* vc, const i
                           int gate_stride, void* o, int dtype, int b, int t, int nh, int nkv, int hd, int max_len,
                           float scale, duo_stream stream);
 
+/* Per (layer, neuron) of a capture cap [layers, t, inter] f32 over tokens t0 .. t - 1: out[(l * inter + n) * 4 + 0..3] =
+ * max, its first token, min, its first token (token indices as f32; out 16-byte aligned).  Replaces `tokenExtremes`,
+ * engine/kernels.js:288-306 (used on DUO_CAP_ACT captures, analysis.js:612-613). */
+int duo_token_extremes(const float* cap, int layers, int t, int inter, int t0, float* out, duo_stream stream);
+
+/* Next-token statistics of the push probe (engine/analysis.js:480-537; its PyTorch form tools/find_steering.py:86-103)
+ * over logits [n, vocab] f32 (row-major, from duo_engine_logits).  With lp = logits - lse (log-softmax, analysis.js:
+ * 693-702), row r gets stats[r * DUO_STATS_COLS + c]:
+ *   DUO_STAT_LSE   lse = log sum_i exp(logits[r, i])
+ *   DUO_STAT_MASS  mass = sum_j exp(lp[r, targets[j]])                      (probability on the target ids)
+ *   DUO_STAT_TLSE  tlse = log sum_j exp(lp[r, targets[j]] + target_logw[j])  (target_logw may be NULL: zeros)
+ * and, when base_row[r] >= 0 (the unsteered row of the same context; its own stats are read, not changed):
+ *   DUO_STAT_KL    kl = sum over i with p_i > 1e-12 of p_i (lp[r, i] - lp[base, i])   (analysis.js:704-708)
+ *   DUO_STAT_DP    mass[r] - mass[base];   DUO_STAT_GAIN  tlse[r] - tlse[base]
+ *   d[r, i] += lp[r, i] - lp[base, i] over the vocabulary when d [n, vocab] is not NULL (analysis.js:523)
+ * Rows with base_row[r] < 0 get kl = dp = gain = 0 and leave d alone.  base_row, targets, target_logw, stats and d
+ * are device arrays.  Out-of-range target ids count as probability 0. */
+enum duo_stat_col {
+  DUO_STAT_LSE = 0, DUO_STAT_MASS, DUO_STAT_TLSE, DUO_STAT_KL, DUO_STAT_DP, DUO_STAT_GAIN, DUO_STATS_COLS
+};
+int duo_push_stats(const float* logits, int n, int vocab, const int32_t* base_row, const int32_t* targets,
+                   const float* target_logw, int n_targets, float* stats, float* d, duo_stream stream);
+
 /* ============================================================================================================
  * Engine: mirrors engine/model.js `Model` (alloc, reset, setVectors, setHeadScales, _forward, _logits, argmaxAll)
  * ============================================================================================================ */
@@ -207,10 +230,26 @@ int duo_engine_alloc(duo_engine* e, int rows, int max_len, int max_tokens);
 int duo_engine_reset(duo_engine* e, int row, duo_stream stream);
 /* reset(r) for every row at once. */
 int duo_engine_reset_all(duo_engine* e, duo_stream stream);
-/* The `resid` hook of model.js:7-12, 461 for one layer: every later forward copies the residual stream after layer
- * `layer` (after its MLP and vector add) into out[rows * T, hidden] (f32, device).  layer = -1 turns it off. */
+/* The capture hooks of model.js:7-12, 445-461 (`resid: true`, `resid: "attn"`, `capture` with capLayers / capT /
+ * capT0).  For every later forward of M = rows * T token rows (row-major: row_base's T tokens first), the i-th listed
+ * layer writes its M rows to out[(i * cap_t + t0 + m) * width], f32, then t0 advances by M (as prefill's chunks
+ * advance capT0, model.js:486-491); t0 starts at 0 and duo_engine_set_capture_t0 sets it.  Kinds:
+ *   DUO_CAP_RESID       residual stream after the layer's MLP and vector add (width hidden; `resid: true`)
+ *   DUO_CAP_RESID_ATTN  residual stream after the layer's mixer out-projection (width hidden; `resid: "attn"`)
+ *   DUO_CAP_ACT         down_proj input silu(gate) * up after the pushes (width inter; `capture`)
+ * layers_host NULL lists layers 0 .. n_layers - 1; n_layers = 0 turns the kind off.  A forward that would write past
+ * cap_t rows fails with DUO_EINVAL before launching anything.  `out` is device memory the caller keeps alive. */
+enum duo_capture_kind { DUO_CAP_RESID = 0, DUO_CAP_RESID_ATTN = 1, DUO_CAP_ACT = 2, DUO_CAP_KINDS = 3 };
+int duo_engine_set_capture(duo_engine* e, int kind, int n_layers, const int32_t* layers_host, float* out, int cap_t);
+int duo_engine_set_capture_t0(duo_engine* e, int kind, int t0);
+/* Every later forward runs layers 0 .. layer only (model.js `stopAfter`, 427); -1 runs them all.  Row lengths and
+ * last hidden states advance as for a full forward (model.js:463-465). */
+int duo_engine_set_stop_after(duo_engine* e, int layer);
+/* Shorthand for one DUO_CAP_RESID layer whose rows always start at row 0 of out[rows * T, hidden]; layer = -1 turns
+ * it off. */
 int duo_engine_capture_resid(duo_engine* e, int layer, float* out);
-/* setVectors(rows) (model.js:372-376): vecs_host [n_rows, hidden]; rows >= n_rows get zero vectors. */
+/* setVectors(rows) (model.js:372-376): vecs_host [n_rows, hidden]; rows >= n_rows get zero vectors.  Synchronises
+ * `stream` before returning (vecs_host may be freed then). */
 int duo_engine_set_vectors(duo_engine* e, const float* vecs_host, int n_rows, duo_stream stream);
 /* setHeadScales (model.js:362-369) for one linear-attention layer; NULL restores all ones. */
 int duo_engine_set_head_scales(duo_engine* e, int layer, const float* scales_host, duo_stream stream);
@@ -220,7 +259,9 @@ int duo_engine_set_head_scales(duo_engine* e, int layer, const float* scales_hos
 int duo_engine_set_pushes(duo_engine* e, int layer, int n, const int32_t* neurons_host, const int32_t* modes_host,
                           const float* vals_host, duo_stream stream);
 /* _forward(ids, rowBase, rows, T, {vec}) (model.js:404-466): ids_host [rows * T] token-major; vec_layer = -1 for
- * none.  Copies the ids to the device on `stream`.  Leaves each row's final hidden state in the engine. */
+ * none.  The ids are copied into engine-owned pinned memory during the call and from there to the device on
+ * `stream` (a few slots in turn; the call waits only if the copy that last used its slot has not run yet), so the
+ * caller may reuse ids_host as soon as the call returns.  Leaves each row's final hidden state in the engine. */
 int duo_engine_forward(duo_engine* e, const int32_t* ids_host, int row_base, int rows, int t, int vec_layer,
                        duo_stream stream);
 /* Same with device-resident ids (no host traffic; capturable in a CUDA graph). */

@@ -43,8 +43,12 @@ class OracleModel:
     """CPU restatement of the engine's Model with its per-row state (model.js:308-360)."""
 
     # Where the 16-bit engines round an intermediate to bf16 / f16 (everything else stays f32): each name marks one
-    # such point in forward() / logits().  round_points maps names to a rounding function (empty: pure f32).
-    ROUND_POINTS = ("norm_in", "proj", "conv", "scan_out", "attn_q", "kv", "attn_out", "norm_post", "mlp_act",
+    # such point in forward() / logits().  round_points maps names to a rounding function (empty: pure f32).  Two
+    # follow the engine's kernel structure: "conv" (the conv prologue's q / k / v) is not rounded in a decode step
+    # (T = 1, hk = hv), whose fused DeltaNet kernel keeps them in registers; "gu" (the gate|up projection stored before
+    # a separate SwiGLU kernel) exists only in forwards of at most gemv_max token rows, which run the int8 GEMV --
+    # larger ones fuse SwiGLU into the tensor-core GEMM's epilogue.
+    ROUND_POINTS = ("norm_in", "proj", "conv", "scan_out", "attn_q", "kv", "attn_out", "norm_post", "gu", "mlp_act",
                     "final")
 
     def __init__(self, cfg, weights, rows, max_len, dtype=torch.float32, round_points=None, gemm_weights=None,
@@ -98,7 +102,11 @@ class OracleModel:
             self.head_scales[l] = torch.ones(self.cfg.hv, dtype=self.dt) if s is None else torch.as_tensor(s, dtype=self.dt)
 
     # -- forward (model.js:404-466)
-    def forward(self, ids, row_base, rows, T, pushes=None, vec=None, capture_resid=False):
+    def forward(self, ids, row_base, rows, T, pushes=None, vec=None, capture_resid=False, capture=None,
+                stop_after=None):
+        """capture: optional dict that receives, per layer, "resid_attn" (after the mixer's out-projection), "act" (the
+        down_proj input after pushes) and "resid" (after the MLP and vector add) as lists of [M, width] tensors
+        (model.js:445-461); stop_after: last layer to run (model.js:427)."""
         c, dt = self.cfg, self.dt
         M = rows * T
         w = self.w_gemm if (self.w_gemm is not None and M > self.gemv_max) else self.w
@@ -117,8 +125,12 @@ class OracleModel:
             else:
                 o = self._attention(l, L, y, row_base, rows, T, pos)
             x = x + o @ L["out"].to(dt).T
+            if capture is not None:
+                capture.setdefault("resid_attn", []).append(x.clone())
             xn = self._r("norm_post", mixer.rmsnorm(x, L["post_norm"], c.eps).to(dt))
             gu = xn @ L["gu"].to(dt).T
+            if M <= self.gemv_max:
+                gu = self._r("gu", gu)
             a = F.silu(gu[:, : c.inter]) * gu[:, c.inter:]
             for rec in pushes.get(l, []):  # kernels_qwen35.js:270-276, in record order
                 vals = torch.as_tensor([rec["vals"][int(r)] if int(r) < len(rec["vals"]) else
@@ -129,11 +141,17 @@ class OracleModel:
                 else:
                     a[:, cols] = a[:, cols] + (vals[:, None] if rec.get("n") is None else vals)
             a = self._r("mlp_act", a)
+            if capture is not None:
+                capture.setdefault("act", []).append(a.clone())
             x = x + a @ L["down"].to(dt).T
             if vec == l:  # kernels.js:190-203, one vector per absolute row
                 x = x + self.vectors[row_of]
             if capture_resid:
                 resid.append(x.clone())
+            if capture is not None:
+                capture.setdefault("resid", []).append(x.clone())
+            if stop_after is not None and l == stop_after:
+                break
         for i in range(rows):
             self.last[row_base + i] = x[i * T + T - 1]
             self.len[row_base + i] += T
@@ -152,15 +170,16 @@ class OracleModel:
         conv_out = conv_out.to(dt)
         q = conv_out[..., : c.kd].reshape(rows, T, c.hk, c.dk)
         k = conv_out[..., c.kd: 2 * c.kd].reshape(rows, T, c.hk, c.dk)
-        v = self._r("conv", conv_out[..., 2 * c.kd:].reshape(rows, T, c.hv, c.dv))
-        if "conv" in self.round_points:  # the engine's conv writes q and k already l2-normalised
-            q, k = self._r("conv", mixer.l2norm(q)), self._r("conv", mixer.l2norm(k))
+        v = conv_out[..., 2 * c.kd:].reshape(rows, T, c.hv, c.dv)
+        conv_rounded = "conv" in self.round_points and not (T == 1 and c.hk == c.hv)
+        if conv_rounded:  # the engine's conv writes q and k already l2-normalised
+            q, k, v = self._r("conv", mixer.l2norm(q)), self._r("conv", mixer.l2norm(k)), self._r("conv", v)
         if c.hv // c.hk > 1:
             q = q.repeat_interleave(c.hv // c.hk, dim=2)
             k = k.repeat_interleave(c.hv // c.hk, dim=2)
         beta, g = mixer.gdn_gates(a, b, L["alog"], L["dtb"])
         rule = mixer.recurrent_gated_delta_rule if T == 1 else mixer.chunk_gated_delta_rule
-        o, s = rule(q, k, v, g.to(dt), beta.to(dt), state=self.S[l][rs], l2norm_qk="conv" not in self.round_points)
+        o, s = rule(q, k, v, g.to(dt), beta.to(dt), state=self.S[l][rs], l2norm_qk=not conv_rounded)
         self.S[l][rs] = s.to(dt)
         o = mixer.gated_rmsnorm(o, z, L["gnorm"], c.eps).to(dt)
         o = o * self.head_scales[l][None, None, :, None]

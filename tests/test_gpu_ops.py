@@ -374,3 +374,32 @@ def test_attention_decode_config3(ops, dtype, ragged):
     o = ops.attention(q, kc, vc, start, gate=gate)
     ref = _attn_ref(q.float().cpu(), kc.float().cpu(), vc.float().cpu(), starts, gate.float().cpu())
     assert rel_max(o.float(), ref) < 2e-2
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# push-probe statistics (engine/analysis.js:480-537): lse, target mass and weighted target lse per row; KL, dp, gain
+# and the per-vocabulary delta against each row's unsteered row
+
+
+@pytest.mark.parametrize("n,vocab", [(6, 248320), (9, 1001), (216, 248320)])
+def test_push_stats(ops, n, vocab):
+    from oracle import probe
+    gen = _seed(n + vocab)
+    logits = torch.randn(n, vocab, generator=gen) * 3
+    # triples (+, 0, -) of one context: the middle row is the base of the other two
+    base = torch.tensor([(r // 3) * 3 + 1 if r % 3 != 1 else -1 for r in range(n)], dtype=torch.int32)
+    for r in range(n):
+        if r % 3 != 1:  # a steered row: its logits move away from the base a little
+            logits[r] = logits[(r // 3) * 3 + 1] + torch.randn(vocab, generator=gen) * 0.3
+    targets = torch.randint(0, vocab, (64,), generator=gen, dtype=torch.int32)
+    targets[5] = vocab + 3  # an out-of-range id counts as probability 0
+    logw = torch.log(torch.rand(64, generator=gen) + 0.1)
+    d0 = torch.randn(n, vocab, generator=gen)
+    stats, d = ops.push_stats(logits.cuda(), base.cuda(), targets.cuda(), logw.cuda(), d=d0.clone().cuda())
+    rs, rd = probe.push_stats(logits.numpy(), base.numpy(), targets.numpy(), logw.numpy())
+    st = stats.double().cpu().numpy()
+    for c in range(6):
+        err = np.abs(st[:, c] - rs[:, c])
+        assert (err <= 1e-5 + 1e-4 * np.abs(rs[:, c])).all(), (c, err.max())
+    assert rel_max(d, torch.from_numpy(rd) + d0.double()) < 1e-5
+    assert ops.fault_status() == 0
