@@ -264,8 +264,9 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
         PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_decode(ca, sa, act, st));
       } else {
         PROF_TRY(DUO_PROF_GDN_CONV, launch_gdn_conv(ca, act, st));
-        // prefill of the 16-bit engines: chunked tensor-core scan; the f32 engine: the recurrent form
-        if (act != DUO_F32 && T > 16) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
+        // prefill of the 16-bit engines (any T > 1; a short call is one partial chunk): chunked tensor-core scan;
+        // the f32 engine: the recurrent form
+        if (act != DUO_F32 && T > 1) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
         else PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_recurrent(sa, act, st));
       }
       out_k = e->vd;

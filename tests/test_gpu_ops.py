@@ -212,7 +212,7 @@ def test_gdn_recurrent_bf16(ops):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("b,t,h,l2", [(1, 64, 2, False), (2, 100, 4, True), (1, 300, 16, False), (3, 17, 2, True),
-                                      (2, 1024, 16, False)])
+                                      (2, 1024, 16, False), (4, 2, 16, False), (3, 5, 4, True), (216, 16, 16, False)])
 def test_gdn_chunk_16bit(ops, dtype, b, t, h, l2):
     """Chunked tensor-core scan vs the oracle's chunk rule (f64) on the same 16-bit inputs; 16-bit bound 2e-2."""
     q, k, v, g, beta, s0 = _gdn_inputs(b, t, h, 1000 + t, not l2)
