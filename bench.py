@@ -15,6 +15,8 @@ collects the generated tokens (config5) or the statistics and logits (config4). 
 batch: reset, prefill, decode / statistics, gather.
 
     python bench.py [--gpus N --steps K --warmup W] [--workload config4]    # our engine (one JSON line on rank 0)
+    python bench.py --workload ops                                          # op cases of configs 2 / 3 and the
+                                                                            # projections, one line ("ops" list)
     python bench.py --impl reference [--steps K --warmup W]                  # the reference's CPU PyTorch path
 """
 import argparse
@@ -39,7 +41,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["duo", "reference"], default="duo")
-    ap.add_argument("--workload", choices=["config5", "config4"], default="config5")
+    ap.add_argument("--workload", choices=["config5", "config4", "ops"], default="config5")
+    ap.add_argument("--no-ops", action="store_true", help="config5: skip the op cases appended to the line")
+    ap.add_argument("--op", default=None, help="ops: run only the cases whose name starts with this")
     ap.add_argument("--rows", type=int, default=256, help="config5: rows of the whole batch (split across GPUs)")
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--decode", type=int, default=512)
@@ -300,6 +304,208 @@ def max_over_ranks(ms, world):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# op cases: config 2 (chunked DeltaNet prefill, recurrent decode step), config 3 (gated attention prefill and decode),
+# the int8 GEMV of the M <= 8 decode path and the forward's projection GEMMs beside cuBLAS.  Each is timed with CUDA
+# events around replays of a CUDA graph of its launches (host launch cost excluded), after warm-up, on inputs larger
+# than L2 or rotated through enough copies that every launch reads them from HBM; one dict per case with the
+# algorithmic work per launch, the achieved rate and its fraction of the measured peak.
+
+
+def op_timed(fn, iters=10, warmup=3):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / (reps * iters)
+
+
+def op_report(case, shape, ms, flops=None, bytes_=None, target=None, extra=None):
+    pk, src = peaks()
+    r = {"case": case, "shape": shape, "ms": round(ms, 5)}
+    if flops is not None:
+        r.update(bound="tensor", achieved=flops / ms / 1e9, unit="TFLOP/s", peak=pk["bf16_tflops"])
+    else:
+        r.update(bound="hbm", achieved=bytes_ / ms / 1e6, unit="GB/s", peak=pk["hbm_gbs"])
+    r["frac"] = r["achieved"] / r["peak"]
+    r["peak_source"] = src
+    if target is not None:
+        r["north_star_target"] = target
+    r.update(extra or {})
+    return r
+
+
+def op_gdn_inputs(b, t, h=16, copies=1, seed=0):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    mk = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    q = torch.nn.functional.normalize(mk(b, t, h, 128), dim=-1).to(torch.bfloat16)
+    k = torch.nn.functional.normalize(mk(b, t, h, 128), dim=-1).to(torch.bfloat16)
+    v = mk(b, t, h, 128).to(torch.bfloat16)
+    beta = torch.sigmoid(mk(b, t, h))
+    gg = -torch.nn.functional.softplus(mk(b, t, h))
+    return q, k, v, gg, beta, [torch.zeros(b, h, 128, 128, device="cuda") for _ in range(copies)]
+
+
+def op_gdn_prefill(b, t, h=16):
+    """config 2a: the chunked scan over b rows x t tokens x 16 heads; 11.62 MFLOP per (64-token chunk, head)."""
+    from duo import ops
+    q, k, v, gg, beta, st = op_gdn_inputs(b, t, h)
+    ms = op_timed(lambda: ops.gdn_chunk(q, k, v, gg, beta, st[0], l2norm_qk=False), iters=5)
+    c = 64
+    flops = b * h * (t / c) * (5 * 2 * c * c * 128 + 3 * 2 * c * 128 * 128 + c ** 3 / 3)
+    return op_report("gdn_chunk_prefill", {"b": b, "t": t, "h": h}, ms, flops=flops, target=">= 0.50 at T >= 4096")
+
+
+def op_gdn_decode(b, steps=64, h=16):
+    """config 2b: single-token steps carrying the f32 state (2 x 64 KiB per row-head + q/k/v/o), the state rotated
+    through enough copies to stream from HBM."""
+    import math
+    from duo import ops
+    copies = max(1, math.ceil(4 * 126e6 / (b * h * 128 * 128 * 4)))
+    q, k, v, gg, beta, states = op_gdn_inputs(b, steps, h, copies=copies)
+    sl = [tuple(x[:, i:i + 1].contiguous() for x in (q, k, v, gg, beta)) for i in range(steps)]
+    it = {"i": 0}
+
+    def one():
+        i = it["i"]
+        it["i"] += 1
+        qq, kk, vv, g1, b1 = sl[i % steps]
+        ops.gdn_recurrent(qq, kk, vv, g1, b1, states[i % copies], l2norm_qk=False)
+
+    ms = op_timed(one, iters=steps, warmup=8)
+    return op_report("gdn_decode_step", {"b": b, "h": h, "state_copies": copies}, ms,
+                     bytes_=b * h * (2 * 128 * 128 * 4 + 4 * 128 * 2 + 8), target=">= 0.70")
+
+
+def op_attn_prefill(b, t):
+    """config 3a: causal GQA prefill (8 q / 2 kv heads, hd 256) with the sigmoid gate; 2 b nh hd t^2 FLOP."""
+    import torch
+    from duo import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    mk = lambda *s: torch.randn(*s, device="cuda", generator=g).to(torch.bfloat16)
+    q, gate, kc, vc = mk(b, t, 8, 256), mk(b, t, 8, 256), mk(b, t, 2, 256), mk(b, t, 2, 256)
+    start = torch.zeros(b, dtype=torch.int32, device="cuda")
+    ms = op_timed(lambda: ops.attention(q, kc, vc, start, gate=gate), iters=3)
+    return op_report("attn_prefill", {"b": b, "t": t}, ms, flops=2.0 * b * 8 * 256 * t * t,
+                     target=">= 0.50 at T >= 4096")
+
+
+def op_attn_decode(b, length):
+    """config 3b: one new token per row against a `length`-token bf16 KV cache (B = 32 x 8192: 537 MB)."""
+    import torch
+    from duo import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    mk = lambda *s: torch.randn(*s, device="cuda", generator=g).to(torch.bfloat16)
+    q, gate, kc, vc = mk(b, 1, 8, 256), mk(b, 1, 8, 256), mk(b, length + 1, 2, 256), mk(b, length + 1, 2, 256)
+    start = torch.full((b,), length, dtype=torch.int32, device="cuda")
+    ms = op_timed(lambda: ops.attention(q, kc, vc, start, gate=gate), iters=20)
+    return op_report("attn_decode", {"b": b, "cache": length}, ms,
+                     bytes_=b * (length + 1) * 2 * 256 * 2 * 2 + 2 * q.numel() * 2)
+
+
+def op_gemv(m, n, k, group=128):
+    """The int8 GEMV of decode (m <= 8 rows): y = x . dequant(W)^T, int8 W [n, k] with an f32 scale per 128-group,
+    bf16 x and y; the weights rotated through copies so that every launch streams them from HBM."""
+    import math
+    import torch
+    from duo import ops
+    copies = max(1, math.ceil(4 * 126e6 / (n * k)))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qs = [torch.randint(-127, 128, (n, k), device="cuda", generator=g, dtype=torch.int8) for _ in range(copies)]
+    ss = [torch.rand(n, k // group, device="cuda", generator=g) * 0.01 for _ in range(copies)]
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    it = {"i": 0}
+
+    def one():
+        i = it["i"] % copies
+        it["i"] += 1
+        ops.q8_gemv(x, qs[i], ss[i], y=y)
+
+    ms = op_timed(one, iters=max(8, copies), warmup=copies)
+    return op_report("q8_gemv", {"m": m, "n": n, "k": k, "group": group, "weight_copies": copies}, ms,
+                     bytes_=n * k + n * (k // group) * 4 + m * k * 2 + m * n * 2, target=">= 0.70")
+
+
+def op_gemm_decode(m=256, iters=8):
+    """The forward's projection shapes at m decode rows with int8-valued weights and the per-row scale in the
+    epilogue, as the engine runs them, each launch reading its own weight copy from HBM; cuBLAS (bf16, no scale, no
+    SwiGLU; for the residual add an f32 matmul plus the add) beside each."""
+    import torch
+    from duo import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    out = []
+    for n, k, epi in [(8224, 1024, "store"), (5120, 1024, "store"), (7168, 1024, "swiglu"), (1024, 2048, "add"),
+                      (1024, 3584, "add")]:
+        a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+        ws = [torch.randint(-127, 128, (n, k), device="cuda", generator=g).to(torch.bfloat16) for _ in range(iters)]
+        cs = torch.rand(n, device="cuda", generator=g) * 1e-3 + 1e-4
+        it, it2 = iter(range(1 << 30)), iter(range(1 << 30))
+        if epi == "add":
+            c = torch.zeros(m, n, device="cuda", dtype=torch.float32)
+            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], col_scale=cs, out=c, accumulate=True)
+            ref = lambda: c.add_(torch.matmul(a, ws[next(it2) % iters].T).float())
+        elif epi == "swiglu":
+            run = lambda: ops.gemm_swiglu(a, ws[next(it) % iters], col_scale=cs)
+            ref = lambda: torch.matmul(a, ws[next(it2) % iters].T)
+        else:
+            c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], col_scale=cs, out=c)
+            ref = lambda: torch.matmul(a, ws[next(it2) % iters].T, out=c)
+        ms, ms_ref = op_timed(run, iters), op_timed(ref, iters)
+        out.append(op_report("gemm_decode", [m, n, k], ms, bytes_=n * k * 2 + m * k * 2,
+                             extra={"epilogue": epi, "cublas_ms": round(ms_ref, 5)}))
+        del ws
+    return out
+
+
+def op_cases(full, only=None):
+    """Every op case (full) or the compact set that the default run appends to its line; `only` keeps the cases
+    whose name starts with it (gdn_chunk_prefill, gdn_decode_step, attn_prefill, attn_decode, q8_gemv, gemm_decode)."""
+    todo = [("gdn_chunk_prefill", op_gdn_prefill, (8, 4096)), ("gdn_decode_step", op_gdn_decode, (8,)),
+            ("attn_prefill", op_attn_prefill, (4, 4096)), ("attn_decode", op_attn_decode, (32, 8192)),
+            ("q8_gemv", op_gemv, (1, 248320, 1024))]
+    if full:
+        todo += [("gdn_chunk_prefill", op_gdn_prefill, (b, t)) for b in (1, 8) for t in (512, 16384)]
+        todo += [("gdn_chunk_prefill", op_gdn_prefill, (1, 4096)), ("gdn_decode_step", op_gdn_decode, (1,)),
+                 ("attn_prefill", op_attn_prefill, (4, 1024)), ("attn_prefill", op_attn_prefill, (4, 16384))]
+        todo += [("q8_gemv", op_gemv, s) for s in [(1, 8224, 1024), (3, 8224, 1024), (8, 7168, 1024),
+                                                    (3, 248320, 1024)]]
+        todo += [("gemm_decode", op_gemm_decode, (256,))]
+    cases = []
+    for name, fn, args in todo:
+        if only and not name.startswith(only):
+            continue
+        r = fn(*args)
+        cases += r if isinstance(r, list) else [r]
+    return cases
+
+
+def bench_ops(a):
+    import torch
+    cases = op_cases(full=True, only=a.op)
+    return {"metric": "mixer op roofline fractions (configs 2 and 3, int8 GEMV, decode projections)",
+            "value": min(c["frac"] for c in cases), "unit": "fraction of measured peak (min over the cases run)", "n_gpus": 1, "steps": 1, "warmup": 3, "higher_is_better": True, "scaling": "none",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) inputs as configs 2 and 3 state)",
+            "config": {"workload": "op cases of configs 2 and 3, the int8 GEMV and the decode projection GEMMs"},
+            "ops": cases, "gpu": torch.cuda.get_device_name()}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -607,7 +813,18 @@ def main():
     cfg = duo.qwen35_0p8b(group=0, act_dtype="bf16")
     W = random_weights(cfg, seed=a.seed)
     stream = torch.cuda.Stream()
+    if a.workload == "ops":
+        if rank == 0:
+            print(json.dumps(bench_ops(a)), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     line = (bench_config4 if a.workload == "config4" else bench_config5)(a, world, rank, local, stream, cfg, W)
+    if a.workload == "config5" and rank == 0 and world == 1 and not a.no_ops:
+        del W
+        torch.cuda.empty_cache()
+        line["ops"] = op_cases(full=False)  # config 2 / 3 / int8 GEMV cases, timed after the step (not in `value`)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
