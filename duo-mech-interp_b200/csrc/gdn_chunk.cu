@@ -605,10 +605,21 @@ static int run_chunk(const GdnScanArgs& a, cudaStream_t st) {
 
 long gdn_chunk_ws_bytes(int b, int t, int h) { return (long)b * h * ((t + CK - 1) / CK) * CHUNK_WS; }
 
+static bool chunk_tc_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("DUO_CHUNK_TC");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int launch_gdn_chunk(const GdnScanArgs& a, int dtype, cudaStream_t st) {
   if (a.b == 0 || a.t == 0) return DUO_OK;
   if (a.dk != 128 || a.dv != 128) return fail(DUO_EINVAL, "gdn_chunk: needs dk = dv = 128");
   if (a.hq <= 0 || a.h % a.hq) return fail(DUO_EINVAL, "gdn_chunk: value heads must be a multiple of q/k heads");
+  // 16-bit inputs without the l2norm option: the tcgen05 kernel (no workspace); DUO_CHUNK_TC=0 keeps the warp-level
+  // two-kernel form, which also serves f32 inputs and l2norm_qk
+  if (chunk_tc_enabled() && gdn_chunk_tc_eligible(a, dtype)) return launch_gdn_chunk_tc(a, dtype, st);
   if ((a.q_stride | a.k_stride | a.v_stride) % 4)
     return fail(DUO_EINVAL, "gdn_chunk: q/k/v token strides must be multiples of 4 elements");
   if (!a.chunk_ws || a.chunk_ws_bytes < gdn_chunk_ws_bytes(a.b, a.t, a.h))

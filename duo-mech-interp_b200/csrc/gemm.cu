@@ -328,6 +328,23 @@ int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long 
   return DUO_OK;
 }
 
+int make_tmap_3d_16(CUtensorMap* map, const void* base, int dtype, long d0, long d1, long d2, long s1, long s2,
+                    int box0, int box1) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || s1 % 16 || s2 % 16 || (box0 * 2) % 16)
+    return fail(DUO_EINVAL, "tensor map: base, strides and the box row must be multiples of 16 bytes");
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)s1, (cuuint64_t)s2};
+  cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = dtype == DUO_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled (3D) failed with code " + std::to_string((int)r));
+  return DUO_OK;
+}
+
 int make_tmap_plain(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
                     int box_cols) {
   PFN_encodeTiled enc = get_encode_fn();

@@ -134,6 +134,9 @@ int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st);
 // decode step (t = 1): conv + gates + l2norm + delta rule + gated norm in one kernel (needs hk == hv)
 int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cudaStream_t st);
 int launch_gdn_chunk(const GdnScanArgs& a, int dtype, cudaStream_t st);
+// the tcgen05 form (gdn_chunk_tc.cu) for 16-bit inputs without the l2norm option; launch_gdn_chunk routes to it
+bool gdn_chunk_tc_eligible(const GdnScanArgs& a, int dtype);
+int launch_gdn_chunk_tc(const GdnScanArgs& a, int dtype, cudaStream_t st);
 
 // ---- gated attention
 struct AttnPrepArgs {

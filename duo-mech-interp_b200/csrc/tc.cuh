@@ -65,6 +65,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// 3D tiled TMA load (no multicast): box at (x, y, z) of a [dim2][dim1][dim0] tensor; rows past a dimension's extent
+// read as zero.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
 // 2D tiled TMA store of a shared-memory tile (rows and columns past the tensor's extent are not written); the
 // writing threads make their generic-proxy stores visible with fence_proxy_async() before the barrier that precedes
 // it.  bulk_commit() closes the group; bulk_wait_all() returns once its writes are done.
@@ -114,6 +123,29 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor of a 128-byte-swizzled operand, either major-ness (PTX ISA tcgen05 matrix
+// descriptor; the canonical layouts are those of a SWIZZLE_128B TMA load or of the same pattern written by threads:
+// rows of 128 bytes whose 16-byte chunks are XOR-permuted by (row % 8), 1024-byte aligned atoms of 8 rows).
+//   K-major  (K contiguous): rows run along M / N; sbo = bytes between 8-row groups (1024 for stacked rows); lbo unused.
+//   MN-major (M / N contiguous): each 128-byte row holds 64 consecutive M / N elements of one k; rows run along K;
+//            sbo = bytes between 8-row (8-k) groups, lbo = bytes between the 64-element M / N blocks.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with A and B both f16 and an f32 accumulator; a_mn / b_mn select the MN-major
+// form of each operand (bits 15 / 16).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
 // Instruction descriptor for kind::f16 with A and B both bf16 (f16 = false) or both f16 (both K-major) and an f32
 // accumulator.
 __host__ __device__ constexpr uint32_t idesc_16_f32(int m, int n, bool f16) {
@@ -154,6 +186,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
 }
 
+// 32 lanes x 32 columns of 32-bit values from registers into TMEM: lane_base + l, columns col .. col + 31; returns
+// once the stores are done.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // tcgen05.ld of 32 lanes x 32 columns without the wait: the registers are valid only after tmem_ld_wait(r).
 __device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -179,6 +231,11 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
 // elements) with a (box_cols x box_rows) box and 128-byte swizzle.  Out-of-range elements of a box read as zero.
 int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
                  int box_cols);
+// Host: a 3D 16-bit tensor map over [d2][d1][d0] elements (d0 contiguous; byte strides s1 between d1 rows and s2
+// between d2 planes, multiples of 16) with a (box0 x box1 x 1) box and 128-byte swizzle; boxes past an extent read as
+// zero (used for [rows][tokens][columns] activations, so a chunk that runs past a row's last token reads zeros).
+int make_tmap_3d_16(CUtensorMap* map, const void* base, int dtype, long d0, long d1, long d2, long s1, long s2,
+                    int box0, int box1);
 // Host: the same over a 16-bit or f32 (DUO_F32) matrix without swizzle (a dense row-major box), for TMA stores.
 int make_tmap_plain(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
                     int box_cols);
