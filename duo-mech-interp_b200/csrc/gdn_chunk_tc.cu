@@ -42,8 +42,8 @@ constexpr uint32_t OFF_S16 = OFF_W + 16384, OFF_SCR = OFF_S16 + 32768;
 constexpr uint32_t OFF_VT = OFF_TB, OFF_VTE = OFF_W;
 constexpr int SCR_L = 0, SCR_T = 16640, SCR_LH = 33280, SCR_TH = 42496, SCR_XH = 51712, SCR_BYTES = 54016;
 constexpr int LP = 65, HP = 72;  // pitches of the f32 and f16 64 x 64 solve tiles
-constexpr uint32_t OFF_SMALL = OFF_SCR + SCR_BYTES;  // G, e^G, e^{G_63 - G}, beta: 64 floats each
-constexpr uint32_t OFF_BAR = OFF_SMALL + 1024;
+constexpr uint32_t OFF_SMALL = OFF_SCR + SCR_BYTES;  // G, e^G, e^{G_63 - G}, beta, e^g: 64 floats each
+constexpr uint32_t OFF_BAR = OFF_SMALL + 1280;
 constexpr int GT_SMEM = OFF_BAR + 64 + 1024;  // + alignment slack
 static_assert(GT_SMEM <= 232448, "shared memory");
 // TMEM columns
@@ -55,6 +55,14 @@ constexpr float QSCALE = 0.08838834764831845f;  // 1 / sqrt(128)
 
 // byte offset of 16-byte chunk c (0..7) of row r of a K-major 128-byte-swizzled tile
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// SiLU as x sigmoid(x) = x (1 + tanh(x / 2)) / 2 on one hardware tanh (tanh.approx.f32, about 2^-11 relative):
+// the gate of an output that is rounded to 16 bits right after
+__device__ __forceinline__ float silu_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return 0.5f * x * (1.f + t);
+}
 
 __device__ __forceinline__ uint4 pack8h(const float* v) {
   uint4 u;
@@ -80,6 +88,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   float* eg = Gs + 64;
   float* egl = Gs + 128;
   float* bs = Gs + 192;
+  float* eg1 = Gs + 256;  // e^{g_t}: the decay of one token, e^{G_t - G_{t-1}}
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // [2]
   uint64_t* mbar = full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 1);
@@ -202,6 +211,8 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
         eg[2 * lane + 1] = expf(G1);
         egl[2 * lane] = expf(Gl - G0);
         egl[2 * lane + 1] = expf(Gl - G1);
+        eg1[2 * lane] = expf(g0);
+        eg1[2 * lane + 1] = expf(g1);
       }
       if constexpr (sizeof(TI) == 2 && !std::is_same<TI, __half>::value) {  // bf16 tiles -> f16 in place
         uint4* ring = reinterpret_cast<uint4*>(sm + s * STAGE);
@@ -247,29 +258,40 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       float x[64];
       tc::tmem_ld32(tmem + TQK + lane_off, x);
       tc::tmem_ld32(tmem + TQK + 32 + lane_off, x + 32);
+      // the decay e^{G_i - G_j} of row i, for j walking down from i: the product of the tokens' own decays e^{g_t},
+      // t = j + 1 .. i (a multiply per entry instead of an exponential; it only shrinks, so it underflows to 0
+      // gracefully however strong the decay)
+      const int i = tid & 63;
+      float d[64];
+      {
+        float run = 1.f;
+#pragma unroll
+        for (int j = 63; j >= 0; j--) {
+          if (j < i) run *= eg1[j + 1];
+          d[j] = j <= i ? run : 0.f;
+        }
+      }
       if (tid < 64) {  // Q row i: A = tril(q.k e^{G_i - G_j}) / sqrt(dk)
-        const int i = tid;
-        const float Gi = Gs[i];
 #pragma unroll
         for (int q = 0; q < 8; q++) {
           float v[8];
 #pragma unroll
-          for (int e = 0; e < 8; e++) {
-            const int j = 8 * q + e;
-            v[e] = j <= i ? x[j] * QSCALE * expf(Gi - Gs[j]) : 0.f;
-          }
+          for (int e = 0; e < 8; e++) v[e] = x[8 * q + e] * QSCALE * d[8 * q + e];
           *reinterpret_cast<uint4*>(sm + OFF_A + swz(i, q)) = pack8h(v);
         }
-      } else {  // K row i: L = strict_lower(beta_i k_i.k_j e^{G_i - G_j}); T's row cleared
-        const int i = tid - 64;
-        const float Gi = Gs[i], bi = bs[i];
+      } else {  // K row i: L = strict_lower(beta_i k_i.k_j e^{G_i - G_j}): its diagonal 16 x 16 block in f32 (the
+                // forward substitution) and the blocks left of it in f16 (the off-diagonal products)
+        const float bi = bs[i];
+        const int o = i & ~15;
 #pragma unroll
-        for (int j = 0; j < 64; j++) {
-          const float l = j < i ? bi * x[j] * expf(Gi - Gs[j]) : 0.f;
-          Lf[i * LP + j] = l;
-          lh[i * HP + j] = __float2half_rn(l);
-          Tf[i * LP + j] = 0.f;
-          th[i * HP + j] = __float2half_rn(0.f);
+        for (int j = 0; j < 64; j += 2) {
+          const float l0 = j < i ? bi * x[j] * d[j] : 0.f, l1 = j + 1 < i ? bi * x[j + 1] * d[j + 1] : 0.f;
+          if (j >= o && j < o + 16) {
+            Lf[i * LP + j] = l0;
+            Lf[i * LP + j + 1] = l1;
+          } else if (j < o) {
+            *reinterpret_cast<uint32_t*>(lh + i * HP + j) = wm::pack_f16(l0, l1);
+          }
         }
       }
     }
@@ -351,7 +373,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 8; e++) {
           const int j = 8 * q + e;
-          v1[e] = Tf[i * LP + j] * bs[j];
+          v1[e] = j <= i ? Tf[i * LP + j] * bs[j] : 0.f;  // T is unit lower triangular; its upper part is not stored
           v2[e] = v1[e] * eg[j];
         }
         *reinterpret_cast<uint4*>(sm + OFF_TB + swz(i, q)) = pack8h(v1);
@@ -501,10 +523,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
           const float rms = rsqrtf(ss / 128.f + a.eps);
           if (t < a.t) {
             const TI* zt = reinterpret_cast<const TI*>(&zr[i]);
-            o[0] *= rms * nw.x * silu16_(to_f(zt[0])) * hs;
-            o[1] *= rms * nw.y * silu16_(to_f(zt[1])) * hs;
-            o[2] *= rms * nw.z * silu16_(to_f(zt[2])) * hs;
-            o[3] *= rms * nw.w * silu16_(to_f(zt[3])) * hs;
+            o[0] *= rms * nw.x * silu_tanh(to_f(zt[0])) * hs;
+            o[1] *= rms * nw.y * silu_tanh(to_f(zt[1])) * hs;
+            o[2] *= rms * nw.z * silu_tanh(to_f(zt[2])) * hs;
+            o[3] *= rms * nw.w * silu_tanh(to_f(zt[3])) * hs;
           }
         }
         if (t < a.t) {
