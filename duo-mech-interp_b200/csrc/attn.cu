@@ -352,12 +352,22 @@ long attn_work_floats(int b, int nh, int max_len) {
   return (long)b * nh * std::min<long>(ns_max, 2L * sm_count()) * (AP_HD + 2);
 }
 
+// DUO_ATTN_TC=0 keeps 16-bit prefill on the mma.sync kernel (for comparisons); the default is the tcgen05 kernel
+static bool attn_tc_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("DUO_ATTN_TC");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <typename T>
 static int run_attention(const AttnArgs& a, cudaStream_t st) {
   if (!std::is_same<T, float>::value && a.t > 1) {
     const int rep = a.nh / a.nkv;
-    if (rep == 1 || rep == 2 || rep == 4)  // tensor cores
-      return launch_attn_prefill_mma(a, std::is_same<T, __half>::value ? DUO_F16 : DUO_BF16, st);
+    const int dt = std::is_same<T, __half>::value ? DUO_F16 : DUO_BF16;
+    if (attn_tc_enabled() && attn_prefill_tc_eligible(a, dt)) return launch_attn_prefill_tc(a, dt, st);  // tcgen05
+    if (rep == 1 || rep == 2 || rep == 4) return launch_attn_prefill_mma(a, dt, st);  // mma.sync
   }
   if (!std::is_same<T, float>::value && a.t == 1)  // HBM-streaming tensor-core decode
     return launch_attn_decode_mma(a, std::is_same<T, __half>::value ? DUO_F16 : DUO_BF16, st);

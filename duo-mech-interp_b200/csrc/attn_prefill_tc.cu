@@ -1,0 +1,359 @@
+// Gated GQA attention, prefill (t > 1) of the 16-bit engines on the Blackwell tensor cores (tcgen05 + TMEM + TMA).
+//
+// Flash attention over the KV cache (causal, head dim 256), then the sigmoid gate (transformers Qwen3_5Attention:
+// attention, then attn_output * sigmoid(gate); the reference's WGSL does the same per (token, head),
+// engine/kernels_qwen35.js:73-123).  One CTA = (row, kv head, tile of 128 / rep query positions); its 128 query rows
+// are the rep q heads of that kv head over the same positions, so every K / V tile is loaded once for all of them.
+//   warp 0     TMA: the Q tile once, then 64-key K and V tiles into a two-stage ring
+//   warp 1     tcgen05: S_j = Q K_j^T into one of two TMEM buffers (M = 128, N = 64, K = 256), then
+//              O += P_{j-1} V_{j-1} (M = 128, N = 256, K = 64; V straight from its tile as an MN-major operand)
+//   warps 2-5  one query row per thread: S_j from TMEM, causal mask, online softmax in base 2, P_j (16-bit) into
+//              shared memory for the next MMA.  O (f32, 256 TMEM columns) is rescaled in place only when a row's
+//              running maximum grows by more than 2^8 (until then P is computed against the older maximum, <= 2^8);
+//              at the end O / l times sigmoid(gate) is stored.
+// Scores of key tile j + 1 are computed while the softmax of tile j runs.  Barriers: q_full, kv_full / kv_empty per
+// stage, s_full / p_full / pv_done per parity of the tile index (a parity's next completion needs a P the waiting
+// thread has not written yet, so a phase can never be skipped).  Cache entries past a row's length are read (and
+// masked), so they must hold finite values (the engine's caches are zero-filled and then only written).
+#include "kernels.cuh"
+#include "tc.cuh"
+
+namespace duo {
+namespace {
+
+constexpr int AT_THREADS = 192, AT_BK = 64, AT_HD = 256;
+constexpr uint32_t AO_Q = 0, AO_RING = 65536, AO_STAGE = 65536, AO_V = 32768;
+constexpr uint32_t AO_P = AO_RING + 2 * AO_STAGE, AO_BAR = AO_P + 2 * 16384;
+constexpr int AT_SMEM = AO_BAR + 128 + 1024;
+static_assert(AT_SMEM <= 232448, "shared memory");
+constexpr uint32_t TA_S = 0, TA_O = 256, TA_COLS = 512;
+constexpr float RESCALE_AT = 8.f;  // log2 units
+
+__device__ __forceinline__ uint32_t swz128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+template <typename T16> __device__ __forceinline__ uint32_t pack2_16(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2_16<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack2_16<__half>(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float ex2(float x) {  // 2^x on the SFU (ex2.approx, 2 ulp; 2^-inf = 0)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T16, int REP>
+__global__ void __launch_bounds__(AT_THREADS, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                           const __grid_constant__ CUtensorMap tv, AttnArgs a, unsigned* fault) {
+  constexpr int QT = 128 / REP;  // query positions per CTA
+  constexpr bool BF = std::is_same<T16, __nv_bfloat16>::value;
+  constexpr uint32_t ID_S = tc::idesc_16_mn(128, AT_BK, BF, false, false);
+  constexpr uint32_t ID_PV = tc::idesc_16_mn(128, AT_HD, BF, false, true);
+  if (tc::fault_pending(fault)) {  // an earlier kernel gave up a wait
+    pdl_wait();
+    return;
+  }
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = tc::smem_u32(sm);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + AO_BAR);
+  uint64_t* q_full = bar;           // [1]
+  uint64_t* kv_full = bar + 1;      // [2]
+  uint64_t* kv_empty = bar + 3;     // [2]
+  uint64_t* s_full = bar + 5;       // [2]
+  uint64_t* p_full = bar + 7;       // [2]
+  uint64_t* pv_done = bar + 9;      // [2]
+  uint64_t* drain = bar + 11;       // [1] the issuer's last commit (every MMA of this CTA complete)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (latest) query tiles first
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int R = a.cache_row0 + b;
+
+  if (tid == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int i = 0; i < 2; i++) {
+      tc::mbar_init(&kv_full[i], 1);
+      tc::mbar_init(&kv_empty[i], 1);
+      tc::mbar_init(&s_full[i], 1);
+      tc::mbar_init(&p_full[i], 128);
+      tc::mbar_init(&pv_done[i], 1);
+    }
+    tc::mbar_init(drain, 1);
+    *abort = 0;
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tq);
+    tc::prefetch_tmap(&tk);
+    tc::prefetch_tmap(&tv);
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, TA_COLS);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
+
+  const int p0 = a.start ? a.start[R] : a.len[R] - a.t;
+  const int tq0 = qt * QT;
+  const int nq = min(QT, a.t - tq0);
+  const int n_keys = p0 + tq0 + nq;
+  const int ntiles = (n_keys + AT_BK - 1) / AT_BK;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      tc::mbar_arrive_expect_tx(q_full, 128 * AT_HD * 2);
+      for (int hl = 0; hl < REP; hl++)
+        for (int qq = 0; qq < 4; qq++)
+          tc::tma_load_4d(sm + AO_Q + qq * 16384 + hl * QT * 128, &tq, qq * 64, kvh * REP + hl, tq0, b, q_full);
+      int issued = 0;
+      for (int j = 0; j < ntiles && !*abort; j++) {
+        const int s = j & 1;
+        if (j >= 2 && !tc::mbar_wait(&kv_empty[s], (uint32_t)(((j - 2) >> 1) & 1))) {
+          atomicOr(fault, 128u);
+          *abort = 1;
+          break;
+        }
+        issued = j + 1;
+        uint8_t* st = sm + AO_RING + s * AO_STAGE;
+        tc::mbar_arrive_expect_tx(&kv_full[s], 2 * AT_BK * AT_HD * 2);
+        for (int qq = 0; qq < 4; qq++) {
+          tc::tma_load_4d(st + qq * 8192, &tk, qq * 64, kvh, j * AT_BK, b, &kv_full[s]);
+          tc::tma_load_4d(st + AO_V + qq * 8192, &tv, qq * 64, kvh, j * AT_BK, b, &kv_full[s]);
+        }
+      }
+      // no copy may still be landing when the CTA exits: wait (bounded) for the Q tile and the last two stages
+      tc::mbar_wait(q_full, 0);
+      for (int j = issued > 2 ? issued - 2 : 0; j < issued; j++) tc::mbar_wait(&kv_full[j & 1], (uint32_t)((j >> 1) & 1));
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      bool ok = tc::mbar_wait(q_full, 0);
+      auto pv = [&](int jp) -> bool {
+        const int sp = jp & 1;
+        if (!tc::mbar_wait(&p_full[sp], (uint32_t)((jp >> 1) & 1))) return false;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++)
+          tc::mma_bf16(tmem + TA_O, tc::desc_sw128(sb + AO_P + sp * 16384 + ks * 32, 16, 1024),
+                       tc::desc_sw128(sb + AO_RING + sp * AO_STAGE + AO_V + ks * 2048, 8192, 1024), ID_PV,
+                       (jp > 0 || ks > 0) ? 1u : 0u);
+        tc::mma_commit(&pv_done[sp]);
+        tc::mma_commit(&kv_empty[sp]);
+        return true;
+      };
+      for (int j = 0; ok && j < ntiles && !*abort; j++) {
+        const int s = j & 1;
+        if (!tc::mbar_wait(&kv_full[s], (uint32_t)((j >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int ks = 0; ks < 16; ks++)
+          tc::mma_bf16(tmem + TA_S + s * AT_BK,
+                       tc::desc_sw128(sb + AO_Q + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
+                       tc::desc_sw128(sb + AO_RING + s * AO_STAGE + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024),
+                       ID_S, ks > 0 ? 1u : 0u);
+        tc::mma_commit(&s_full[s]);
+        if (j >= 1 && !pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && !*abort && ntiles > 0) ok = pv(ntiles - 1);
+      if (!ok) {
+        atomicOr(fault, 128u);
+        *abort = 1;
+      }
+      tc::mma_commit(drain);  // arrives once every MMA issued above has completed
+      tc::mbar_wait(drain, 0);
+    }
+  } else {  // ---- softmax and epilogue: one query row per thread
+    const int qw = warp & 3, r = qw * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const int hl = r / QT, qi = r % QT;
+    const int pos = p0 + tq0 + qi;
+    const float sl2 = a.scale * 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; j++) {
+      const int s = j & 1;
+      if (!tc::mbar_wait(&s_full[s], (uint32_t)((j >> 1) & 1)) || *abort) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      uint32_t raw[2][32];
+      tc::tmem_ld32_issue(tmem + TA_S + s * AT_BK + lane_off, raw[0]);
+      tc::tmem_ld32_issue(tmem + TA_S + s * AT_BK + 32 + lane_off, raw[1]);
+      tc::tmem_ld_wait(raw[0]);
+      tc::tmem_ld_wait(raw[1]);
+      float x[64];
+      float mt = -INFINITY;
+      const int k0 = j * AT_BK;
+#pragma unroll
+      for (int c = 0; c < 64; c++) {
+        const int key = k0 + c;
+        x[c] = (key <= pos && key < n_keys) ? __uint_as_float(raw[c >> 5][c & 31]) * sl2 : -INFINITY;
+        mt = fmaxf(mt, x[c]);
+      }
+      // P buffer s was read by PV_{j-2}
+      if (j >= 2 && !tc::mbar_wait(&pv_done[s], (uint32_t)(((j - 2) >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      if (m == -INFINITY || mt > m + RESCALE_AT) {
+        const float mn = fmaxf(m, mt);
+        if (j > 0 && m != -INFINITY) {  // O holds P_{<j} V against the old maximum: rescale it once PV_{j-1} is in
+          const float al = ex2(m - mn);
+          if (!tc::mbar_wait(&pv_done[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1))) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+#pragma unroll 1
+          for (int c0 = 0; c0 < AT_HD; c0 += 32) {
+            float v[32];
+            tc::tmem_ld32(tmem + TA_O + c0 + lane_off, v);
+#pragma unroll
+            for (int e = 0; e < 32; e++) v[e] *= al;
+            tc::tmem_st32(tmem + TA_O + c0 + lane_off, v);
+          }
+          l *= al;
+        }
+        m = mn;
+      }
+      float ls = 0.f;
+#pragma unroll
+      for (int q8 = 0; q8 < 8; q8++) {
+        float p[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float v = x[8 * q8 + e];
+          p[e] = ex2(v - m);
+          ls += p[e];
+        }
+        uint4 u;
+        u.x = pack2_16<T16>(p[0], p[1]);
+        u.y = pack2_16<T16>(p[2], p[3]);
+        u.z = pack2_16<T16>(p[4], p[5]);
+        u.w = pack2_16<T16>(p[6], p[7]);
+        *reinterpret_cast<uint4*>(sm + AO_P + s * 16384 + swz128(r, q8)) = u;
+      }
+      l += ls;
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      tc::mbar_arrive(&p_full[s]);
+    }
+    // epilogue: O / l * sigmoid(gate)
+    if (ok && ntiles > 0) ok = tc::mbar_wait(&pv_done[(ntiles - 1) & 1], (uint32_t)(((ntiles - 1) >> 1) & 1));
+    if (!ok) {
+      atomicOr(fault, 128u);
+      *abort = 1;
+    } else {
+      tc::fence_after_sync();
+      const bool valid = qi < nq;
+      const int head = kvh * REP + hl;
+      const long tok = (long)b * a.t + tq0 + qi;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const T16* gp = a.gate ? static_cast<const T16*>(a.gate) + tok * a.gate_stride + (long)head * a.gate_hstride
+                             : nullptr;
+      T16* op = static_cast<T16*>(a.o) + (tok * a.nh + head) * AT_HD;
+#pragma unroll 1
+      for (int c0 = 0; c0 < AT_HD; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(tmem + TA_O + c0 + lane_off, v);
+        if (valid) {
+#pragma unroll
+          for (int c8 = 0; c8 < 32; c8 += 8) {
+            float g[8];
+            if (gp) load8(gp + c0 + c8, g);
+            uint4 u;
+            uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              float o0 = v[c8 + 2 * e] * inv, o1 = v[c8 + 2 * e + 1] * inv;
+              if (gp) {
+                o0 /= 1.f + __expf(-g[2 * e]);
+                o1 /= 1.f + __expf(-g[2 * e + 1]);
+              }
+              w[e] = pack2_16<T16>(o0, o1);
+            }
+            *reinterpret_cast<uint4*>(op + c0 + c8) = u;
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {  // the issuer waited on `drain` above: no MMA reads or writes this CTA's TMEM any more
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, TA_COLS);
+  }
+}
+
+template <typename T16, int REP>
+int run_attn_tc(const AttnArgs& a, int dtype, cudaStream_t st) {
+  constexpr int QT = 128 / REP;
+  const long hd = AT_HD, es = 2;
+  CUtensorMap tq, tk, tv;
+  {
+    const long dims[4] = {hd, a.nh, a.t, a.b};
+    const long strides[3] = {hd * es, a.nh * hd * es, (long)a.t * a.nh * hd * es};
+    const int box[4] = {64, 1, QT, 1};
+    DUO_TRY(make_tmap_nd_16(&tq, a.q, dtype, 4, dims, strides, box));
+  }
+  {
+    const long dims[4] = {hd, a.nkv, a.max_len, a.b};
+    const long strides[3] = {hd * es, a.nkv * hd * es, (long)a.max_len * a.nkv * hd * es};
+    const int box[4] = {64, 1, AT_BK, 1};
+    const long row0 = (long)a.cache_row0 * a.max_len * a.nkv * hd;
+    DUO_TRY(make_tmap_nd_16(&tk, static_cast<const T16*>(a.kc) + row0, dtype, 4, dims, strides, box));
+    DUO_TRY(make_tmap_nd_16(&tv, static_cast<const T16*>(a.vc) + row0, dtype, 4, dims, strides, box));
+  }
+  unsigned* fault = tc_fault_ptr();
+  if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
+  DUO_TRY(ensure_smem_attr(attn_prefill_tc_kernel<T16, REP>, AT_SMEM));
+  DUO_CUDA_TRY(::duo::launch_kernel(attn_prefill_tc_kernel<T16, REP>, dim3(cdiv(a.t, QT), a.nkv, a.b), AT_THREADS,
+                                    AT_SMEM, st, tq, tk, tv, a, fault));
+  DUO_LAUNCH_CHECK("attn_prefill_tc_kernel");
+  return DUO_OK;
+}
+
+}  // namespace
+
+bool attn_prefill_tc_eligible(const AttnArgs& a, int dtype) {
+  if (dtype != DUO_BF16 && dtype != DUO_F16) return false;
+  if (a.hd != AT_HD || a.t < 2 || a.nkv <= 0 || a.nh % a.nkv) return false;
+  const int rep = a.nh / a.nkv;
+  if (rep != 1 && rep != 2 && rep != 4) return false;
+  const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al(a.q) || !al(a.kc) || !al(a.vc) || !al(a.o) || (a.gate && !al(a.gate))) return false;
+  if (a.gate && (a.gate_stride % 8 || a.gate_hstride % 8)) return false;
+  return true;
+}
+
+int launch_attn_prefill_tc(const AttnArgs& a, int dtype, cudaStream_t st) {
+  if (a.b == 0 || a.t == 0) return DUO_OK;
+  const int rep = a.nh / a.nkv;
+  if (dtype == DUO_F16) {
+    if (rep == 4) return run_attn_tc<__half, 4>(a, dtype, st);
+    if (rep == 2) return run_attn_tc<__half, 2>(a, dtype, st);
+    return run_attn_tc<__half, 1>(a, dtype, st);
+  }
+  if (rep == 4) return run_attn_tc<__nv_bfloat16, 4>(a, dtype, st);
+  if (rep == 2) return run_attn_tc<__nv_bfloat16, 2>(a, dtype, st);
+  return run_attn_tc<__nv_bfloat16, 1>(a, dtype, st);
+}
+
+}  // namespace duo

@@ -328,6 +328,31 @@ int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long 
   return DUO_OK;
 }
 
+int make_tmap_nd_16(CUtensorMap* map, const void* base, int dtype, int rank, const long* dims, const long* strides,
+                    const int* box) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (rank < 2 || rank > 5) return fail(DUO_EINVAL, "tensor map: rank must be 2..5");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (box[0] * 2) % 16 || box[0] * 2 > 128)
+    return fail(DUO_EINVAL, "tensor map: base 16-byte aligned, box row a multiple of 16 bytes and at most 128");
+  cuuint64_t d[5], s[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; i++) {
+    d[i] = (cuuint64_t)dims[i];
+    bx[i] = (cuuint32_t)box[i];
+    es[i] = 1;
+    if (i + 1 < rank) {
+      if (strides[i] % 16) return fail(DUO_EINVAL, "tensor map: strides must be multiples of 16 bytes");
+      s[i] = (cuuint64_t)strides[i];
+    }
+  }
+  const CUtensorMapDataType dt = dtype == DUO_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = enc(map, dt, (cuuint32_t)rank, const_cast<void*>(base), d, s, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled (N-d) failed with code " + std::to_string((int)r));
+  return DUO_OK;
+}
+
 int make_tmap_3d_16(CUtensorMap* map, const void* base, int dtype, long d0, long d1, long d2, long s1, long s2,
                     int box0, int box1) {
   PFN_encodeTiled enc = get_encode_fn();

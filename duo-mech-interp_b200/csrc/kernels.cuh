@@ -176,6 +176,9 @@ int launch_attn_decode_mma(const AttnArgs& a, int dtype, cudaStream_t st);
 int attn_decode_mma_plan(int b, int nkv, int max_len, int* split_len);
 int launch_attn_combine(const AttnArgs& a, int dtype, int nsplit, cudaStream_t st);
 int launch_attn_prefill_mma(const AttnArgs& a, int dtype, cudaStream_t st);  // bf16 / f16, t > 1, hd 256
+// bf16 / f16, t > 1, hd 256, nh / nkv in {1, 2, 4}, 16-byte aligned operands: tcgen05 + TMA flash attention
+bool attn_prefill_tc_eligible(const AttnArgs& a, int dtype);
+int launch_attn_prefill_tc(const AttnArgs& a, int dtype, cudaStream_t st);
 
 // int8 -> 16-bit (bf16 or f16) copy of a weight matrix for the tensor-core GEMM: dst row of src row n is n, or
 // (interleave > 0) the gate/up interleaved order [gate 64 | up 64]* with `interleave` = rows of each half.

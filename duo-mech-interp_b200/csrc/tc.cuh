@@ -74,6 +74,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
+// 4D tiled TMA load (no multicast): box at (x, y, z, w); coordinates past an extent read as zero.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
 // 2D tiled TMA store of a shared-memory tile (rows and columns past the tensor's extent are not written); the
 // writing threads make their generic-proxy stores visible with fence_proxy_async() before the barrier that precedes
 // it.  bulk_commit() closes the group; bulk_wait_all() returns once its writes are done.
@@ -139,11 +148,14 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr, uint32_t lbo_
   return d;
 }
 
-// Instruction descriptor for kind::f16 with A and B both f16 and an f32 accumulator; a_mn / b_mn select the MN-major
-// form of each operand (bits 15 / 16).
+// Instruction descriptor for kind::f16 with A and B both f16 (bf16 = false) or both bf16 and an f32 accumulator;
+// a_mn / b_mn select the MN-major form of each operand (bits 15 / 16).
+__host__ __device__ constexpr uint32_t idesc_16_mn(int m, int n, bool bf16, bool a_mn, bool b_mn) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool a_mn, bool b_mn) {
-  return (1u << 4) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
-         ((uint32_t)(m >> 4) << 24);
+  return idesc_16_mn(m, n, false, a_mn, b_mn);
 }
 
 // Instruction descriptor for kind::f16 with A and B both bf16 (f16 = false) or both f16 (both K-major) and an f32
@@ -236,6 +248,10 @@ int make_tmap_16(CUtensorMap* map, const void* base, int dtype, long rows, long 
 // zero (used for [rows][tokens][columns] activations, so a chunk that runs past a row's last token reads zeros).
 int make_tmap_3d_16(CUtensorMap* map, const void* base, int dtype, long d0, long d1, long d2, long s1, long s2,
                     int box0, int box1);
+// Host: an N-d (2..5) 16-bit tensor map with 128-byte swizzle: dims[0] contiguous, byte strides[i] of dims[i + 1]
+// (multiples of 16), box[i] elements per dim (box[0] * 2 bytes = 128 at most); boxes past an extent read as zero.
+int make_tmap_nd_16(CUtensorMap* map, const void* base, int dtype, int rank, const long* dims, const long* strides,
+                    const int* box);
 // Host: the same over a 16-bit or f32 (DUO_F32) matrix without swizzle (a dense row-major box), for TMA stores.
 int make_tmap_plain(CUtensorMap* map, const void* base, int dtype, long rows, long cols, long ld, int box_rows,
                     int box_cols);
