@@ -4,32 +4,36 @@
 // attention, then attn_output * sigmoid(gate); the reference's WGSL does the same per (token, head),
 // engine/kernels_qwen35.js:73-123).  One CTA = (row, kv head, tile of 128 / rep query positions); its 128 query rows
 // are the rep q heads of that kv head over the same positions, so every K / V tile is loaded once for all of them.
-//   warp 0     TMA: the Q tile once, then 64-key K and V tiles into a two-stage ring
+//   warp 0     TMA: the Q tile once, then 64-key K and V tiles into two two-stage rings; K_{j+1} is requested
+//              before V_j, so the scores of the next tile never wait behind the previous tile's P V product
 //   warp 1     tcgen05: S_j = Q K_j^T into one of two TMEM buffers (M = 128, N = 64, K = 256), then
-//              O += P_{j-1} V_{j-1} (M = 128, N = 256, K = 64; V straight from its tile as an MN-major operand)
-//   warps 2-5  one query row per thread: S_j from TMEM, causal mask, online softmax in base 2, P_j (16-bit) into
-//              shared memory for the next MMA.  O (f32, 256 TMEM columns) is rescaled in place only when a row's
-//              running maximum grows by more than 2^8 (until then P is computed against the older maximum, <= 2^8);
-//              at the end O / l times sigmoid(gate) is stored.
-// Scores of key tile j + 1 are computed while the softmax of tile j runs.  Barriers: q_full, kv_full / kv_empty per
-// stage, s_full / p_full / pv_done per parity of the tile index (a parity's next completion needs a P the waiting
-// thread has not written yet, so a phase can never be skipped).  Cache entries past a row's length are read (and
-// masked), so they must hold finite values (the engine's caches are zero-filled and then only written).
+//              O += P_{j-1} V_{j-1} (M = 128, N = 256, K = 64) with P read from TMEM and V straight from its tile
+//              as an MN-major operand
+//   warps 2-9  two threads per query row (warps w and w + 4 share TMEM lanes 32 (w % 4) ..; each takes 32 of a
+//              tile's 64 keys and 128 of O's 256 columns): S from TMEM, the causal mask on the tiles that cross the
+//              diagonal only, online softmax in base 2 (the pair swaps tile maxima through shared memory), P as
+//              16-bit pairs into TMEM for the next MMA.  O (f32, 256 TMEM columns) is rescaled in place only when a
+//              row's running maximum grows by more than 2^8 (until then P is formed against the older maximum, so
+//              P <= 2^8); at the end O / l times sigmoid(gate) is stored.
+// Scores of tile j + 1 are computed while the softmax of tile j runs.  Barriers: q_full; k_full / k_empty and
+// v_full / v_empty per stage; s_full / p_full / pv_done per parity of the tile index (a parity's next completion needs
+// a P the waiting thread has not written yet, so no phase is skipped).  Cache entries past a row's length are read and
+// masked; V there must be finite (0 x inf would poison O), which the engine's zero-filled caches are.
 #include "kernels.cuh"
 #include "tc.cuh"
 
 namespace duo {
 namespace {
 
-constexpr int AT_THREADS = 192, AT_BK = 64, AT_HD = 256;
-constexpr uint32_t AO_Q = 0, AO_RING = 65536, AO_STAGE = 65536, AO_V = 32768;
-constexpr uint32_t AO_P = AO_RING + 2 * AO_STAGE, AO_BAR = AO_P + 2 * 16384;
-constexpr int AT_SMEM = AO_BAR + 128 + 1024;
+constexpr int AT_THREADS = 320, AT_BK = 64, AT_HD = 256;
+constexpr uint32_t AO_Q = 0, AO_K = 65536, AO_V = AO_K + 2 * 32768, AO_BAR = AO_V + 2 * 32768;
+// exchange between the two threads of a row: tile maxima and failure flags [parity][half][row], final sums [half][row]
+constexpr uint32_t AO_RED = AO_BAR + 256, AO_REDF = AO_RED + 2048, AO_REDL = AO_REDF + 2048;
+constexpr int AT_SMEM = AO_REDL + 1024 + 1024;
 static_assert(AT_SMEM <= 232448, "shared memory");
-constexpr uint32_t TA_S = 0, TA_O = 256, TA_COLS = 512;
+// TMEM columns: S_0, S_1 (64 f32 each), P_0, P_1 (64 16-bit keys in 32 columns each), O (256 f32)
+constexpr uint32_t TA_S = 0, TA_P = 128, TA_O = 256, TA_COLS = 512;
 constexpr float RESCALE_AT = 8.f;  // log2 units
-
-__device__ __forceinline__ uint32_t swz128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 template <typename T16> __device__ __forceinline__ uint32_t pack2_16(float a, float b);
 template <> __device__ __forceinline__ uint32_t pack2_16<__nv_bfloat16>(float a, float b) {
@@ -63,15 +67,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = tc::smem_u32(sm);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + AO_BAR);
-  uint64_t* q_full = bar;           // [1]
-  uint64_t* kv_full = bar + 1;      // [2]
-  uint64_t* kv_empty = bar + 3;     // [2]
-  uint64_t* s_full = bar + 5;       // [2]
-  uint64_t* p_full = bar + 7;       // [2]
-  uint64_t* pv_done = bar + 9;      // [2]
-  uint64_t* drain = bar + 11;       // [1] the issuer's last commit (every MMA of this CTA complete)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+  uint64_t* q_full = bar;        // [1]
+  uint64_t* k_full = bar + 1;    // [2]
+  uint64_t* k_empty = bar + 3;   // [2]
+  uint64_t* v_full = bar + 5;    // [2]
+  uint64_t* v_empty = bar + 7;   // [2]
+  uint64_t* s_full = bar + 9;    // [2]
+  uint64_t* p_full = bar + 11;   // [2]
+  uint64_t* pv_done = bar + 13;  // [2]
+  uint64_t* drain = bar + 15;    // [1] the issuer's last commit: every MMA of this CTA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(sm + AO_RED);
+  int* redf = reinterpret_cast<int*>(sm + AO_REDF);
+  float* redl = reinterpret_cast<float*>(sm + AO_REDL);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (latest) query tiles first
@@ -81,10 +90,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   if (tid == 0) {
     tc::mbar_init(q_full, 1);
     for (int i = 0; i < 2; i++) {
-      tc::mbar_init(&kv_full[i], 1);
-      tc::mbar_init(&kv_empty[i], 1);
+      tc::mbar_init(&k_full[i], 1);
+      tc::mbar_init(&k_empty[i], 1);
+      tc::mbar_init(&v_full[i], 1);
+      tc::mbar_init(&v_empty[i], 1);
       tc::mbar_init(&s_full[i], 1);
-      tc::mbar_init(&p_full[i], 128);
+      tc::mbar_init(&p_full[i], 256);
       tc::mbar_init(&pv_done[i], 1);
     }
     tc::mbar_init(drain, 1);
@@ -109,50 +120,67 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const int ntiles = (n_keys + AT_BK - 1) / AT_BK;
 
   if (warp == 0) {
-    if (lane == 0) {  // ---- TMA producer
+    if (lane == 0) {  // ---- TMA producer: Q, K_0, then K_{j+1} and V_j for j = 0, 1, ...
+      auto load_k = [&](int j) -> bool {
+        const int s = j & 1;
+        if (j >= 2 && !tc::mbar_wait(&k_empty[s], (uint32_t)(((j - 2) >> 1) & 1))) return false;
+        tc::mbar_arrive_expect_tx(&k_full[s], AT_BK * AT_HD * 2);
+        for (int qq = 0; qq < 4; qq++)
+          tc::tma_load_4d(sm + AO_K + s * 32768 + qq * 8192, &tk, qq * 64, kvh, j * AT_BK, b, &k_full[s]);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j & 1;
+        if (j >= 2 && !tc::mbar_wait(&v_empty[s], (uint32_t)(((j - 2) >> 1) & 1))) return false;
+        tc::mbar_arrive_expect_tx(&v_full[s], AT_BK * AT_HD * 2);
+        for (int qq = 0; qq < 4; qq++)
+          tc::tma_load_4d(sm + AO_V + s * 32768 + qq * 8192, &tv, qq * 64, kvh, j * AT_BK, b, &v_full[s]);
+        return true;
+      };
       tc::mbar_arrive_expect_tx(q_full, 128 * AT_HD * 2);
       for (int hl = 0; hl < REP; hl++)
         for (int qq = 0; qq < 4; qq++)
           tc::tma_load_4d(sm + AO_Q + qq * 16384 + hl * QT * 128, &tq, qq * 64, kvh * REP + hl, tq0, b, q_full);
-      int issued = 0;
-      for (int j = 0; j < ntiles && !*abort; j++) {
-        const int s = j & 1;
-        if (j >= 2 && !tc::mbar_wait(&kv_empty[s], (uint32_t)(((j - 2) >> 1) & 1))) {
-          atomicOr(fault, 128u);
-          *abort = 1;
-          break;
+      int nk = 0, nv = 0;  // tiles requested
+      bool ok = load_k(0);
+      nk = ok ? 1 : 0;
+      for (int j = 0; ok && j < ntiles && !*abort; j++) {
+        if (j + 1 < ntiles) {
+          if (!(ok = load_k(j + 1))) break;
+          nk = j + 2;
         }
-        issued = j + 1;
-        uint8_t* st = sm + AO_RING + s * AO_STAGE;
-        tc::mbar_arrive_expect_tx(&kv_full[s], 2 * AT_BK * AT_HD * 2);
-        for (int qq = 0; qq < 4; qq++) {
-          tc::tma_load_4d(st + qq * 8192, &tk, qq * 64, kvh, j * AT_BK, b, &kv_full[s]);
-          tc::tma_load_4d(st + AO_V + qq * 8192, &tv, qq * 64, kvh, j * AT_BK, b, &kv_full[s]);
-        }
+        if (!(ok = load_v(j))) break;
+        nv = j + 1;
       }
-      // no copy may still be landing when the CTA exits: wait (bounded) for the Q tile and the last two stages
+      if (!ok) {
+        atomicOr(fault, 128u);
+        *abort = 1;
+      }
+      // no copy may still be landing when the CTA exits: wait (bounded) for Q and the last two stages of each ring
       tc::mbar_wait(q_full, 0);
-      for (int j = issued > 2 ? issued - 2 : 0; j < issued; j++) tc::mbar_wait(&kv_full[j & 1], (uint32_t)((j >> 1) & 1));
+      for (int j = nk > 2 ? nk - 2 : 0; j < nk; j++) tc::mbar_wait(&k_full[j & 1], (uint32_t)((j >> 1) & 1));
+      for (int j = nv > 2 ? nv - 2 : 0; j < nv; j++) tc::mbar_wait(&v_full[j & 1], (uint32_t)((j >> 1) & 1));
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer
       bool ok = tc::mbar_wait(q_full, 0);
       auto pv = [&](int jp) -> bool {
         const int sp = jp & 1;
+        if (!tc::mbar_wait(&v_full[sp], (uint32_t)((jp >> 1) & 1))) return false;
         if (!tc::mbar_wait(&p_full[sp], (uint32_t)((jp >> 1) & 1))) return false;
         tc::fence_after_sync();
 #pragma unroll
         for (int ks = 0; ks < 4; ks++)
-          tc::mma_bf16(tmem + TA_O, tc::desc_sw128(sb + AO_P + sp * 16384 + ks * 32, 16, 1024),
-                       tc::desc_sw128(sb + AO_RING + sp * AO_STAGE + AO_V + ks * 2048, 8192, 1024), ID_PV,
-                       (jp > 0 || ks > 0) ? 1u : 0u);
+          tc::mma_ts(tmem + TA_O, tmem + TA_P + sp * 32 + ks * 8,
+                     tc::desc_sw128(sb + AO_V + sp * 32768 + ks * 2048, 8192, 1024), ID_PV,
+                     (jp > 0 || ks > 0) ? 1u : 0u);
         tc::mma_commit(&pv_done[sp]);
-        tc::mma_commit(&kv_empty[sp]);
+        tc::mma_commit(&v_empty[sp]);
         return true;
       };
       for (int j = 0; ok && j < ntiles && !*abort; j++) {
         const int s = j & 1;
-        if (!tc::mbar_wait(&kv_full[s], (uint32_t)((j >> 1) & 1))) {
+        if (!tc::mbar_wait(&k_full[s], (uint32_t)((j >> 1) & 1))) {
           ok = false;
           break;
         }
@@ -161,9 +189,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         for (int ks = 0; ks < 16; ks++)
           tc::mma_bf16(tmem + TA_S + s * AT_BK,
                        tc::desc_sw128(sb + AO_Q + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
-                       tc::desc_sw128(sb + AO_RING + s * AO_STAGE + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024),
-                       ID_S, ks > 0 ? 1u : 0u);
+                       tc::desc_sw128(sb + AO_K + s * 32768 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), ID_S,
+                       ks > 0 ? 1u : 0u);
         tc::mma_commit(&s_full[s]);
+        tc::mma_commit(&k_empty[s]);
         if (j >= 1 && !pv(j - 1)) {
           ok = false;
           break;
@@ -177,84 +206,92 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       tc::mma_commit(drain);  // arrives once every MMA issued above has completed
       tc::mbar_wait(drain, 0);
     }
-  } else {  // ---- softmax and epilogue: one query row per thread
-    const int qw = warp & 3, r = qw * 32 + lane;
+  } else {  // ---- softmax and epilogue: two threads per query row
+    const int qw = warp & 3, half = (warp - 2) >> 2, r = qw * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     const int hl = r / QT, qi = r % QT;
     const int pos = p0 + tq0 + qi;
+    const int diag = p0 + tq0;  // tiles whose last key is past this (or past n_keys) need the mask
     const float sl2 = a.scale * 1.4426950408889634f;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
+    float m = -INFINITY, l = 0.f;  // m: running maximum of the scaled scores (log2 units)
+    // The two threads of a row meet at one named barrier per tile and one in the epilogue, always the same number of
+    // times: a failed wait only marks `bad`, and both leave the loop together right after the barrier that shows it.
+    bool bad = false;
     for (int j = 0; j < ntiles; j++) {
       const int s = j & 1;
-      if (!tc::mbar_wait(&s_full[s], (uint32_t)((j >> 1) & 1)) || *abort) {
-        ok = false;
+      if (!bad && (!tc::mbar_wait(&s_full[s], (uint32_t)((j >> 1) & 1)) || *abort)) bad = true;
+      float x[32];
+      float mt = -INFINITY;
+      if (!bad) {
+        tc::fence_after_sync();
+        uint32_t raw[32];
+        tc::tmem_ld32_issue(tmem + TA_S + s * AT_BK + half * 32 + lane_off, raw);
+        tc::tmem_ld_wait(raw);
+#pragma unroll
+        for (int c = 0; c < 32; c++) x[c] = __uint_as_float(raw[c]);
+        const int k0 = j * AT_BK + half * 32;
+        if (j * AT_BK + AT_BK - 1 > diag || j * AT_BK + AT_BK > n_keys) {
+#pragma unroll
+          for (int c = 0; c < 32; c++)
+            if (k0 + c > pos || k0 + c >= n_keys) x[c] = -INFINITY;
+        }
+        float mx[4] = {x[0], x[1], x[2], x[3]};
+#pragma unroll
+        for (int c = 4; c < 32; c++) mx[c & 3] = fmaxf(mx[c & 3], x[c]);
+        mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      }
+      red[(s * 2 + half) * 128 + r] = mt;
+      redf[(s * 2 + half) * 128 + r] = bad ? 1 : 0;
+      tc::bar_sync(1 + qw, 64);
+      if (bad || redf[(s * 2 + (half ^ 1)) * 128 + r]) {
+        bad = true;
         break;
       }
-      tc::fence_after_sync();
-      uint32_t raw[2][32];
-      tc::tmem_ld32_issue(tmem + TA_S + s * AT_BK + lane_off, raw[0]);
-      tc::tmem_ld32_issue(tmem + TA_S + s * AT_BK + 32 + lane_off, raw[1]);
-      tc::tmem_ld_wait(raw[0]);
-      tc::tmem_ld_wait(raw[1]);
-      float x[64];
-      float mt = -INFINITY;
-      const int k0 = j * AT_BK;
-#pragma unroll
-      for (int c = 0; c < 64; c++) {
-        const int key = k0 + c;
-        x[c] = (key <= pos && key < n_keys) ? __uint_as_float(raw[c >> 5][c & 31]) * sl2 : -INFINITY;
-        mt = fmaxf(mt, x[c]);
-      }
+      mt = fmaxf(mt, red[(s * 2 + (half ^ 1)) * 128 + r]) * sl2;
       // P buffer s was read by PV_{j-2}
       if (j >= 2 && !tc::mbar_wait(&pv_done[s], (uint32_t)(((j - 2) >> 1) & 1))) {
-        ok = false;
-        break;
+        bad = true;
+        continue;
       }
-      if (m == -INFINITY || mt > m + RESCALE_AT) {
-        const float mn = fmaxf(m, mt);
-        if (j > 0 && m != -INFINITY) {  // O holds P_{<j} V against the old maximum: rescale it once PV_{j-1} is in
-          const float al = ex2(m - mn);
+      if (mt > m + RESCALE_AT) {  // both threads of the row take this branch together (same m, same mt)
+        if (j > 0) {  // O holds P_{<j} V against the old maximum: rescale this half once PV_{j-1} is in
+          const float al = ex2(m - mt);
           if (!tc::mbar_wait(&pv_done[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1))) {
-            ok = false;
-            break;
+            bad = true;
+            continue;
           }
           tc::fence_after_sync();
 #pragma unroll 1
-          for (int c0 = 0; c0 < AT_HD; c0 += 32) {
+          for (int c0 = 0; c0 < 128; c0 += 32) {
             float v[32];
-            tc::tmem_ld32(tmem + TA_O + c0 + lane_off, v);
+            tc::tmem_ld32(tmem + TA_O + half * 128 + c0 + lane_off, v);
 #pragma unroll
             for (int e = 0; e < 32; e++) v[e] *= al;
-            tc::tmem_st32(tmem + TA_O + c0 + lane_off, v);
+            tc::tmem_st32(tmem + TA_O + half * 128 + c0 + lane_off, v);
           }
           l *= al;
         }
-        m = mn;
+        m = mt;
       }
-      float ls = 0.f;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[16];
 #pragma unroll
-      for (int q8 = 0; q8 < 8; q8++) {
-        float p[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const float v = x[8 * q8 + e];
-          p[e] = ex2(v - m);
-          ls += p[e];
-        }
-        uint4 u;
-        u.x = pack2_16<T16>(p[0], p[1]);
-        u.y = pack2_16<T16>(p[2], p[3]);
-        u.z = pack2_16<T16>(p[4], p[5]);
-        u.w = pack2_16<T16>(p[6], p[7]);
-        *reinterpret_cast<uint4*>(sm + AO_P + s * 16384 + swz128(r, q8)) = u;
+      for (int c = 0; c < 32; c += 2) {
+        const float e0 = ex2(fmaf(x[c], sl2, -m)), e1 = ex2(fmaf(x[c + 1], sl2, -m));
+        ls[(c >> 1) & 3] += e0 + e1;
+        pk[c >> 1] = pack2_16<T16>(e0, e1);
       }
-      l += ls;
-      tc::fence_proxy_async();
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      tc::tmem_st16_issue(tmem + TA_P + s * 32 + half * 16 + lane_off, pk);
+      tc::tmem_st_wait();
       tc::fence_before_sync();
       tc::mbar_arrive(&p_full[s]);
     }
-    // epilogue: O / l * sigmoid(gate)
+    bool ok = !bad;
+    // epilogue: O / l * sigmoid(gate); the row's l is the sum of both halves'
+    redl[half * 128 + r] = l;
+    tc::bar_sync(1 + qw, 64);
+    l += redl[(half ^ 1) * 128 + r];
     if (ok && ntiles > 0) ok = tc::mbar_wait(&pv_done[(ntiles - 1) & 1], (uint32_t)(((ntiles - 1) >> 1) & 1));
     if (!ok) {
       atomicOr(fault, 128u);
@@ -269,26 +306,30 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                              : nullptr;
       T16* op = static_cast<T16*>(a.o) + (tok * a.nh + head) * AT_HD;
 #pragma unroll 1
-      for (int c0 = 0; c0 < AT_HD; c0 += 32) {
+      for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
+        uint4 graw[4];
+        if (gp && valid)
+#pragma unroll
+          for (int i = 0; i < 4; i++) graw[i] = *reinterpret_cast<const uint4*>(gp + c0 + 8 * i);
         float v[32];
         tc::tmem_ld32(tmem + TA_O + c0 + lane_off, v);
         if (valid) {
 #pragma unroll
-          for (int c8 = 0; c8 < 32; c8 += 8) {
+          for (int i = 0; i < 4; i++) {
             float g[8];
-            if (gp) load8(gp + c0 + c8, g);
+            if (gp) load8(reinterpret_cast<const T16*>(&graw[i]), g);
             uint4 u;
             uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-              float o0 = v[c8 + 2 * e] * inv, o1 = v[c8 + 2 * e + 1] * inv;
+              float o0 = v[8 * i + 2 * e] * inv, o1 = v[8 * i + 2 * e + 1] * inv;
               if (gp) {
                 o0 /= 1.f + __expf(-g[2 * e]);
                 o1 /= 1.f + __expf(-g[2 * e + 1]);
               }
               w[e] = pack2_16<T16>(o0, o1);
             }
-            *reinterpret_cast<uint4*>(op + c0 + c8) = u;
+            *reinterpret_cast<uint4*>(op + c0 + 8 * i) = u;
           }
         }
       }
