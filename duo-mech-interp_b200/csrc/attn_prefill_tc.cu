@@ -4,35 +4,40 @@
 // attention, then attn_output * sigmoid(gate); the reference's WGSL does the same per (token, head),
 // engine/kernels_qwen35.js:73-123).  One CTA = (row, kv head, tile of 128 / rep query positions); its 128 query rows
 // are the rep q heads of that kv head over the same positions, so every K / V tile is loaded once for all of them.
-//   warp 0     TMA: the Q tile once, then 64-key K and V tiles into two two-stage rings; K_{j+1} is requested
-//              before V_j, so the scores of the next tile never wait behind the previous tile's P V product
-//   warp 1     tcgen05: S_j = Q K_j^T into one of two TMEM buffers (M = 128, N = 64, K = 256), then
-//              O += P_{j-1} V_{j-1} (M = 128, N = 256, K = 64) with P read from TMEM and V straight from its tile
-//              as an MN-major operand
-//   warps 2-9  two threads per query row (warps w and w + 4 share TMEM lanes 32 (w % 4) ..; each takes 32 of a
-//              tile's 64 keys and 128 of O's 256 columns): S from TMEM, the causal mask on the tiles that cross the
+// Key tiles are 128 wide: an M = 128 MMA runs at the tensor core's full rate only from N = 128 up.
+//   warp 0     TMA: the Q tile once, then K as 16 KB slabs (128 keys x 64 head dims) through a six-slot ring and V as
+//              32 KB halves (64 keys x 256 head dims) through a two-slot ring, in the order the MMAs consume them
+//   warp 1     tcgen05: S_j = Q K_j^T (M = 128, N = 128, K = 256) into TMEM buffer j % 2, then
+//              O += P_{j-1} V_{j-1} (M = 128, N = 256, K = 128) with P read from TMEM and V straight from its slots
+//              as an MN-major operand.  Descriptors are computed once and advanced by adds: one thread issues every
+//              MMA, so its instruction count per MMA bounds the pipe at small N.
+//   warps 2-9  two threads per query row (warps w and w + 4 share TMEM lanes 32 (w % 4) ..; each takes 64 of a
+//              tile's 128 keys and 128 of O's 256 columns): S from TMEM, the causal mask on the tiles that cross the
 //              diagonal only, online softmax in base 2 (the pair swaps tile maxima through shared memory), P as
-//              16-bit pairs into TMEM for the next MMA.  O (f32, 256 TMEM columns) is rescaled in place only when a
-//              row's running maximum grows by more than 2^8 (until then P is formed against the older maximum, so
-//              P <= 2^8); at the end O / l times sigmoid(gate) is stored.
-// Scores of tile j + 1 are computed while the softmax of tile j runs.  Barriers: q_full; k_full / k_empty and
-// v_full / v_empty per stage; s_full / p_full / pv_done per parity of the tile index (a parity's next completion needs
-// a P the waiting thread has not written yet, so no phase is skipped).  Cache entries past a row's length are read and
-// masked; V there must be finite (0 x inf would poison O), which the engine's zero-filled caches are.
+//              16-bit pairs written over the first half of its own S buffer for the next MMA.  O (f32, 256 TMEM
+//              columns) is rescaled in place only when a row's running maximum grows by more than 2^8 (until then
+//              P is formed against the older maximum, so P <= 2^8); at the end O / l times sigmoid(gate) is stored.
+// TMEM: S_0, S_1 (128 f32 columns each, P inside), O (256) = all 512.  S_{j+2} is issued only once P_j V_j has
+// completed (it overwrites P_j).  Barriers: q_full; k_full / k_empty per K slot, v_full / v_empty per V slot; s_full,
+// p_full, pv_done per S buffer.  A barrier's next completion always needs an arrival its waiter has not made yet, so
+// no phase is skipped.  Cache entries past a row's length are read and masked; V there must be finite (0 x inf would
+// poison O), which the engine's zero-filled caches are.
 #include "kernels.cuh"
 #include "tc.cuh"
 
 namespace duo {
 namespace {
 
-constexpr int AT_THREADS = 320, AT_BK = 64, AT_HD = 256;
-constexpr uint32_t AO_Q = 0, AO_K = 65536, AO_V = AO_K + 2 * 32768, AO_BAR = AO_V + 2 * 32768;
-// exchange between the two threads of a row: tile maxima and failure flags [parity][half][row], final sums [half][row]
-constexpr uint32_t AO_RED = AO_BAR + 256, AO_REDF = AO_RED + 2048, AO_REDL = AO_REDF + 2048;
-constexpr int AT_SMEM = AO_REDL + 1024 + 1024;
+constexpr int AT_THREADS = 320, AT_BK = 128, AT_HD = 256;
+constexpr int KSLOTS = 6, VSLOTS = 2;
+constexpr uint32_t KSLAB = 16384, VHALF = 32768;
+constexpr uint32_t AO_Q = 0, AO_K = 65536, AO_V = AO_K + KSLOTS * KSLAB, AO_BAR = AO_V + VSLOTS * VHALF;
+// tile maxima of the two threads of a row [parity][half][row] (a failed thread publishes the pattern kBad)
+constexpr uint32_t AO_RED = AO_BAR + 256;
+constexpr int AT_SMEM = AO_RED + 2 * 2 * 128 * 4;  // the base is checked to be 1024-aligned at run time
 static_assert(AT_SMEM <= 232448, "shared memory");
-// TMEM columns: S_0, S_1 (64 f32 each), P_0, P_1 (64 16-bit keys in 32 columns each), O (256 f32)
-constexpr uint32_t TA_S = 0, TA_P = 128, TA_O = 256, TA_COLS = 512;
+constexpr uint32_t kBad = 0xFFFFFFFFu;  // a NaN that fmaxf never returns
+constexpr uint32_t TA_S = 0, TA_O = 256, TA_COLS = 512;
 constexpr float RESCALE_AT = 8.f;  // log2 units
 
 template <typename T16> __device__ __forceinline__ uint32_t pack2_16(float a, float b);
@@ -63,24 +68,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     pdl_wait();
     return;
   }
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t sm[];
   const uint32_t sb = tc::smem_u32(sm);
+  if (sb & 1023u) {  // the swizzled tiles need a 1024-byte aligned base; never observed otherwise
+    if (threadIdx.x == 0) atomicOr(fault, 256u);
+    pdl_wait();
+    return;
+  }
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + AO_BAR);
   uint64_t* q_full = bar;        // [1]
-  uint64_t* k_full = bar + 1;    // [2]
-  uint64_t* k_empty = bar + 3;   // [2]
-  uint64_t* v_full = bar + 5;    // [2]
-  uint64_t* v_empty = bar + 7;   // [2]
-  uint64_t* s_full = bar + 9;    // [2]
-  uint64_t* p_full = bar + 11;   // [2]
-  uint64_t* pv_done = bar + 13;  // [2]
-  uint64_t* drain = bar + 15;    // [1] the issuer's last commit: every MMA of this CTA complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+  uint64_t* k_full = bar + 1;    // [KSLOTS]
+  uint64_t* k_empty = bar + 7;   // [KSLOTS]
+  uint64_t* v_full = bar + 13;   // [VSLOTS]
+  uint64_t* v_empty = bar + 15;  // [VSLOTS]
+  uint64_t* s_full = bar + 17;   // [2]
+  uint64_t* p_full = bar + 19;   // [2]
+  uint64_t* pv_done = bar + 21;  // [2]
+  uint64_t* drain = bar + 23;    // [1] the issuer's last commit: every MMA of this CTA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 24);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(sm + AO_RED);
-  int* redf = reinterpret_cast<int*>(sm + AO_REDF);
-  float* redl = reinterpret_cast<float*>(sm + AO_REDL);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (latest) query tiles first
@@ -89,11 +96,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
   if (tid == 0) {
     tc::mbar_init(q_full, 1);
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < KSLOTS; i++) {
       tc::mbar_init(&k_full[i], 1);
       tc::mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VSLOTS; i++) {
       tc::mbar_init(&v_full[i], 1);
       tc::mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&p_full[i], 256);
       tc::mbar_init(&pv_done[i], 1);
@@ -120,21 +131,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const int ntiles = (n_keys + AT_BK - 1) / AT_BK;
 
   if (warp == 0) {
-    if (lane == 0) {  // ---- TMA producer: Q, K_0, then K_{j+1} and V_j for j = 0, 1, ...
+    if (lane == 0) {  // ---- TMA producer: Q; K_0; then K_{j+1} and V_j for j = 0, 1, ...
+      // K slab u = 4 j + (head-dim quarter) lives in slot u % KSLOTS; V half v = 2 j + (key half) in slot v % VSLOTS.
+      // A slot's barriers complete once per use (parity (u / slots) & 1); its next use waits for the previous one.
       auto load_k = [&](int j) -> bool {
-        const int s = j & 1;
-        if (j >= 2 && !tc::mbar_wait(&k_empty[s], (uint32_t)(((j - 2) >> 1) & 1))) return false;
-        tc::mbar_arrive_expect_tx(&k_full[s], AT_BK * AT_HD * 2);
-        for (int qq = 0; qq < 4; qq++)
-          tc::tma_load_4d(sm + AO_K + s * 32768 + qq * 8192, &tk, qq * 64, kvh, j * AT_BK, b, &k_full[s]);
+        for (int q = 0; q < 4; q++) {
+          const int u = 4 * j + q, sl = u % KSLOTS;
+          if (u >= KSLOTS && !tc::mbar_wait(&k_empty[sl], (uint32_t)((u / KSLOTS - 1) & 1))) return false;
+          tc::mbar_arrive_expect_tx(&k_full[sl], KSLAB);
+          tc::tma_load_4d(sm + AO_K + sl * KSLAB, &tk, q * 64, kvh, j * AT_BK, b, &k_full[sl]);
+        }
         return true;
       };
       auto load_v = [&](int j) -> bool {
-        const int s = j & 1;
-        if (j >= 2 && !tc::mbar_wait(&v_empty[s], (uint32_t)(((j - 2) >> 1) & 1))) return false;
-        tc::mbar_arrive_expect_tx(&v_full[s], AT_BK * AT_HD * 2);
-        for (int qq = 0; qq < 4; qq++)
-          tc::tma_load_4d(sm + AO_V + s * 32768 + qq * 8192, &tv, qq * 64, kvh, j * AT_BK, b, &v_full[s]);
+        for (int h = 0; h < 2; h++) {
+          const int v = 2 * j + h, sl = v % VSLOTS;
+          if (v >= VSLOTS && !tc::mbar_wait(&v_empty[sl], (uint32_t)((v / VSLOTS - 1) & 1))) return false;
+          tc::mbar_arrive_expect_tx(&v_full[sl], VHALF);
+          for (int q = 0; q < 4; q++)
+            tc::tma_load_4d(sm + AO_V + sl * VHALF + q * 8192, &tv, q * 64, kvh, j * AT_BK + h * 64, b, &v_full[sl]);
+        }
         return true;
       };
       tc::mbar_arrive_expect_tx(q_full, 128 * AT_HD * 2);
@@ -156,43 +172,59 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         atomicOr(fault, 128u);
         *abort = 1;
       }
-      // no copy may still be landing when the CTA exits: wait (bounded) for Q and the last two stages of each ring
+      // no copy may still be landing when the CTA exits: wait (bounded) for Q and every slot's last use
       tc::mbar_wait(q_full, 0);
-      for (int j = nk > 2 ? nk - 2 : 0; j < nk; j++) tc::mbar_wait(&k_full[j & 1], (uint32_t)((j >> 1) & 1));
-      for (int j = nv > 2 ? nv - 2 : 0; j < nv; j++) tc::mbar_wait(&v_full[j & 1], (uint32_t)((j >> 1) & 1));
+      for (int u = max(0, 4 * nk - KSLOTS); u < 4 * nk; u++)
+        tc::mbar_wait(&k_full[u % KSLOTS], (uint32_t)((u / KSLOTS) & 1));
+      for (int v = max(0, 2 * nv - VSLOTS); v < 2 * nv; v++)
+        tc::mbar_wait(&v_full[v % VSLOTS], (uint32_t)((v / VSLOTS) & 1));
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer
+      // descriptor of each operand base; a byte offset o inside a swizzled region adds o >> 4 (start-address field)
+      const uint64_t dq = tc::desc_sw128(sb + AO_Q, 16, 1024);
+      const uint64_t dk = tc::desc_sw128(sb + AO_K, 16, 1024);
+      const uint64_t dv = tc::desc_sw128(sb + AO_V, 8192, 1024);
       bool ok = tc::mbar_wait(q_full, 0);
       auto pv = [&](int jp) -> bool {
-        const int sp = jp & 1;
-        if (!tc::mbar_wait(&v_full[sp], (uint32_t)((jp >> 1) & 1))) return false;
-        if (!tc::mbar_wait(&p_full[sp], (uint32_t)((jp >> 1) & 1))) return false;
-        tc::fence_after_sync();
+        const int bf = jp & 1;
+        if (!tc::mbar_wait(&p_full[bf], (uint32_t)((jp >> 1) & 1))) return false;
+        for (int h = 0; h < 2; h++) {
+          const int v = 2 * jp + h, sl = v % VSLOTS;
+          if (!tc::mbar_wait(&v_full[sl], (uint32_t)((v / VSLOTS) & 1))) return false;
+          tc::fence_after_sync();
+          const uint64_t d0 = dv + ((sl * VHALF) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < 4; ks++)
-          tc::mma_ts(tmem + TA_O, tmem + TA_P + sp * 32 + ks * 8,
-                     tc::desc_sw128(sb + AO_V + sp * 32768 + ks * 2048, 8192, 1024), ID_PV,
-                     (jp > 0 || ks > 0) ? 1u : 0u);
-        tc::mma_commit(&pv_done[sp]);
-        tc::mma_commit(&v_empty[sp]);
+          for (int ks = 0; ks < 4; ks++)  // keys 64 h + 16 ks ..: 2048 bytes of the half per step
+            tc::mma_ts(tmem + TA_O, tmem + TA_S + bf * 128 + h * 32 + ks * 8, d0 + ks * 128, ID_PV,
+                       (jp > 0 || h > 0 || ks > 0) ? 1u : 0u);
+          tc::mma_commit(&v_empty[sl]);
+        }
+        tc::mma_commit(&pv_done[bf]);
         return true;
       };
       for (int j = 0; ok && j < ntiles && !*abort; j++) {
-        const int s = j & 1;
-        if (!tc::mbar_wait(&k_full[s], (uint32_t)((j >> 1) & 1))) {
+        const int bf = j & 1;
+        // S_j overwrites P_{j-2} (same buffer): P_{j-2} V_{j-2} must have completed
+        if (j >= 2 && !tc::mbar_wait(&pv_done[bf], (uint32_t)(((j - 2) >> 1) & 1))) {
           ok = false;
           break;
         }
-        tc::fence_after_sync();
+        for (int q = 0; q < 4 && ok; q++) {
+          const int u = 4 * j + q, sl = u % KSLOTS;
+          if (!tc::mbar_wait(&k_full[sl], (uint32_t)((u / KSLOTS) & 1))) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint64_t a0 = dq + ((q * 16384) >> 4), b0 = dk + ((sl * KSLAB) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < 16; ks++)
-          tc::mma_bf16(tmem + TA_S + s * AT_BK,
-                       tc::desc_sw128(sb + AO_Q + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
-                       tc::desc_sw128(sb + AO_K + s * 32768 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), ID_S,
-                       ks > 0 ? 1u : 0u);
-        tc::mma_commit(&s_full[s]);
-        tc::mma_commit(&k_empty[s]);
+          for (int ks = 0; ks < 4; ks++)  // 16 head dims = 32 bytes of the K-major rows per step
+            tc::mma_bf16(tmem + TA_S + bf * 128, a0 + ks * 2, b0 + ks * 2, ID_S, (q > 0 || ks > 0) ? 1u : 0u);
+          tc::mma_commit(&k_empty[sl]);
+        }
+        if (!ok) break;
+        tc::mma_commit(&s_full[bf]);
         if (j >= 1 && !pv(j - 1)) {
           ok = false;
           break;
@@ -218,41 +250,43 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     // times: a failed wait only marks `bad`, and both leave the loop together right after the barrier that shows it.
     bool bad = false;
     for (int j = 0; j < ntiles; j++) {
-      const int s = j & 1;
-      if (!bad && (!tc::mbar_wait(&s_full[s], (uint32_t)((j >> 1) & 1)) || *abort)) bad = true;
-      float x[32];
+      const int bf = j & 1;
+      if (!bad && (!tc::mbar_wait(&s_full[bf], (uint32_t)((j >> 1) & 1)) || *abort)) bad = true;
+      float x[64];
       float mt = -INFINITY;
       if (!bad) {
         tc::fence_after_sync();
-        uint32_t raw[32];
-        tc::tmem_ld32_issue(tmem + TA_S + s * AT_BK + half * 32 + lane_off, raw);
-        tc::tmem_ld_wait(raw);
+        uint32_t raw0[32], raw1[32];
+        tc::tmem_ld32_issue(tmem + TA_S + bf * 128 + half * 64 + lane_off, raw0);
+        tc::tmem_ld32_issue(tmem + TA_S + bf * 128 + half * 64 + 32 + lane_off, raw1);
+        tc::tmem_ld_wait(raw0);
+        tc::tmem_ld_wait(raw1);
 #pragma unroll
-        for (int c = 0; c < 32; c++) x[c] = __uint_as_float(raw[c]);
-        const int k0 = j * AT_BK + half * 32;
+        for (int c = 0; c < 32; c++) {
+          x[c] = __uint_as_float(raw0[c]);
+          x[32 + c] = __uint_as_float(raw1[c]);
+        }
+        const int k0 = j * AT_BK + half * 64;
         if (j * AT_BK + AT_BK - 1 > diag || j * AT_BK + AT_BK > n_keys) {
 #pragma unroll
-          for (int c = 0; c < 32; c++)
+          for (int c = 0; c < 64; c++)
             if (k0 + c > pos || k0 + c >= n_keys) x[c] = -INFINITY;
         }
-        float mx[4] = {x[0], x[1], x[2], x[3]};
+        float mx[8];
 #pragma unroll
-        for (int c = 4; c < 32; c++) mx[c & 3] = fmaxf(mx[c & 3], x[c]);
-        mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        for (int c = 0; c < 8; c++) mx[c] = x[c];
+#pragma unroll
+        for (int c = 8; c < 64; c++) mx[c & 7] = fmaxf(mx[c & 7], x[c]);
+        mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       }
-      red[(s * 2 + half) * 128 + r] = mt;
-      redf[(s * 2 + half) * 128 + r] = bad ? 1 : 0;
+      red[(bf * 2 + half) * 128 + r] = bad ? __uint_as_float(kBad) : mt;
       tc::bar_sync(1 + qw, 64);
-      if (bad || redf[(s * 2 + (half ^ 1)) * 128 + r]) {
+      const float mo = red[(bf * 2 + (half ^ 1)) * 128 + r];
+      if (bad || __float_as_uint(mo) == kBad) {
         bad = true;
         break;
       }
-      mt = fmaxf(mt, red[(s * 2 + (half ^ 1)) * 128 + r]) * sl2;
-      // P buffer s was read by PV_{j-2}
-      if (j >= 2 && !tc::mbar_wait(&pv_done[s], (uint32_t)(((j - 2) >> 1) & 1))) {
-        bad = true;
-        continue;
-      }
+      mt = fmaxf(mt, mo) * sl2;
       if (mt > m + RESCALE_AT) {  // both threads of the row take this branch together (same m, same mt)
         if (j > 0) {  // O holds P_{<j} V against the old maximum: rescale this half once PV_{j-1} is in
           const float al = ex2(m - mt);
@@ -274,24 +308,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         m = mt;
       }
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[16];
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 32; c += 2) {
+      for (int c = 0; c < 64; c += 2) {
         const float e0 = ex2(fmaf(x[c], sl2, -m)), e1 = ex2(fmaf(x[c + 1], sl2, -m));
         ls[(c >> 1) & 3] += e0 + e1;
         pk[c >> 1] = pack2_16<T16>(e0, e1);
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      tc::tmem_st16_issue(tmem + TA_P + s * 32 + half * 16 + lane_off, pk);
-      tc::tmem_st_wait();
+      // keys 64 half .. + 63 as 16-bit pairs: columns 32 half .. + 31 of this tile's S buffer (both threads of the
+      // row have read their S columns: they met at the barrier above)
+      tc::tmem_st32(tmem + TA_S + bf * 128 + half * 32 + lane_off, reinterpret_cast<const float*>(pk));
       tc::fence_before_sync();
-      tc::mbar_arrive(&p_full[s]);
+      tc::mbar_arrive(&p_full[bf]);
     }
     bool ok = !bad;
-    // epilogue: O / l * sigmoid(gate); the row's l is the sum of both halves'
-    redl[half * 128 + r] = l;
+    // epilogue: O / l * sigmoid(gate); the row's l is the sum of both halves' (through the parity buffer that the
+    // last tile did not use: its last reader finished before that tile's barrier)
+    red[((ntiles & 1) * 2 + half) * 128 + r] = l;
     tc::bar_sync(1 + qw, 64);
-    l += redl[(half ^ 1) * 128 + r];
+    l += red[((ntiles & 1) * 2 + (half ^ 1)) * 128 + r];
     if (ok && ntiles > 0) ok = tc::mbar_wait(&pv_done[(ntiles - 1) & 1], (uint32_t)(((ntiles - 1) >> 1) & 1));
     if (!ok) {
       atomicOr(fault, 128u);
@@ -357,10 +393,10 @@ int run_attn_tc(const AttnArgs& a, int dtype, cudaStream_t st) {
   {
     const long dims[4] = {hd, a.nkv, a.max_len, a.b};
     const long strides[3] = {hd * es, a.nkv * hd * es, (long)a.max_len * a.nkv * hd * es};
-    const int box[4] = {64, 1, AT_BK, 1};
+    const int kbox[4] = {64, 1, AT_BK, 1}, vbox[4] = {64, 1, 64, 1};
     const long row0 = (long)a.cache_row0 * a.max_len * a.nkv * hd;
-    DUO_TRY(make_tmap_nd_16(&tk, static_cast<const T16*>(a.kc) + row0, dtype, 4, dims, strides, box));
-    DUO_TRY(make_tmap_nd_16(&tv, static_cast<const T16*>(a.vc) + row0, dtype, 4, dims, strides, box));
+    DUO_TRY(make_tmap_nd_16(&tk, static_cast<const T16*>(a.kc) + row0, dtype, 4, dims, strides, kbox));
+    DUO_TRY(make_tmap_nd_16(&tv, static_cast<const T16*>(a.vc) + row0, dtype, 4, dims, strides, vbox));
   }
   unsigned* fault = tc_fault_ptr();
   if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
