@@ -3,7 +3,9 @@
 // Every kernel that waits on an mbarrier (TMA loads, tcgen05 commits) bounds the wait to 2 s of %globaltimer.  A wait
 // that gives up ORs a code into the device word g_tc_fault and the kernel unwinds instead of hanging the GPU.  Codes:
 // 1 a producer waited for a free ring slot, 2 the MMA issuer waited for a filled slot, 4 the epilogue waited for the
-// accumulator, 8 the persistent MMA issuer waited for a drained accumulator, 16 the conv prologue waited for a tile.
+// accumulator, 8 the persistent MMA issuer waited for a drained accumulator, 16 the conv prologue waited for a tile,
+// 32 / 64 the tcgen05 chunked scan waited for its TMA tiles / its MMAs, 128 the tcgen05 attention prefill gave up a
+// pipeline wait, 256 that kernel found its shared memory misaligned (it then does nothing).
 //
 // A give-up is not allowed to turn into a long stall.  Two mechanisms keep it short:
 //   - device side: the tensor-core kernels that run without a cluster read the word when they start and, if it is

@@ -84,6 +84,11 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = tc::smem_u32(sm);
+  // operand descriptors at the base of shared memory, one per (LBO, SBO) layout; an operand at byte offset o is
+  // desc_add(base, o) (one add per MMA for the single issuing thread)
+  const uint64_t dkm = tc::desc_sw128(sb, 16, 1024);       // K-major
+  const uint64_t dmn8 = tc::desc_sw128(sb, 8192, 1024);    // MN-major, 64-element blocks 8 KB apart (V tile)
+  const uint64_t dmn16 = tc::desc_sw128(sb, 16384, 1024);  // MN-major, 64-element blocks 16 KB apart (K tile)
   float* Gs = reinterpret_cast<float*>(sm + OFF_SMALL);
   float* eg = Gs + 64;
   float* egl = Gs + 128;
@@ -239,8 +244,8 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
 #pragma unroll
       for (int ks = 0; ks < 8; ks++) {
         const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-        tc::mma_bf16(tmem + TQK, tc::desc_sw128(st + OFF_Q0 + off, 16, 1024),
-                     tc::desc_sw128(st + OFF_K0 + off, 16, 1024), IDK64, ks > 0);
+        tc::mma_bf16(tmem + TQK, tc::desc_add(dkm, (st - sb) + OFF_Q0 + off),
+                     tc::desc_add(dkm, (st - sb) + OFF_K0 + off), IDK64, ks > 0);
       }
       tc::mma_commit(mbar);
       n_commit++;
@@ -387,10 +392,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       tc::fence_after_sync();
 #pragma unroll
       for (int ks = 0; ks < 4; ks++) {
-        const uint64_t btb = tc::desc_sw128(sb + OFF_TB + ks * 32, 16, 1024);
-        const uint64_t btbe = tc::desc_sw128(sb + OFF_TBE + ks * 32, 16, 1024);
-        tc::mma_bf16(tmem + TU, tc::desc_sw128(st + OFF_V0 + ks * 2048, 8192, 1024), btb, IDMN64, ks > 0);
-        tc::mma_bf16(tmem + TW, tc::desc_sw128(st + OFF_K0 + ks * 2048, 16384, 1024), btbe, IDMN64, ks > 0);
+        const uint64_t btb = tc::desc_add(dkm, OFF_TB + ks * 32);
+        const uint64_t btbe = tc::desc_add(dkm, OFF_TBE + ks * 32);
+        tc::mma_bf16(tmem + TU, tc::desc_add(dmn8, (st - sb) + OFF_V0 + ks * 2048), btb, IDMN64, ks > 0);
+        tc::mma_bf16(tmem + TW, tc::desc_add(dmn16, (st - sb) + OFF_K0 + ks * 2048), btbe, IDMN64, ks > 0);
       }
       tc::mma_commit(mbar);
       n_commit++;
@@ -444,10 +449,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
 #pragma unroll
       for (int ks = 0; ks < 8; ks++) {
         const uint32_t ak = (ks >> 2) * 16384 + (ks & 3) * 32;
-        const uint64_t as16 = tc::desc_sw128(sb + OFF_S16 + ak, 16, 1024);
-        tc::mma_bf16(tmem + TU, as16, tc::desc_sw128(sb + OFF_W + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), IDK64,
+        const uint64_t as16 = tc::desc_add(dkm, OFF_S16 + ak);
+        tc::mma_bf16(tmem + TU, as16, tc::desc_add(dkm, OFF_W + (ks >> 2) * 8192 + (ks & 3) * 32), IDK64,
                      1);
-        tc::mma_bf16(tmem + TO1, as16, tc::desc_sw128(st + OFF_Q0 + ak, 16, 1024), IDK64, ks > 0);
+        tc::mma_bf16(tmem + TO1, as16, tc::desc_add(dkm, (st - sb) + OFF_Q0 + ak), IDK64, ks > 0);
       }
       tc::mma_commit(mbar);
       n_commit++;
@@ -482,10 +487,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       tc::fence_after_sync();
 #pragma unroll
       for (int ks = 0; ks < 4; ks++) {
-        tc::mma_bf16(tmem + TO2, tc::desc_sw128(sb + OFF_VT + ks * 32, 16, 1024),
-                     tc::desc_sw128(sb + OFF_A + ks * 32, 16, 1024), IDK64, ks > 0);
-        tc::mma_bf16(tmem + TS, tc::desc_sw128(sb + OFF_VTE + ks * 32, 16, 1024),
-                     tc::desc_sw128(st + OFF_K0 + ks * 2048, 16384, 1024), IDBMN128, 1);
+        tc::mma_bf16(tmem + TO2, tc::desc_add(dkm, OFF_VT + ks * 32),
+                     tc::desc_add(dkm, OFF_A + ks * 32), IDK64, ks > 0);
+        tc::mma_bf16(tmem + TS, tc::desc_add(dkm, OFF_VTE + ks * 32),
+                     tc::desc_add(dmn16, (st - sb) + OFF_K0 + ks * 2048), IDBMN128, 1);
       }
       tc::mma_commit(mbar);
       n_commit++;

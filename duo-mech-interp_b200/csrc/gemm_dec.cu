@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = tc::idesc_16_f32(DBM, NB, F16);
+    const uint64_t dw0 = tc::desc_kmajor_sw128(tc::smem_u32(sw)), dx0 = tc::desc_kmajor_sw128(tc::smem_u32(sx));
     for (int kb = 0; kb < num_k; kb++) {
       const int s = kb % C::STAGES;
       const uint32_t ph = (kb / C::STAGES) & 1;
@@ -164,11 +165,10 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         break;
       }
       tc::fence_after_sync();
-      const uint32_t a0 = tc::smem_u32(sw + s * C::W_BYTES), b0 = tc::smem_u32(sx + s * C::X_BYTES);
+      const uint64_t dw = tc::desc_add(dw0, s * C::W_BYTES), dx = tc::desc_add(dx0, s * C::X_BYTES);
 #pragma unroll
-      for (int k = 0; k < DBK / 16; k++)
-        tc::mma_bf16(tmem, tc::desc_kmajor_sw128(a0 + k * 32), tc::desc_kmajor_sw128(b0 + k * 32), idesc,
-                     (kb | k) != 0);
+      for (int k = 0; k < DBK / 16; k++)  // 16 k = 32 bytes along the swizzled rows
+        tc::mma_bf16(tmem, tc::desc_add(dw, 32 * k), tc::desc_add(dx, 32 * k), idesc, (kb | k) != 0);
       tc::mma_commit(&empty[s]);
     }
     if (ok) tc::mma_commit(tmem_full);

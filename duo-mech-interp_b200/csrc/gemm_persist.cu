@@ -153,6 +153,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_16_f32(PBM, BN, F16);
+      const uint64_t da0 = tc::desc_kmajor_sw128(tc::smem_u32(sa)), db0 = tc::desc_kmajor_sw128(tc::smem_u32(sb));
       long use = 0;
       int it = 0;
       for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, it++) {
@@ -174,11 +175,10 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             break;
           }
           tc::fence_after_sync();
-          const uint32_t a0 = tc::smem_u32(sa + s * C::A_BYTES), b0 = tc::smem_u32(sb + s * C::B_BYTES);
+          const uint64_t da = tc::desc_add(da0, s * C::A_BYTES), db = tc::desc_add(db0, s * C::B_BYTES);
 #pragma unroll
-          for (int k = 0; k < PBK / 16; k++)
-            tc::mma_bf16(acc, tc::desc_kmajor_sw128(a0 + k * 32), tc::desc_kmajor_sw128(b0 + k * 32), idesc,
-                         (kb | k) != 0);
+          for (int k = 0; k < PBK / 16; k++)  // 16 k = 32 bytes along the swizzled rows
+            tc::mma_bf16(acc, tc::desc_add(da, 32 * k), tc::desc_add(db, 32 * k), idesc, (kb | k) != 0);
           tc::mma_commit(&empty[s]);
         }
         if (!ok) break;

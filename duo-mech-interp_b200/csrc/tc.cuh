@@ -148,6 +148,12 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr, uint32_t lbo_
   return d;
 }
 
+// The descriptor of the same operand layout starting `bytes` (a multiple of 16) further on: the start address is
+// the low 14 bits (address >> 4) and shared-memory addresses stay below 2^18, so the add never carries out of the
+// field.  One thread issues every MMA of a CTA; building each descriptor from scratch costs it more instructions than
+// a small MMA takes to run, so issue loops compute the base once and advance it with this add.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (uint64_t)(bytes >> 4); }
+
 // Instruction descriptor for kind::f16 with A and B both f16 (bf16 = false) or both bf16 and an f32 accumulator;
 // a_mn / b_mn select the MN-major form of each operand (bits 15 / 16).
 __host__ __device__ constexpr uint32_t idesc_16_mn(int m, int n, bool bf16, bool a_mn, bool b_mn) {
