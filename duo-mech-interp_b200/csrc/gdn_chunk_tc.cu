@@ -167,6 +167,28 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   if (NORM && math) nw = *reinterpret_cast<const float4*>(a.norm_w + 4 * lane);
   uint32_t mph = 0;  // parity of the next MMA commit the math warps wait for
   bool ok = true;
+  // bf16 tiles -> f16 in place (the MMAs mix them with f16 operands written here): part p of np of stage stg.
+  // Chunk 0's stage is converted at its start; chunk c + 1's in two halves while chunk c's U / W and V' / O1 MMAs run.
+  auto convert_tiles = [&](int stg, int p, int np) {
+    if constexpr (sizeof(TI) == 2 && !std::is_same<TI, __half>::value) {
+      uint4* ring = reinterpret_cast<uint4*>(sm + stg * STAGE);
+      const int n = (int)(STAGE / 16), q0 = n * p / np, q1 = n * (p + 1) / np;
+#pragma unroll 4
+      for (int q = q0 + tid; q < q1; q += 128) {
+        const uint4 u = ring[q];
+        const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&u);
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float2 x = __bfloat1622float2(bp[e]);
+          f[2 * e] = x.x;
+          f[2 * e + 1] = x.y;
+        }
+        ring[q] = pack8h(f);
+      }
+      tc::fence_proxy_async();
+    }
+  };
 
 #pragma unroll 1
   for (int c = 0; c < nch; c++) {
@@ -219,22 +241,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
         eg1[2 * lane] = expf(g0);
         eg1[2 * lane + 1] = expf(g1);
       }
-      if constexpr (sizeof(TI) == 2 && !std::is_same<TI, __half>::value) {  // bf16 tiles -> f16 in place
-        uint4* ring = reinterpret_cast<uint4*>(sm + s * STAGE);
-#pragma unroll 4
-        for (int q = tid; q < (int)(STAGE / 16); q += 128) {
-          const uint4 u = ring[q];
-          const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&u);
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const float2 x = __bfloat1622float2(bp[e]);
-            f[2 * e] = x.x;
-            f[2 * e + 1] = x.y;
-          }
-          ring[q] = pack8h(f);
-        }
-      }
+      if (c == 0) convert_tiles(s, 0, 1);
       tc::fence_proxy_async();
     }
     __syncthreads();
@@ -251,6 +258,26 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       n_commit++;
     }
     if (math) {
+      // while P1 runs: S^T (final after chunk c - 1) -> its f16 operand copy, and back into TMEM scaled by e^{G_63}
+      tc::fence_after_sync();
+      {
+        const float el = eg[63];
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          float v[32];
+          tc::tmem_ld32(tmem + TS + c0 + lane_off, v);
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const int dk = c0 + 8 * q;
+            *reinterpret_cast<uint4*>(sm + OFF_S16 + (dk >> 6) * 16384 + swz(tid, (dk & 63) >> 3)) = pack8h(v + 8 * q);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j++) v[j] *= el;
+          tc::tmem_st32(tmem + TS + c0 + lane_off, v);
+        }
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
       ok = tc::mbar_wait(mbar, mph);
       mph ^= 1;
     }
@@ -301,27 +328,51 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       }
     }
     __syncthreads();
-    // ---- T = (I + L)^-1: the 16 x 16 diagonal blocks by forward substitution (2 threads per column)
+    // ---- T = (I + L)^-1: the 16 x 16 diagonal blocks, warp w on block w, by recursive doubling: once the diagonal
+    // blocks of size bs of T hold the inverses of M = I + L's, each pair of them [[A, 0], [C, B]] completes to
+    // [[A^-1, 0], [-B^-1 C A^-1, B^-1]] (two bs x bs products; bs = 1, 2, 4, 8).  Four dependent levels instead of a
+    // 16-step substitution; every entry is an f32 dot product over the triangle only.
     if (math) {
-      const int col = tid >> 1, sub = tid & 1, o = (col >> 4) * 16, cl = col & 15;
-      float tr[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // T[o + 2u + sub][o + cl]
+      const int o = warp * 16;
+      float* T = Tf + o * LP + o;
+      const float* Lb = Lf + o * LP + o;
+      float* Xs = reinterpret_cast<float*>(sm + OFF_SCR + SCR_XH) + warp * 64;  // C A^-1 of the current level
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        float part = 0.f;
+      for (int e = 0; e < 8; e++) {  // identity (the strictly upper part stays zero)
+        const int idx = lane + 32 * e, r = idx >> 4, c = idx & 15;
+        T[r * LP + c] = r == c ? 1.f : 0.f;
+      }
+      __syncwarp();
+      if (lane < 8) T[(2 * lane + 1) * LP + 2 * lane] = -Lb[(2 * lane + 1) * LP + 2 * lane];  // bs = 1
+      __syncwarp();
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const int j = 2 * u + sub;
-          if (j < i) part += Lf[(o + i) * LP + o + j] * tr[u];
+      for (int bs = 2; bs <= 8; bs *= 2) {
+        const int n = 8 * bs;  // entries of the lower-left blocks of this level: (16 / 2 bs) pairs x bs x bs
+#pragma unroll
+        for (int idx = lane; idx < n; idx += 32) {  // X = C A^-1 (A^-1 lower triangular: k >= c)
+          const int pr = idx / (bs * bs), rem = idx % (bs * bs), r = rem / bs, c = rem % bs, p0 = 2 * bs * pr;
+          float x = 0.f;
+#pragma unroll
+          for (int k = 0; k < bs; k++)
+            if (k >= c) x += Lb[(p0 + bs + r) * LP + p0 + k] * T[(p0 + k) * LP + p0 + c];
+          Xs[idx] = x;
         }
-        part += __shfl_xor_sync(0xffffffffu, part, 1);
-        const float v = (i == cl ? 1.f : 0.f) - part;
-        if ((i & 1) == sub) tr[i >> 1] = v;
+        __syncwarp();
+#pragma unroll
+        for (int idx = lane; idx < n; idx += 32) {  // T21 = -B^-1 X (B^-1 unit lower triangular: k <= r)
+          const int pr = idx / (bs * bs), rem = idx % (bs * bs), r = rem / bs, c = rem % bs, p0 = 2 * bs * pr;
+          float y = Xs[pr * bs * bs + r * bs + c];
+#pragma unroll
+          for (int k = 0; k < bs; k++)
+            if (k < r) y += T[(p0 + bs + r) * LP + p0 + bs + k] * Xs[pr * bs * bs + k * bs + c];
+          T[(p0 + bs + r) * LP + p0 + c] = -y;
+        }
+        __syncwarp();
       }
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int r = o + 2 * u + sub;
-        Tf[r * LP + o + cl] = tr[u];
-        th[r * HP + o + cl] = __float2half_rn(tr[u]);
+      for (int e = 0; e < 8; e++) {  // the f16 copy for the off-diagonal products (whole blocks, zeros included)
+        const int idx = lane + 32 * e, r = idx >> 4, c = idx & 15;
+        th[(o + r) * HP + o + c] = __float2half_rn(T[r * LP + c]);
       }
     }
     __syncthreads();
@@ -401,7 +452,11 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       n_commit++;
     }
     if (math) {
-      ok = tc::mbar_wait(mbar, mph);
+      if (c + 1 < nch) {  // while U / W run: the first half of chunk c + 1's tiles (requested at this chunk's start)
+        ok = tc::mbar_wait(&full[s ^ 1], (uint32_t)(((c + 1) >> 1) & 1));
+        if (ok) convert_tiles(s ^ 1, 0, 2);
+      }
+      ok = tc::mbar_wait(mbar, mph) && ok;
       mph ^= 1;
     }
     if (__syncthreads_or(!ok)) {
@@ -422,23 +477,6 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
         for (int i = 0; i < 64; i++)
           wb[(i * 128 + ((cidx ^ (i & 7)) << 4)) / 2 + e] = __float2half_rn(-w[i]);
       }
-      // S^T -> its f16 operand copy, and back into TMEM scaled by e^{G_63}
-      {
-        const float el = eg[63];
-#pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          float v[32];
-          tc::tmem_ld32(tmem + TS + c0 + lane_off, v);
-#pragma unroll
-          for (int q = 0; q < 4; q++) {
-            const int dk = c0 + 8 * q;
-            *reinterpret_cast<uint4*>(sm + OFF_S16 + (dk >> 6) * 16384 + swz(tid, (dk & 63) >> 3)) = pack8h(v + 8 * q);
-          }
-#pragma unroll
-          for (int j = 0; j < 32; j++) v[j] *= el;
-          tc::tmem_st32(tmem + TS + c0 + lane_off, v);
-        }
-      }
       tc::fence_proxy_async();
       tc::fence_before_sync();
     }
@@ -458,6 +496,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       n_commit++;
     }
     if (math) {
+      if (c + 1 < nch) convert_tiles(s ^ 1, 1, 2);  // while V' / O1 run: the second half
       ok = tc::mbar_wait(mbar, mph);
       mph ^= 1;
     }
