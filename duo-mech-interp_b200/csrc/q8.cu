@@ -4,8 +4,10 @@
 // along a row; scale = absmax / 127 (1 for an all-zero group); q = round(v / scale), half to even.  A row-major
 // int8[n, k] array is byte-for-byte the reference's packing of four values per little-endian u32.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace duo {
 
@@ -176,11 +178,207 @@ __global__ void __launch_bounds__(256) q8_gemv_kernel(const TX* __restrict__ x, 
 
 template <int M> constexpr int gemv_rows() { return M <= 2 ? 8 : M <= 4 ? 4 : 2; }
 
+// The same GEMV with the weights streamed through shared memory: a persistent grid (one CTA per SM), whose producer
+// thread copies blocks of CW RPW consecutive weight rows (contiguous bytes of the row-major [n, k] matrix) and their
+// group scales into a ring of `nst` slots with 1D bulk copies (cp.async.bulk, completion on a per-slot mbarrier), so
+// ~200 KB per SM are in flight however long the consumers take; CW consumer warps take RPW rows of each block
+// (16 for one activation row, whose ~3 instructions per weight byte need the warps to hide latency).
+// CTA b handles blocks b, b + grid, ..., so neighbouring CTAs stream neighbouring memory.  Per row the arithmetic is
+// exactly the register kernel's (lane l takes bytes 16 l + 512 j, 16 products in f32 times the group scale,
+// accumulated over j, then the same butterfly), so the two give identical outputs.  Waits are bounded (fault code
+// 1024 when one gives up).
+constexpr int GS_RING = 210 * 1024;
+template <int M> constexpr int gemv_stream_warps() { return M == 1 ? 16 : 8; }
+
+template <int M, int RPW, bool XPRE, typename TX, typename TY>
+__global__ void __launch_bounds__(32 * gemv_stream_warps<M>() + 32, 1)
+    q8_gemv_stream_kernel(const TX* __restrict__ x, int k, const int8_t* __restrict__ q, const float* __restrict__ s,
+                          int group, int n, TY* __restrict__ y, int accumulate, int nst, unsigned* fault) {
+  constexpr int CW = gemv_stream_warps<M>(), RS = CW * RPW;  // consumer warps, rows per block
+  if (tc::fault_pending(fault)) {
+    pdl_wait();
+    return;
+  }
+  extern __shared__ __align__(128) uint8_t gsm[];
+  const int ng = k / group;
+  const uint32_t wb = (uint32_t)(RS * k), sbytes = (uint32_t)(RS * ng * 4);
+  uint8_t* wring = gsm;
+  float* sring = reinterpret_cast<float*>(gsm + (size_t)nst * wb);
+  uint64_t* full = reinterpret_cast<uint64_t*>(gsm + (size_t)nst * (wb + sbytes));
+  uint64_t* empty = full + nst;
+  volatile int* abort = reinterpret_cast<volatile int*>(empty + nst);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nst; i++) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], CW);
+    }
+    *abort = 0;
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_enter();
+  const int nblk = (n + RS - 1) / RS;
+  if (warp == CW) {
+    if (lane == 0) {  // producer
+      int issued = 0;
+      for (int bk = blockIdx.x, li = 0; bk < nblk && !*abort; bk += gridDim.x, li++) {
+        const int sl = li % nst;
+        if (li >= nst && !tc::mbar_wait(&empty[sl], (uint32_t)((li / nst - 1) & 1))) {
+          atomicOr(fault, 1024u);
+          *abort = 1;
+          break;
+        }
+        const int rows = min(RS, n - bk * RS);  // n % 4 == 0: the scale bytes stay a multiple of 16
+        tc::mbar_arrive_expect_tx(&full[sl], (uint32_t)(rows * k + rows * ng * 4));
+        tc::bulk_g2s(wring + (size_t)sl * wb, q + (long)bk * RS * k, (uint32_t)(rows * k), &full[sl]);
+        tc::bulk_g2s(sring + (size_t)sl * (sbytes / 4), s + (long)bk * RS * ng, (uint32_t)(rows * ng * 4), &full[sl]);
+        issued = li + 1;
+      }
+      // no copy may still be landing when the CTA exits (the consumers wait for every block unless aborted)
+      for (int li = max(0, issued - nst); li < issued; li++) tc::mbar_wait(&full[li % nst], (uint32_t)((li / nst) & 1));
+    }
+  } else {  // consumers: warp w takes rows w RPW .. of each block
+    // XPRE (one activation row, k <= 1024): this lane's 32 activations stay in registers for the whole call
+    float xr[XPRE ? 2 : 1][16];
+    if constexpr (XPRE) {
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const int c = lane * 16 + 512 * j;
+        if (c < k) ld_x16(x + c, xr[j]);
+      }
+    }
+    for (int bk = blockIdx.x, li = 0; bk < nblk; bk += gridDim.x, li++) {
+      const int sl = li % nst;
+      if (*abort || !tc::mbar_wait(&full[sl], (uint32_t)((li / nst) & 1))) {
+        if (lane == 0) {
+          atomicOr(fault, 1024u);
+          *abort = 1;
+        }
+        break;
+      }
+      const int r0 = bk * RS + warp * RPW;
+      const uint8_t* wr = wring + (size_t)sl * wb + (size_t)warp * RPW * k;
+      const float* sr = sring + (size_t)sl * (sbytes / 4) + warp * RPW * ng;
+      float acc[M][RPW];
+#pragma unroll
+      for (int i = 0; i < M; i++)
+#pragma unroll
+        for (int r = 0; r < RPW; r++) acc[i][r] = 0.f;
+#pragma unroll 2
+      for (int c = lane * 16, j = 0; c < k; c += 512, j++) {
+        uint4 u[RPW];
+        float sc[RPW];
+#pragma unroll
+        for (int r = 0; r < RPW; r++) {  // rows past n hold stale bytes: computed, never stored
+          u[r] = *reinterpret_cast<const uint4*>(wr + (size_t)r * k + c);
+          sc[r] = sr[r * ng + c / group];
+        }
+#pragma unroll
+        for (int i = 0; i < M; i++) {
+          float xv[16];
+          if constexpr (XPRE) {
+#pragma unroll
+            for (int e = 0; e < 16; e++) xv[e] = xr[j & 1][e];
+          } else {
+            ld_x16(x + (long)i * k + c, xv);
+          }
+#pragma unroll
+          for (int r = 0; r < RPW; r++) {
+            float w[16];
+            i8x4_to_f32(u[r].x, w);
+            i8x4_to_f32(u[r].y, w + 4);
+            i8x4_to_f32(u[r].z, w + 8);
+            i8x4_to_f32(u[r].w, w + 12);
+            float d = 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; j++) d = fmaf(w[j], xv[j], d);
+            acc[i][r] = fmaf(d, sc[r], acc[i][r]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty[sl]);  // this warp is done with the slot's bytes
+#pragma unroll
+      for (int i = 0; i < M; i++)
+#pragma unroll
+        for (int r = 0; r < RPW; r++) acc[i][r] = warp_sum(acc[i][r]);
+#pragma unroll
+      for (int i = 0; i < M; i++)
+#pragma unroll
+        for (int r = 0; r < RPW; r++)
+          if (lane == i * RPW + r && r0 + r < n) {
+            TY* yp = y + (long)i * n + r0 + r;
+            float v = acc[i][r];
+            if (accumulate) v += to_f(*yp);
+            *yp = from_f<TY>(v);
+          }
+    }
+  }
+  __syncthreads();
+}
+
+template <int M, int RPW, bool XPRE, typename TX, typename TY>
+int run_gemv_stream(const TX* x, int k, const int8_t* q, const float* s, int group, int n, TY* y, int accumulate,
+                    cudaStream_t st) {
+  constexpr int RS = gemv_stream_warps<M>() * RPW;
+  const long slot = (long)RS * k + (long)RS * (k / group) * 4;
+  const int nst = (int)std::min<long>(8, GS_RING / slot);
+  const int smem = (int)(nst * slot + 16 * nst + 16);
+  unsigned* fault = tc_fault_ptr();
+  if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
+  auto kern = q8_gemv_stream_kernel<M, RPW, XPRE, TX, TY>;
+  DUO_TRY(ensure_smem_attr(kern, smem));
+  const int grid = std::min(cdiv(n, RS), sm_count());
+  DUO_CUDA_TRY(::duo::launch_kernel(kern, grid, 32 * gemv_stream_warps<M>() + 32, smem, st, x, k, q, s, group, n, y,
+                                    accumulate, nst, fault));
+  DUO_LAUNCH_CHECK("q8_gemv_stream_kernel");
+  return DUO_OK;
+}
+
+// Streaming form for matrices large enough to be bandwidth-bound: 16-byte aligned weights and scales, k a multiple
+// of 16 and of the group, n a multiple of 4 (whole 16-byte scale copies), and at least two ring slots.
+// Rows per consumer warp and block: ~4 KB of a block per warp, at most 2 rows when m > 4 (registers).
+static int gemv_stream_rpw(int m, int k) {
+  const int r = k <= 1024 ? 4 : k <= 2048 ? 2 : 1;
+  return m > 4 ? std::min(r, 2) : r;
+}
+static bool gemv_stream_ok(int m, int k, const int8_t* q, const float* s, int group, int n) {
+  if (n < 2048 || n % 4 || k % 16 || group <= 0 || k % group) return false;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(s)) & 15) return false;
+  const int rpw = gemv_stream_rpw(m, k);
+  const long rs = (m == 1 ? 16L : 8L) * rpw;
+  const long slot = rs * k + rs * (k / group) * 4;
+  return GS_RING / slot >= 2;
+}
+
 template <typename TX, typename TY>
 int launch_gemv_t(const void* x, int m, int k, const int8_t* q, const float* s, int group, int n, void* y,
                   int accumulate, cudaStream_t st) {
   const TX* xp = static_cast<const TX*>(x);
   TY* yp = static_cast<TY*>(y);
+  if (m >= 1 && m <= 8 && gemv_stream_ok(m, k, q, s, group, n)) {
+    const int rpw = gemv_stream_rpw(m, k);
+    auto pick = [&](auto mm) -> int {
+      constexpr int MM = decltype(mm)::value;
+      if constexpr (MM == 1)
+        if (rpw == 4) return run_gemv_stream<1, 4, true>(xp, k, q, s, group, n, yp, accumulate, st);  // k <= 1024
+      if constexpr (MM <= 4)
+        if (rpw == 4) return run_gemv_stream<MM, 4, false>(xp, k, q, s, group, n, yp, accumulate, st);
+      if (rpw == 2) return run_gemv_stream<MM, 2, false>(xp, k, q, s, group, n, yp, accumulate, st);
+      return run_gemv_stream<MM, 1, false>(xp, k, q, s, group, n, yp, accumulate, st);
+    };
+    switch (m) {
+      case 1: return pick(std::integral_constant<int, 1>{});
+      case 2: return pick(std::integral_constant<int, 2>{});
+      case 3: return pick(std::integral_constant<int, 3>{});
+      case 4: return pick(std::integral_constant<int, 4>{});
+      case 5: return pick(std::integral_constant<int, 5>{});
+      case 6: return pick(std::integral_constant<int, 6>{});
+      case 7: return pick(std::integral_constant<int, 7>{});
+      default: return pick(std::integral_constant<int, 8>{});
+    }
+  }
   auto grid_for = [&](int rows_per_warp) { return std::max(1, std::min(cdiv(n, 8 * rows_per_warp), 4 * sm_count())); };
   switch (m) {
 #define DUO_GEMV_CASE(MM)                                                                                          \

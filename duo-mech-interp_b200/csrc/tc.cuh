@@ -98,6 +98,14 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, i
                "r"(x), "r"(y)
                : "memory");
 }
+// 1D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global to this CTA's shared
+// memory, completing as transactions on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // returns once the source shared memory of every committed bulk store has been read
