@@ -3,6 +3,7 @@
 #include <atomic>
 #include <cstring>
 #include <mutex>
+#include <map>
 #include <set>
 #include <tuple>
 
@@ -52,12 +53,15 @@ int ensure_smem_attr_fn(const void* func, int bytes) {
   int dev = 0;
   DUO_CUDA_TRY(cudaGetDevice(&dev));
   static std::mutex mu;
-  static std::set<std::tuple<int, const void*, int>> done;
-  const auto key = std::make_tuple(dev, func, bytes);
+  // the largest size set so far per (device, kernel): the attribute is a maximum, so it is only ever raised (a
+  // kernel launched with several sizes would otherwise be left at a smaller one than a size recorded as done)
+  static std::map<std::pair<int, const void*>, int> set_to;
+  const auto key = std::make_pair(dev, func);
   std::lock_guard<std::mutex> lock(mu);
-  if (done.count(key)) return DUO_OK;
+  const auto it = set_to.find(key);
+  if (it != set_to.end() && it->second >= bytes) return DUO_OK;
   DUO_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  done.insert(key);
+  set_to[key] = bytes;
   return DUO_OK;
 }
 

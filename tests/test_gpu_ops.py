@@ -94,6 +94,20 @@ def test_q8_gemv_streaming(ops, m, n, k, group):
     assert ops.fault_status() == 0
 
 
+def test_q8_gemv_streaming_alternating_sizes(ops):
+    """One streaming kernel launched with a large, a small, then the large shared-memory ring again (k = 1024 and
+    k = 256 give different ring sizes): the kernel's shared-memory limit must never be left below a size in use."""
+    outs = []
+    for n, k in [(4096, 1024), (2048, 256), (4096, 1024), (2048, 256)]:
+        w = torch.randn(n, k, generator=_seed(n + k)) * 0.02
+        x = torch.randn(1, k, generator=_seed(k))
+        q, s = ops.q8_quantize(w.cuda(), 128)
+        ref = oq8.matvec(x.numpy(), q.cpu().numpy(), s.cpu().numpy(), 128)
+        outs.append(rel_max(ops.q8_gemv(x.cuda(), q, s), ref))
+    assert max(outs) < 1e-5
+    assert ops.fault_status() == 0
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # tcgen05 GEMM vs a torch fp32 matmul of the same bf16 operands
 
