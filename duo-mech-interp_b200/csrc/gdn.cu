@@ -496,7 +496,9 @@ template <typename T>
 __global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnConvArgs ca, GdnScanArgs a) {
   extern __shared__ __align__(16) float ring[];  // [DEC_NS][128 rows][64 columns]
   __shared__ float qs[128], ks[128], vs[128], os[128];
-  __shared__ __align__(16) float red[8][64];
+  // per-warp partial column sums of u (redu) and o (redo): two buffers, so that each is rewritten only after a
+  // barrier that every reader of its previous contents has passed (two barriers per slice instead of four)
+  __shared__ __align__(16) float redu[8][64], redo[8][64];
   __shared__ float red8[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cg = tid & 15, rg = tid >> 4;
@@ -605,7 +607,7 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnCon
       }
 #pragma unroll
       for (int i = 0; i < 4; i++) u4[i] += __shfl_xor_sync(0xffffffffu, u4[i], 16);
-      if (lane < 16) *reinterpret_cast<float4*>(&red[warp][cg * 4]) = make_float4(u4[0], u4[1], u4[2], u4[3]);
+      if (lane < 16) *reinterpret_cast<float4*>(&redu[warp][cg * 4]) = make_float4(u4[0], u4[1], u4[2], u4[3]);
       __syncthreads();
       float d4[4];
 #pragma unroll
@@ -613,10 +615,9 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnCon
         const int col = cg * 4 + i;
         float u = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; w++) u += red[w][col];
+        for (int w = 0; w < 8; w++) u += redu[w][col];
         d4[i] = beta * (vs[half * 64 + col] - u);
       }
-      __syncthreads();  // red is reused below
       float o4[4] = {0, 0, 0, 0};
       float4* S4 = state_of(j) + half * 16 + cg;
 #pragma unroll
@@ -630,16 +631,16 @@ __global__ void __launch_bounds__(DEC_THREADS, DEC_CPS) gdn_decode_kernel(GdnCon
       }
 #pragma unroll
       for (int i = 0; i < 4; i++) o4[i] += __shfl_xor_sync(0xffffffffu, o4[i], 16);
-      if (lane < 16) *reinterpret_cast<float4*>(&red[warp][cg * 4]) = make_float4(o4[0], o4[1], o4[2], o4[3]);
+      if (lane < 16) *reinterpret_cast<float4*>(&redo[warp][cg * 4]) = make_float4(o4[0], o4[1], o4[2], o4[3]);
       __syncthreads();
       if (tid < 64) {
         float o = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; w++) o += red[w][tid];
+        for (int w = 0; w < 8; w++) o += redo[w][tid];
         os[half * 64 + tid] = o;
       }
-      __syncthreads();  // os complete; red free for the next slice
     }
+    __syncthreads();  // os complete
 
     // 3. gated RMSNorm over the head's 128 outputs (warps 0..3)
     if (tid < 128) {
