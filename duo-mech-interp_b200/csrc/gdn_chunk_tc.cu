@@ -205,14 +205,13 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
         bnext = a.beta[m * a.h + h];
       }
     }
-    // this chunk's z (gate of the gated norm): warp w takes token rows w, w + 4, ..; lane 4 dv columns
-    uint2 zr[16];
+    // this chunk's z (gate of the gated norm) into L2 now, into registers only for the output (32 registers held
+    // across the whole chunk cost this 254-register kernel more than an L2 round trip): thread i, one 128-byte line
     if (NORM && math) {
-      const TI* zp = static_cast<const TI*>(a.z);
-#pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const int t = t0 + warp + 4 * i;
-        if (t < a.t) zr[i] = *reinterpret_cast<const uint2*>(zp + ((long)b * a.t + t) * a.z_stride + h * 128 + 4 * lane);
+      const int t = t0 + (tid >> 1);
+      if (t < a.t) {
+        const TI* zl = static_cast<const TI*>(a.z) + ((long)b * a.t + t) * a.z_stride + h * 128 + (tid & 1) * 64;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(zl));
       }
     }
     if (math) ok = tc::mbar_wait(&full[s], (uint32_t)((c >> 1) & 1));
@@ -543,6 +542,15 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       goto bail;
     }
     // ---- output: O = e^G O1 / sqrt(dk) + O2, through shared memory to token rows, gated RMSNorm, store
+    uint2 zr[16];  // z: warp w takes token rows w, w + 4, ..; lane 4 dv columns (L2 hits under the TMEM drain below)
+    if (NORM && math) {
+      const TI* zp = static_cast<const TI*>(a.z);
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const int t = t0 + warp + 4 * i;
+        if (t < a.t) zr[i] = *reinterpret_cast<const uint2*>(zp + ((long)b * a.t + t) * a.z_stride + h * 128 + 4 * lane);
+      }
+    }
     if (math) {
       tc::fence_after_sync();
 #pragma unroll 1
