@@ -542,15 +542,6 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       goto bail;
     }
     // ---- output: O = e^G O1 / sqrt(dk) + O2, through shared memory to token rows, gated RMSNorm, store
-    uint2 zr[16];  // z: warp w takes token rows w, w + 4, ..; lane 4 dv columns (L2 hits under the TMEM drain below)
-    if (NORM && math) {
-      const TI* zp = static_cast<const TI*>(a.z);
-#pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const int t = t0 + warp + 4 * i;
-        if (t < a.t) zr[i] = *reinterpret_cast<const uint2*>(zp + ((long)b * a.t + t) * a.z_stride + h * 128 + 4 * lane);
-      }
-    }
     if (math) {
       tc::fence_after_sync();
 #pragma unroll 1
@@ -565,28 +556,64 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
     __syncthreads();
     if (math) {
       TI* op = static_cast<TI*>(a.o);
+      uint2 zr[16];  // z (in L2 since the chunk's start): warp w takes token rows w, w + 4, ..; lane 4 dv columns
+      if (NORM) {
+        const TI* zp = static_cast<const TI*>(a.z);
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const int tt = warp + 4 * i, t = t0 + tt;
-        const float4 ov = *reinterpret_cast<const float4*>(Ot + tt * 128 + 4 * lane);
-        float o[4] = {ov.x, ov.y, ov.z, ov.w};
+        for (int i = 0; i < 16; i++) {
+          const int t = t0 + warp + 4 * i;
+          if (t < a.t) zr[i] = *reinterpret_cast<const uint2*>(zp + ((long)b * a.t + t) * a.z_stride + h * 128 + 4 * lane);
+        }
+      }
+#pragma unroll
+      for (int ps = 0; ps < 2; ps++) {  // token rows warp + 4 i, i = 8 ps .. 8 ps + 7 (two passes: registers)
+        float o[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float4 ov = *reinterpret_cast<const float4*>(Ot + (warp + 4 * (8 * ps + i)) * 128 + 4 * lane);
+          o[i][0] = ov.x; o[i][1] = ov.y; o[i][2] = ov.z; o[i][3] = ov.w;
+        }
         if (NORM) {
-          const float ss = warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
-          const float rms = rsqrtf(ss / 128.f + a.eps);
-          if (t < a.t) {
-            const TI* zt = reinterpret_cast<const TI*>(&zr[i]);
-            o[0] *= rms * nw.x * silu_tanh(to_f(zt[0])) * hs;
-            o[1] *= rms * nw.y * silu_tanh(to_f(zt[1])) * hs;
-            o[2] *= rms * nw.z * silu_tanh(to_f(zt[2])) * hs;
-            o[3] *= rms * nw.w * silu_tanh(to_f(zt[3])) * hs;
+          // the 8 rows' sums of squares over the warp together, by recursive halving: lane l ends with row
+          // 4 b4 + 2 b3 + b2 (bits of l); 10 shuffles for the 8 rows instead of 5 dependent ones per row
+          float v[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) v[i] = o[i][0] * o[i][0] + o[i][1] * o[i][1] + o[i][2] * o[i][2] + o[i][3] * o[i][3];
+#pragma unroll
+          for (int w = 16, n = 4; w >= 4; w >>= 1, n >>= 1) {
+            const bool up = lane & w;
+#pragma unroll
+            for (int i = 0; i < n; i++) {
+              const float send = up ? v[i] : v[i + n];
+              const float keep = up ? v[i + n] : v[i];
+              v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+            }
+          }
+          v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+          v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+          const float rms_mine = rsqrtf(v[0] / 128.f + a.eps);
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const float rms = __shfl_sync(0xffffffffu, rms_mine, ((i >> 2) << 4) | (((i >> 1) & 1) << 3) | ((i & 1) << 2));
+            if (t0 + warp + 4 * (8 * ps + i) < a.t) {
+              const TI* zt = reinterpret_cast<const TI*>(&zr[8 * ps + i]);
+              o[i][0] *= rms * nw.x * silu_tanh(to_f(zt[0])) * hs;
+              o[i][1] *= rms * nw.y * silu_tanh(to_f(zt[1])) * hs;
+              o[i][2] *= rms * nw.z * silu_tanh(to_f(zt[2])) * hs;
+              o[i][3] *= rms * nw.w * silu_tanh(to_f(zt[3])) * hs;
+            }
           }
         }
-        if (t < a.t) {
-          uint2 u;
-          TI* p = reinterpret_cast<TI*>(&u);
 #pragma unroll
-          for (int e = 0; e < 4; e++) p[e] = from_f<TI>(o[e]);
-          *reinterpret_cast<uint2*>(op + ((long)b * a.t + t) * a.o_stride + h * 128 + 4 * lane) = u;
+        for (int i = 0; i < 8; i++) {
+          const int t = t0 + warp + 4 * (8 * ps + i);
+          if (t < a.t) {
+            uint2 u;
+            TI* p = reinterpret_cast<TI*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; e++) p[e] = from_f<TI>(o[i][e]);
+            *reinterpret_cast<uint2*>(op + ((long)b * a.t + t) * a.o_stride + h * 128 + 4 * lane) = u;
+          }
         }
       }
     }
