@@ -262,17 +262,18 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       {
         const float el = eg[63];
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          float v[32];
-          tc::tmem_ld32(tmem + TS + c0 + lane_off, v);
+        for (int c0 = 0; c0 < 128; c0 += 64) {  // 64 columns per TMEM round trip
+          float v[64];
+          tc::tmem_ld2x32(tmem + TS + c0 + lane_off, tmem + TS + c0 + 32 + lane_off, v, v + 32);
 #pragma unroll
-          for (int q = 0; q < 4; q++) {
+          for (int q = 0; q < 8; q++) {
             const int dk = c0 + 8 * q;
             *reinterpret_cast<uint4*>(sm + OFF_S16 + (dk >> 6) * 16384 + swz(tid, (dk & 63) >> 3)) = pack8h(v + 8 * q);
           }
 #pragma unroll
-          for (int j = 0; j < 32; j++) v[j] *= el;
+          for (int j = 0; j < 64; j++) v[j] *= el;
           tc::tmem_st32(tmem + TS + c0 + lane_off, v);
+          tc::tmem_st32(tmem + TS + c0 + 32 + lane_off, v + 32);
         }
       }
       tc::fence_proxy_async();
@@ -287,8 +288,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
     if (math) {
       tc::fence_after_sync();
       float x[64];
-      tc::tmem_ld32(tmem + TQK + lane_off, x);
-      tc::tmem_ld32(tmem + TQK + 32 + lane_off, x + 32);
+      tc::tmem_ld2x32(tmem + TQK + lane_off, tmem + TQK + 32 + lane_off, x, x + 32);
       // the decay e^{G_i - G_j} of row i, for j walking down from i: the product of the tokens' own decays e^{g_t},
       // t = j + 1 .. i (a multiply per entry instead of an exponential; it only shrinks, so it underflows to 0
       // gracefully however strong the decay)
@@ -467,8 +467,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       // -W, token-major (row i, dk contiguous; two 64-dk atoms): thread d writes column d
       {
         float w[64];
-        tc::tmem_ld32(tmem + TW + lane_off, w);
-        tc::tmem_ld32(tmem + TW + 32 + lane_off, w + 32);
+        tc::tmem_ld2x32(tmem + TW + lane_off, tmem + TW + 32 + lane_off, w, w + 32);
         const int d = tid;
         __half* wb = reinterpret_cast<__half*>(sm + OFF_W + (d >> 6) * 8192);
         const int cidx = (d & 63) >> 3, e = d & 7;
@@ -506,8 +505,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
     if (math) {  // V'^T and V'^T diag(e^{G_63 - G}), K-major (row dv, 64 tokens)
       tc::fence_after_sync();
       float v[64];
-      tc::tmem_ld32(tmem + TU + lane_off, v);
-      tc::tmem_ld32(tmem + TU + 32 + lane_off, v + 32);
+      tc::tmem_ld2x32(tmem + TU + lane_off, tmem + TU + 32 + lane_off, v, v + 32);
 #pragma unroll
       for (int q = 0; q < 8; q++) {
         *reinterpret_cast<uint4*>(sm + OFF_VT + swz(tid, q)) = pack8h(v + 8 * q);
@@ -547,8 +545,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < 64; c0 += 32) {
         float o1[32], o2[32];
-        tc::tmem_ld32(tmem + TO1 + c0 + lane_off, o1);
-        tc::tmem_ld32(tmem + TO2 + c0 + lane_off, o2);
+        tc::tmem_ld2x32(tmem + TO1 + c0 + lane_off, tmem + TO2 + c0 + lane_off, o1, o2);
 #pragma unroll
         for (int t = 0; t < 32; t++) Ot[(c0 + t) * 128 + tid] = eg[c0 + t] * QSCALE * o1[t] + o2[t];
       }

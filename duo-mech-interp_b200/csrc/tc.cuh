@@ -277,6 +277,20 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
   for (int j = 0; j < 32; j++) asm volatile("" : "+r"(r[j]));
 }
 
+// Two 32-column loads (columns of TMEM addresses ta and tb) in flight together, one wait: a and b receive 32 floats.
+__device__ __forceinline__ void tmem_ld2x32(uint32_t ta, uint32_t tb, float* a, float* b) {
+  uint32_t ra[32], rb[32];
+  tmem_ld32_issue(ta, ra);
+  tmem_ld32_issue(tb, rb);
+  tmem_ld_wait(ra);
+  tmem_ld_wait(rb);
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    a[j] = __uint_as_float(ra[j]);
+    b[j] = __uint_as_float(rb[j]);
+  }
+}
+
 }  // namespace tc
 
 // Host: build a 2D 16-bit (DUO_BF16 / DUO_F16) tensor map over a row-major [rows, cols] matrix (leading dim ld
