@@ -5,6 +5,7 @@
 // stream is f32; GEMM inputs, projections, caches and mixer outputs use the engine's activation dtype (f32 = the
 // reference's precision, bf16 = the tensor-core path).  The Gated DeltaNet state and the conv state are f32 always.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -56,6 +57,7 @@ struct duo_engine {
   int rows = 0, max_len = 0, max_tokens = 0;
   float* x = nullptr;
   void* xn = nullptr;
+  float* nrm_part[2] = {nullptr, nullptr};  // fused-norm row partials: [256 rows][hidden / 128] each
   void* y = nullptr;
   void* qkv = nullptr;
   float* g = nullptr;
@@ -216,19 +218,48 @@ int capture_rows(duo_engine* e, int kind, int l, const void* src, int dtype, int
   return DUO_OK;
 }
 
+bool fused_norm_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("DUO_FUSED_NORM");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// the residual-add epilogue also writes the next RMSNorm's weighted input (xn) and its row partials
+void set_norm_out(GemmEpiArgs& ep, const float* w, void* xn, float* part) {
+  ep.nrm_w = w;
+  ep.nrm_out = xn;
+  ep.nrm_part = part;
+}
+
+// the GEMM consumes xn written by set_norm_out: its accumulator rows are scaled by rsqrt(mean x^2 + eps)
+void set_row_norm(GemmEpiArgs& ep, const float* part, int d, float eps) {
+  ep.row_part = part;
+  ep.row_blocks = d / 128;
+  ep.row_d = d;
+  ep.row_eps = eps;
+}
+
 int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, int T, int vec_layer,
                  cudaStream_t st) {
   const duo_config& c = e->cfg;
   const int M = rows * T;
   const int H = c.hidden;
   const int act = e->act;
+  // RMSNorm fused into the decode GEMMs (bf16, 8 < M <= 256 rows): the residual-add epilogue writes the next norm's
+  // weighted input and per-block sums of squares; the consuming GEMM scales its accumulator rows by the rsqrt.  The
+  // norm before layer 0's input projection stays a launch.  f16 keeps the launch: the weighted input before the
+  // rsqrt could leave the f16 range.
+  const bool fuse_norm = act == DUO_BF16 && M > kGemvMax && M <= 256 && H % 128 == 0 && fused_norm_enabled();
   PROF_TRY(DUO_PROF_GATHER, launch_gather(ids_dev, M, e->w.embed.q, e->w.embed.s, e->gsize(H), H, c.vocab, e->x, st));
   for (int l = 0; l < c.layers; l++) {
     const duo_layer_view& L = e->lw[l];
     LayerState& S = e->ls[l];
     const bool full = e->is_full(l);
     const int wproj = full ? e->w_full : e->w_lin;
-    PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->x, M, H, L.in_norm, c.eps, 1, e->xn, act, st));
+    const bool in_fused = fuse_norm && l > 0;  // the previous layer's down projection wrote xn and the partials
+    if (!in_fused) PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->x, M, H, L.in_norm, c.eps, 1, e->xn, act, st));
     const void* xin = e->xn;
     {
       GemmEpiArgs ep;
@@ -236,6 +267,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.c = e->y;
       ep.c_dtype = act;
       ep.ldc = wproj;
+      if (in_fused) set_row_norm(ep, e->nrm_part[1], H, c.eps);
       PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, xin, M, H, L.proj, e->p_proj[l], wproj, ep, st));
     }
     int out_k;
@@ -297,10 +329,11 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.c = e->x;
       ep.c_dtype = DUO_F32;
       ep.ldc = H;
+      if (fuse_norm) set_norm_out(ep, L.post_norm, e->xn, e->nrm_part[0]);
       PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->o, M, out_k, L.out, e->p_out[l], H, ep, st));
     }
     DUO_TRY(capture_rows(e, DUO_CAP_RESID_ATTN, l, e->x, DUO_F32, M, H, st));
-    PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->x, M, H, L.post_norm, c.eps, 1, e->xn, act, st));
+    if (!fuse_norm) PROF_TRY(DUO_PROF_RMSNORM, launch_rmsnorm(e->x, M, H, L.post_norm, c.eps, 1, e->xn, act, st));
     PushTable pt{S.push_neuron, S.push_mode, S.push_vals, S.push_count, e->rows};
     if (M > kGemvMax && act != DUO_F32) {
       GemmEpiArgs ep;
@@ -313,6 +346,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.row_base = row_base;
       ep.push = pt;
       ep.b_const = true;  // weight packs are written once, at creation
+      if (fuse_norm) set_row_norm(ep, e->nrm_part[0], H, c.eps);
       PROF_TRY(DUO_PROF_GEMM, launch_gemm_tc(e->xn, M, H, e->p_gu[l].w, 2 * c.inter, act, ep, st));
     } else {
       GemmEpiArgs ep;
@@ -333,6 +367,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.vec = (vec_layer == l) ? e->vec : nullptr;
       ep.t = T;
       ep.row_base = row_base;
+      if (fuse_norm && l + 1 < c.layers && l != e->stop_after) set_norm_out(ep, e->lw[l + 1].in_norm, e->xn, e->nrm_part[1]);
       PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, e->a, M, c.inter, L.down, e->p_down[l], H, ep, st));
     }
     DUO_TRY(capture_rows(e, DUO_CAP_RESID, l, e->x, DUO_F32, M, H, st));
@@ -488,6 +523,10 @@ extern "C" int duo_engine_alloc(duo_engine* e, int rows, int max_len, int max_to
   void* p;
   DUO_TRY(A(&p, Mx * c.hidden * 4)); e->x = (float*)p;
   DUO_TRY(A(&e->xn, Mx * c.hidden * as));
+  for (auto& np : e->nrm_part) {
+    DUO_TRY(A(&p, (size_t)256 * (c.hidden / 128 + 1) * 4));
+    np = (float*)p;
+  }
   DUO_TRY(A(&e->y, Mx * e->wmax * as));
   DUO_TRY(A(&e->qkv, Mx * e->conv_dim * as));
   DUO_TRY(A(&p, Mx * c.hv * 4)); e->g = (float*)p;

@@ -442,6 +442,7 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dty
   DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_tc: operands must be bf16 or f16");
   // decode-sized row counts: the weights-on-M kernel (row groups x weight blocks x K slices)
   if (m <= 256 && ep.epi != EPI_ARGMAX) return launch_gemm_dec(a, m, k, b, n, ab_dtype, ep, st);
+  DUO_CHECK_ARG(!ep.nrm_out && !ep.row_part, "gemm_tc: the fused norm is a decode-GEMM epilogue (m <= 256)");
   const int sms = sm_count();
   const long tiles_m = cdiv(m, TC_BM);
   // the widest N tile that still gives every SM work (SwiGLU: gate / up interleaved per 64 rows, tiles >= 128)

@@ -197,6 +197,19 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       for (int i = 0; i < 32; i++) r[j][i] = 0u;
   }
   auto acc = [&](int c) { return __uint_as_float(r[c >> 5][c & 31]); };  // accumulator column c_lo + c
+  // fused RMSNorm of the activation rows (consumer side): rrs[c] = rsqrt(mean x^2 + eps) of row m0 + c
+  __shared__ float rrs[NB];
+  if (ep.row_part) {
+    for (int c = threadIdx.x; c < NB; c += DTHREADS) {
+      const int m = m0 + c;
+      float sum = 0.f;
+      if (m < M)
+        for (int b = 0; b < ep.row_blocks; b++) sum += ep.row_part[(long)m * ep.row_blocks + b];
+      rrs[c] = rsqrtf(sum / (float)ep.row_d + ep.row_eps);
+    }
+    __syncthreads();
+  }
+  auto rr = [&](int c) { return ep.row_part ? rrs[c] : 1.f; };  // factor of accumulator column (row) c
 
   if (direct) {
     // no K split, store or SwiGLU: the output tile is assembled in shared memory and leaves by one TMA store
@@ -206,7 +219,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       // instruction cache) forms 4 outputs per step into the [NB][64] 16-bit tile that follows the partial
       const float cs = ep.colscale ? ep.colscale[n0 + nl] : 1.f;
 #pragma unroll
-      for (int c = 0; c < CW; c++) part[(c_lo + c) * DP + nl] = acc(c) * cs;
+      for (int c = 0; c < CW; c++) part[(c_lo + c) * DP + nl] = acc(c) * cs * rr(c_lo + c);
       __syncthreads();
       uint8_t* tile = smem + C::OUT_OFF;
 #pragma unroll 1
@@ -236,15 +249,15 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       if (ep.c_dtype == DUO_F32) {
         float* o = reinterpret_cast<float*>(smem);
 #pragma unroll
-        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = acc(c) * cs;
+        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = acc(c) * cs * rr(c_lo + c);
       } else if (ep.c_dtype == DUO_F16) {
         __half* o = reinterpret_cast<__half*>(smem);
 #pragma unroll
-        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = cvt16<__half>(acc(c) * cs);
+        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = cvt16<__half>(acc(c) * cs * rr(c_lo + c));
       } else {
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(smem);
 #pragma unroll
-        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = cvt16<__nv_bfloat16>(acc(c) * cs);
+        for (int c = 0; c < CW; c++) o[(c_lo + c) * DBM + nl] = cvt16<__nv_bfloat16>(acc(c) * cs * rr(c_lo + c));
       }
     }
     tc::fence_proxy_async();
@@ -326,7 +339,9 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         for (int i = 0; i < RB; i++) {
           if (cr[i] < 0) break;
           const int m = m0 + cr[i];
-          const float gv[4] = {g[i].x, g[i].y, g[i].z, g[i].w}, uv[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+          const float f = rr(cr[i]);
+          const float gv[4] = {g[i].x * f, g[i].y * f, g[i].z * f, g[i].w * f};
+          const float uv[4] = {u[i].x * f, u[i].y * f, u[i].z * f, u[i].w * f};
           const int rw = ep.row_base + m / ep.t;
           float o[4];
 #pragma unroll
@@ -354,19 +369,21 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         for (int i = 0; i < RB; i++) {
           if (cr[i] < 0) break;
           const int m = m0 + cr[i];
-          float x[4] = {a[i].x * csv[0], a[i].y * csv[1], a[i].z * csv[2], a[i].w * csv[3]};
+          const float f = EPI == EPI_ADD_F32 ? 1.f : rr(cr[i]);
+          float x[4] = {a[i].x * csv[0] * f, a[i].y * csv[1] * f, a[i].z * csv[2] * f, a[i].w * csv[3] * f};
           const long off = (long)m * ep.ldc + n;
           const bool full4 = al && n + 4 <= N;
           if (EPI == EPI_ADD_F32) {
             float* X = static_cast<float*>(ep.c) + off;
             const float* vr = ep.vec ? ep.vec + (long)(ep.row_base + m / ep.t) * ep.ldc + n : nullptr;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);  // the new residual values (for the fused norm)
             if (pre_x) {  // one batch: i is the preload slot of this row
-              float4 o = xold[i];
+              o = xold[i];
               o.x += x[0]; o.y += x[1]; o.z += x[2]; o.w += x[3];
               if (ep.vec) { o.x += vold[i].x; o.y += vold[i].y; o.z += vold[i].z; o.w += vold[i].w; }
               *reinterpret_cast<float4*>(X) = o;
             } else if (full4) {
-              float4 o = *reinterpret_cast<float4*>(X);
+              o = *reinterpret_cast<float4*>(X);
               o.x += x[0]; o.y += x[1]; o.z += x[2]; o.w += x[3];
               if (vr) {
                 const float4 v4 = *reinterpret_cast<const float4*>(vr);
@@ -375,6 +392,21 @@ __global__ void __launch_bounds__(DTHREADS, 1)
               *reinterpret_cast<float4*>(X) = o;
             } else {
               for (int c = 0; c < 4 && n + c < N; c++) X[c] += x[c] + (vr ? vr[c] : 0.f);
+            }
+            if (ep.nrm_out) {  // the next RMSNorm's input (host: n % 128 == 0, aligned, so every lane is in range)
+              const float4 w4 = *reinterpret_cast<const float4*>(ep.nrm_w + n);
+              const float y[4] = {o.x * (1.f + w4.x), o.y * (1.f + w4.y), o.z * (1.f + w4.z), o.w * (1.f + w4.w)};
+              uint2 u;
+              if (F16) {
+                const __half2 lo = __floats2half2_rn(y[0], y[1]), hi = __floats2half2_rn(y[2], y[3]);
+                u = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+              } else {
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(y[0], y[1]), hi = __floats2bfloat162_rn(y[2], y[3]);
+                u = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+              }
+              *reinterpret_cast<uint2*>(static_cast<uint8_t*>(ep.nrm_out) + off * 2) = u;
+              const float ss = warp_sum(o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w);
+              if (lane == 0) ep.nrm_part[(long)m * gridDim.x + blockIdx.x] = ss;
             }
           } else if (ep.c_dtype == DUO_F32) {
             float* Cp = static_cast<float*>(ep.c) + off;
@@ -518,6 +550,16 @@ int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dt
     DUO_CHECK_ARG(ep.c_dtype == ab_dtype, "gemm_dec: SwiGLU output is 16-bit");
   }
   if (ep.epi == EPI_ADD_F32) DUO_CHECK_ARG(ep.c_dtype == DUO_F32, "gemm_dec: the residual add is into f32");
+  if (ep.nrm_out) {
+    const bool al = ((reinterpret_cast<uintptr_t>(ep.nrm_out) | reinterpret_cast<uintptr_t>(ep.c) |
+                      reinterpret_cast<uintptr_t>(ep.nrm_w)) & 15) == 0 && ep.ldc % 8 == 0 &&
+                    (ep.vec == nullptr || (reinterpret_cast<uintptr_t>(ep.vec) & 15) == 0);
+    DUO_CHECK_ARG(ep.epi == EPI_ADD_F32 && n % DBM == 0 && al && ep.nrm_w && ep.nrm_part,
+                  "gemm_dec: the fused norm needs the residual add, n a multiple of 128 and 16-byte aligned rows");
+  }
+  if (ep.row_part)
+    DUO_CHECK_ARG((ep.epi == EPI_STORE || ep.epi == EPI_SWIGLU) && ep.row_blocks > 0 && ep.row_d > 0,
+                  "gemm_dec: row factors apply to the store and SwiGLU epilogues");
   const int num_k = k / DBK;
   DecPlan p;
   if (m > 64) plan_dec<128>(m, n, num_k, p);

@@ -50,6 +50,17 @@ struct GemmEpiArgs {
   int32_t* idx = nullptr;       // ARGMAX: column of each partial maximum (c holds the f32 maxima)
   bool b_const = false;         // B is not written by the kernel launched just before (weight packs): its first
                                 // tiles may be fetched before the programmatic-launch wait
+  // RMSNorm fused across two decode GEMMs (launch_gemm_dec only; n a multiple of 128).  The residual add also
+  // writes the next norm's input scaled by its weight, nrm_out[m, n] = x_new[m, n] * (1 + nrm_w[n]) in the operand
+  // dtype (row stride ldc), and each CTA's sum of x_new^2 over its 128 columns to nrm_part[m * (n / 128) + block];
+  // the consuming GEMM multiplies the accumulator of activation row m by
+  // rsqrt(sum_b row_part[m * row_blocks + b] / row_d + row_eps), summed in block order (deterministic).
+  const float* nrm_w = nullptr;
+  void* nrm_out = nullptr;
+  float* nrm_part = nullptr;
+  const float* row_part = nullptr;
+  int row_blocks = 0, row_d = 0;
+  float row_eps = 0.f;
 };
 
 // decode-sized tcgen05 GEMM (m <= 256 rows; weights on the MMA's M side, grid = weight blocks x row groups x K
