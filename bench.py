@@ -445,9 +445,10 @@ def op_gemv(m, n, k, group=128):
 
 
 def op_gemm_decode(m=256, iters=8):
-    """The forward's projection shapes at m decode rows with int8-valued weights and the per-row scale in the
-    epilogue, as the engine runs them, each launch reading its own weight copy from HBM; cuBLAS (bf16, no scale, no
-    SwiGLU; for the residual add an f32 matmul plus the add) beside each."""
+    """The forward's projection shapes at m decode rows as the engine runs them: the int8 weights (one scale per row)
+    streamed and converted on chip (`ms`, bytes = the int8 weights + the activations), the same GEMM on the 16-bit
+    pack of those weights (`pack_ms`), and cuBLAS on the 16-bit weights (bf16, no scale, no SwiGLU; for the residual
+    add an f32 matmul plus the add; `cublas_ms`); each launch reads its own weight copy from HBM."""
     import torch
     from duo import ops
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -455,24 +456,31 @@ def op_gemm_decode(m=256, iters=8):
     for n, k, epi in [(8224, 1024, "store"), (5120, 1024, "store"), (7168, 1024, "swiglu"), (1024, 2048, "add"),
                       (1024, 3584, "add")]:
         a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
-        ws = [torch.randint(-127, 128, (n, k), device="cuda", generator=g).to(torch.bfloat16) for _ in range(iters)]
+        qs = [torch.randint(-127, 128, (n, k), device="cuda", generator=g, dtype=torch.int8) for _ in range(iters)]
+        ws = [q.to(torch.bfloat16) for q in qs]
         cs = torch.rand(n, device="cuda", generator=g) * 1e-3 + 1e-4
-        it, it2 = iter(range(1 << 30)), iter(range(1 << 30))
+        s = cs[:, None].contiguous()
+        it, it2, it3 = iter(range(1 << 30)), iter(range(1 << 30)), iter(range(1 << 30))
         if epi == "add":
             c = torch.zeros(m, n, device="cuda", dtype=torch.float32)
-            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], col_scale=cs, out=c, accumulate=True)
+            run = lambda: ops.q8_gemm(a, qs[next(it3) % iters], s, y=c, accumulate=True)
+            pack = lambda: ops.gemm_bf16(a, ws[next(it) % iters], col_scale=cs, out=c, accumulate=True)
             ref = lambda: c.add_(torch.matmul(a, ws[next(it2) % iters].T).float())
         elif epi == "swiglu":
-            run = lambda: ops.gemm_swiglu(a, ws[next(it) % iters], col_scale=cs)
+            o = torch.empty(m, n // 2, device="cuda", dtype=torch.bfloat16)
+            run = lambda: ops.q8_gemm(a, qs[next(it3) % iters], s, y=o, swiglu=True)
+            pack = lambda: ops.gemm_swiglu(a, ws[next(it) % iters], col_scale=cs)
             ref = lambda: torch.matmul(a, ws[next(it2) % iters].T)
         else:
             c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
-            run = lambda: ops.gemm_bf16(a, ws[next(it) % iters], col_scale=cs, out=c)
+            run = lambda: ops.q8_gemm(a, qs[next(it3) % iters], s, y=c)
+            pack = lambda: ops.gemm_bf16(a, ws[next(it) % iters], col_scale=cs, out=c)
             ref = lambda: torch.matmul(a, ws[next(it2) % iters].T, out=c)
-        ms, ms_ref = op_timed(run, iters), op_timed(ref, iters)
-        out.append(op_report("gemm_decode", [m, n, k], ms, bytes_=n * k * 2 + m * k * 2,
-                             extra={"epilogue": epi, "cublas_ms": round(ms_ref, 5)}))
-        del ws
+        ms, ms_pack, ms_ref = op_timed(run, iters), op_timed(pack, iters), op_timed(ref, iters)
+        out.append(op_report("gemm_decode", [m, n, k], ms, bytes_=n * k + m * k * 2,
+                             extra={"epilogue": epi, "weights": "int8", "pack_ms": round(ms_pack, 5),
+                                    "cublas_ms": round(ms_ref, 5)}))
+        del ws, qs
     return out
 
 

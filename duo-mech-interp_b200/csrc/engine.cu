@@ -173,8 +173,19 @@ int check_engine(duo_engine* e, bool need_weights, bool need_state) {
   return DUO_OK;
 }
 
-// y[m, n] (+)= x[m, k] . W^T through the GEMV (m <= 8, int8 weights), the f32 GEMM (f32 engine) or the tensor-core
-// GEMM on the bf16 pack.
+// Decode projections on the int8 weights converted on chip (DUO_DEC_Q8=1) instead of the 16-bit pack.  Off by
+// default: at 256 rows the conversion sits in the MMA's critical path and the pack is faster (8224 x 1024:
+// 12.3 us on the pack, 14.8 us converting; 32 rows: 8.1 against 9.1 us).
+bool dec_q8_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("DUO_DEC_Q8");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
+// y[m, n] (+)= x[m, k] . W^T through the GEMV (m <= 8, int8 weights), the f32 GEMM (f32 engine), the decode GEMM
+// streaming the int8 weights (m <= 256) or the tensor-core GEMM on the 16-bit pack.
 int project(duo_engine* e, const void* xin, int m, int k, const duo_q8_view& wq, const Pack& pk, int n,
             const GemmEpiArgs& ep, cudaStream_t st) {
   const int grp = e->gsize(k);
@@ -186,6 +197,12 @@ int project(duo_engine* e, const void* xin, int m, int k, const duo_q8_view& wq,
     return DUO_OK;
   }
   if (e->act == DUO_F32) return launch_gemm_f32_q8(static_cast<const float*>(xin), m, k, wq.q, wq.s, grp, n, ep, st);
+  if (m <= 256 && dec_q8_enabled()) {
+    GemmEpiArgs ep2 = ep;
+    ep2.colscale = grp == k ? wq.s : nullptr;  // one scale per row: the epilogue's column scale
+    ep2.b_const = true;
+    return launch_gemm_dec_q8(xin, m, k, wq.q, wq.s, grp, 0, n, e->act, ep2, st);
+  }
   GemmEpiArgs ep2 = ep;
   ep2.colscale = pk.colscale;
   ep2.b_const = true;  // packed once at creation, before any forward
@@ -347,7 +364,15 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.push = pt;
       ep.b_const = true;  // weight packs are written once, at creation
       if (fuse_norm) set_row_norm(ep, e->nrm_part[0], H, c.eps);
-      PROF_TRY(DUO_PROF_GEMM, launch_gemm_tc(e->xn, M, H, e->p_gu[l].w, 2 * c.inter, act, ep, st));
+      if (M <= 256 && dec_q8_enabled()) {
+        // int8 gate / up rows in their own order: the kernel reads them through the pack's interleave
+        const int grp = e->gsize(H);
+        ep.colscale = grp == H ? L.gu.s : nullptr;
+        ep.cs_inter = c.inter;
+        PROF_TRY(DUO_PROF_GEMM, launch_gemm_dec_q8(e->xn, M, H, L.gu.q, L.gu.s, grp, c.inter, 2 * c.inter, act, ep, st));
+      } else {
+        PROF_TRY(DUO_PROF_GEMM, launch_gemm_tc(e->xn, M, H, e->p_gu[l].w, 2 * c.inter, act, ep, st));
+      }
     } else {
       GemmEpiArgs ep;
       ep.epi = EPI_STORE;

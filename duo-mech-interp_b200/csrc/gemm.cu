@@ -553,6 +553,28 @@ extern "C" int duo_gemm_bf16(const void* a, int m, int k, const void* b, int n, 
   return launch_gemm_tc(a, m, k, b, n, DUO_BF16, ep, as_stream(stream));
 }
 
+extern "C" int duo_q8_gemm(const void* x, int x_dtype, int m, int k, const int8_t* q, const float* s, int group,
+                           int n, int swiglu, void* y, int y_dtype, int ldy, int accumulate, duo_stream stream) {
+  DUO_CHECK_ARG(m >= 0 && m <= 256 && n >= 0 && k > 0, "q8_gemm: 0 <= m <= 256 rows, n >= 0, k > 0");
+  DUO_CHECK_ARG(x_dtype == DUO_BF16 || x_dtype == DUO_F16, "q8_gemm: x must be bf16 or f16");
+  DUO_CHECK_ARG(k % 64 == 0 && group > 0 && group % 64 == 0 && k % group == 0,
+                "q8_gemm: k and the group size multiples of 64, the group dividing k");
+  DUO_CHECK_ARG(valid_act(y_dtype), "q8_gemm: y dtype must be f32, bf16 or f16");
+  DUO_CHECK_ARG(m == 0 || n == 0 || (x && q && s && y), "q8_gemm: null pointer");
+  DUO_CHECK_ARG(!accumulate || y_dtype == DUO_F32, "q8_gemm: accumulate needs an f32 y");
+  DUO_CHECK_ARG(!swiglu || (n % 128 == 0 && y_dtype == x_dtype && !accumulate),
+                "q8_gemm: SwiGLU needs n a multiple of 128 and y in x's dtype");
+  DUO_CHECK_ARG(ldy >= (swiglu ? n / 2 : n), "q8_gemm: ldy too small");
+  GemmEpiArgs ep;
+  ep.epi = swiglu ? EPI_SWIGLU : accumulate ? EPI_ADD_F32 : EPI_STORE;
+  ep.c = y;
+  ep.c_dtype = y_dtype;
+  ep.ldc = ldy;
+  if (group == k) ep.colscale = s;  // one scale per row: the epilogue's column scale
+  if (swiglu) ep.cs_inter = n / 2;
+  return launch_gemm_dec_q8(x, m, k, q, s, group, swiglu ? n / 2 : 0, n, x_dtype, ep, as_stream(stream));
+}
+
 extern "C" int duo_gemm_swiglu(const void* a, int m, int k, const void* b, int inter, int ab_dtype,
                                const float* col_scale, void* out, int ldo, const int32_t* push_neurons,
                                const int32_t* push_modes, const float* push_vals, int push_count, int push_rows, int t,

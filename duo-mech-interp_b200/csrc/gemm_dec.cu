@@ -14,6 +14,13 @@
 // coalesced along the output row: store, SwiGLU (+ pushes; gate / up packs interleaved per 64 rows) or
 // X += acc * colscale (+ vec).
 //
+// int8 weights (Q8).  The weight tile can also arrive as the int8 matrix itself (half the bytes of the 16-bit pack):
+// TMA brings 128 rows x 64 int8 per stage, four converter warps turn it into the 16-bit tile of the MMA's A operand
+// (the 128-byte swizzled K-major layout TMA would have written) in one of two converted slots, and the MMA reads it
+// from there.  With group scales (G < K) the converted value is 16-bit(f32(q) * s), the exact value of the 16-bit
+// pack; with one scale per row it is q itself (exact) and the scale is the epilogue's colscale, as for the pack.  So
+// both forms feed the tensor core identical operands and give identical results.
+//
 // The arithmetic is the reference's matmul (engine/kernels.js:97-151): f32 accumulation of products of the 16-bit
 // operands; the per-row int8 scale (colscale) multiplies the reduced sum.
 #include <cooperative_groups.h>
@@ -31,30 +38,59 @@ namespace duo {
 namespace {
 
 constexpr int DBM = 128, DBK = 64, DTHREADS = 256, DP = DBM + 4;  // DP: partial-tile row pitch (floats)
+constexpr int kQ8Groups = 8;  // group scales of one CTA's K slice held in shared memory (per weight row)
 
-template <int NB> struct DCfg {
-  static constexpr int W_BYTES = DBM * DBK * 2;
+// Shared memory: [16-bit weight tiles: one per stage, or (Q8) CV converted slots | X tiles | (Q8) int8 weight tiles |
+// (Q8) group scales | barriers].  A stage is what one TMA transaction brings: the weight tile (16-bit or int8) and the
+// X tile.
+template <int NB, bool Q8> struct DCfg {
+  static constexpr int W_BYTES = DBM * DBK * 2;         // 16-bit weight tile (the MMA's A operand)
+  static constexpr int RAW_BYTES = Q8 ? DBM * DBK : 0;  // int8 weight tile as loaded
   static constexpr int X_BYTES = NB * DBK * 2;
-  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
-  static constexpr int RING = STAGES * STAGE_BYTES;
-  static constexpr int SMEM = 1024 + RING + 256;
+  static constexpr int CV = Q8 ? 3 : 0;                 // converted slots
+  static constexpr int CVN = Q8 ? CV : 1;               // CV as a divisor
+  static constexpr int SCALE_BYTES = Q8 ? DBM * kQ8Groups * 4 : 0;
+  static constexpr int STAGE_BYTES = (Q8 ? RAW_BYTES : W_BYTES) + X_BYTES;
+  static constexpr int BUDGET = Q8 ? 221 * 1024 : 200 * 1024;
+  static constexpr int STAGES = (BUDGET - CV * W_BYTES - SCALE_BYTES) / STAGE_BYTES;
+  static constexpr int RING = CV * W_BYTES + STAGES * STAGE_BYTES;
+  static constexpr int BARS = (2 * STAGES + 2 * CV + 1) * 8 + 8;
+  static constexpr int SMEM = 1024 + RING + SCALE_BYTES + BARS;
   static constexpr int OUT_OFF = (NB * DP * 4 + 1023) / 1024 * 1024;  // SwiGLU output tile, after the partial
   static_assert(OUT_OFF + NB * 64 * 2 <= RING, "the partial and SwiGLU tiles must fit in the ring");
   static_assert(NB * DBM * 4 <= RING, "the f32 output tile must fit in the ring");
-  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(SMEM + NB * 4 <= 227 * 1024, "shared memory (with the static row factors)");
 };
+
+// int8 weight operand (Q8 kernels)
+struct Q8Args {
+  const float* s = nullptr;  // scales [n][k / group], rows in the int8 matrix's order
+  int group = 0;             // group size, a multiple of 64 (= k: one scale per row, applied as the colscale)
+  int ngroups = 0;           // k / group
+  int inter = 0;             // > 0: SwiGLU weights [gate (inter rows) | up (inter rows)], block b = gate rows
+                             // 64 b .. 64 b + 63 then up rows inter + 64 b .., the 16-bit pack's interleave
+  int apply = 0;             // group scales multiplied into the converted operand (group < k)
+};
+
+template <bool F16> __device__ __forceinline__ uint32_t pack2_16(float a, float b) {
+  if (F16) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 
 template <typename T> __device__ __forceinline__ T cvt16(float v);
 template <> __device__ __forceinline__ __nv_bfloat16 cvt16<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <> __device__ __forceinline__ __half cvt16<__half>(float v) { return __float2half_rn(v); }
 
-template <int NB, int EPI, bool F16>
+template <int NB, int EPI, bool F16, bool Q8>
 __global__ void __launch_bounds__(DTHREADS, 1)
     gemm_dec_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x,
                     const __grid_constant__ CUtensorMap tma_c, int M, int N, int K, int kper, int direct,
-                    GemmEpiArgs ep, unsigned* fault) {
-  using C = DCfg<NB>;
+                    GemmEpiArgs ep, Q8Args qa, unsigned* fault) {
+  using C = DCfg<NB, Q8>;
   constexpr int CW = NB / 2;  // accumulator columns (X rows) drained per warp
   if (gridDim.z == 1 && tc::fault_pending(fault)) {  // an earlier kernel gave up a wait (no cluster when z == 1)
     pdl_wait();
@@ -63,11 +99,15 @@ __global__ void __launch_bounds__(DTHREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sw = smem;
-  uint8_t* sx = smem + C::STAGES * C::W_BYTES;
+  uint8_t* sx = smem + (Q8 ? C::CV : C::STAGES) * C::W_BYTES;
+  uint8_t* sraw = sx + C::STAGES * C::X_BYTES;                    // Q8: int8 weight tiles
+  float* scl = reinterpret_cast<float*>(smem + C::RING);          // Q8: group scales [DBM rows][kQ8Groups]
   float* part = reinterpret_cast<float*>(smem);  // epilogue tiles reuse the ring once every MMA has completed
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING + C::SCALE_BYTES);
   uint64_t* empty = full + C::STAGES;
-  uint64_t* tmem_full = empty + C::STAGES;
+  uint64_t* cfull = empty + C::STAGES;  // Q8: converted slot written (6 converter warps)
+  uint64_t* cempty = cfull + C::CV;     // Q8: converted slot read by the MMAs
+  uint64_t* tmem_full = cempty + C::CV;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -80,6 +120,10 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     for (int s = 0; s < C::STAGES; s++) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
+    }
+    for (int c = 0; c < C::CV; c++) {
+      tc::mbar_init(&cfull[c], 6);
+      tc::mbar_init(&cempty[c], 1);
     }
     tc::mbar_init(tmem_full, 1);
     tc::fence_mbar_init();
@@ -97,13 +141,31 @@ __global__ void __launch_bounds__(DTHREADS, 1)
   // so HBM latency is paid about once rather than once per ring turn.  Programmatic launch: constant weights are
   // requested while the preceding kernel finishes.
   const int pre = ep.b_const ? min(num_k, C::STAGES) : 0;
+  // the weight tile of K block kb into stage s (Q8 SwiGLU: the gate and up halves of the block, 64 rows each)
+  auto load_w = [&](int kb, int s, uint64_t* bar) {
+    const int kx = (kb0 + kb) * DBK;
+    if (!Q8) {
+      tc::tma_load_2d(sw + s * C::W_BYTES, &tma_w, kx, n0, bar);
+    } else if (qa.inter > 0) {
+      tc::tma_load_2d(sraw + s * C::RAW_BYTES, &tma_w, kx, blockIdx.x * 64, bar);
+      tc::tma_load_2d(sraw + s * C::RAW_BYTES + C::RAW_BYTES / 2, &tma_w, kx, qa.inter + blockIdx.x * 64, bar);
+    } else {
+      tc::tma_load_2d(sraw + s * C::RAW_BYTES, &tma_w, kx, n0, bar);
+    }
+  };
   auto request_w = [&](int from) {
     for (int kb = from; kb < num_k; kb++) {
       if (kb < pre) {
         tc::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
-        tc::tma_load_2d(sw + kb * C::W_BYTES, &tma_w, (kb0 + kb) * DBK, n0, &full[kb]);
+        load_w(kb, kb, &full[kb]);
       } else if (kb >= C::STAGES) {
-        tc::tma_prefetch_2d(&tma_w, (kb0 + kb) * DBK, n0);
+        const int kx = (kb0 + kb) * DBK;
+        if (Q8 && qa.inter > 0) {
+          tc::tma_prefetch_2d(&tma_w, kx, blockIdx.x * 64);
+          tc::tma_prefetch_2d(&tma_w, kx, qa.inter + blockIdx.x * 64);
+        } else {
+          tc::tma_prefetch_2d(&tma_w, kx, n0);
+        }
       }
     }
   };
@@ -150,7 +212,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         break;
       }
       tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-      tc::tma_load_2d(sw + s * C::W_BYTES, &tma_w, (kb0 + kb) * DBK, n0, &full[s]);
+      load_w(kb, s, &full[s]);
       tc::tma_load_2d(sx + s * C::X_BYTES, &tma_x, (kb0 + kb) * DBK, m0, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
@@ -159,19 +221,79 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     for (int kb = 0; kb < num_k; kb++) {
       const int s = kb % C::STAGES;
       const uint32_t ph = (kb / C::STAGES) & 1;
-      if (!tc::mbar_wait(&full[s], ph)) {
+      const int c = Q8 ? kb % C::CVN : 0;
+      if (!tc::mbar_wait(&full[s], ph) || (Q8 && !tc::mbar_wait(&cfull[c], (kb / C::CVN) & 1))) {
         atomicOr(fault, 2u);
         ok = false;
         break;
       }
       tc::fence_after_sync();
-      const uint64_t dw = tc::desc_add(dw0, s * C::W_BYTES), dx = tc::desc_add(dx0, s * C::X_BYTES);
+      const uint64_t dw = tc::desc_add(dw0, (Q8 ? c : s) * C::W_BYTES), dx = tc::desc_add(dx0, s * C::X_BYTES);
 #pragma unroll
       for (int k = 0; k < DBK / 16; k++)  // 16 k = 32 bytes along the swizzled rows
         tc::mma_bf16(tmem, tc::desc_add(dw, 32 * k), tc::desc_add(dx, 32 * k), idesc, (kb | k) != 0);
       tc::mma_commit(&empty[s]);
+      if (Q8) tc::mma_commit(&cempty[c]);
     }
     if (ok) tc::mma_commit(tmem_full);
+  } else if (Q8 && warp >= 2) {
+    // converters (warps 2..7): int8 stage s -> 16-bit converted slot c.  Thread ct takes 16-byte pieces ct + 192 i
+    // (row p / 4, quarter p % 4): a warp's loads cover 512 consecutive bytes and its stores the 8 chunk positions of
+    // 8 rows, so neither has bank conflicts.
+    constexpr int NCV = DTHREADS - 64;
+    const int ct = threadIdx.x - 64;
+    const int g0 = qa.apply ? kb0 * DBK / qa.group : 0;
+    if (qa.apply) {
+      for (int i = ct; i < DBM * kQ8Groups; i += NCV) {
+        const int r = i / kQ8Groups, g = g0 + i % kQ8Groups;
+        const int orow = qa.inter > 0 ? (r < 64 ? blockIdx.x * 64 + r : qa.inter + blockIdx.x * 64 + r - 64) : n0 + r;
+        scl[i] = (orow < N && g < qa.ngroups) ? qa.s[(long)orow * qa.ngroups + g] : 0.f;
+      }
+      tc::bar_sync(1, NCV);
+    }
+    for (int kb = 0; kb < num_k; kb++) {
+      const int s = kb % C::STAGES, c = kb % C::CVN;
+      if (!tc::mbar_wait(&full[s], (kb / C::STAGES) & 1) ||
+          (kb >= C::CV && !tc::mbar_wait(&cempty[c], ((kb / C::CVN) & 1) ^ 1))) {
+        if (lane == 0) atomicOr(fault, 2u);
+        break;
+      }
+      const uint8_t* raw = sraw + s * C::RAW_BYTES;
+      uint8_t* dst = sw + c * C::W_BYTES;
+      const int gi = qa.apply ? (kb0 + kb) * DBK / qa.group - g0 : 0;
+#pragma unroll
+      for (int i = 0; i < (DBM * 4 + NCV - 1) / NCV; i++) {
+        const int p = ct + NCV * i, r = p >> 2, qd = p & 3;
+        if (p >= DBM * 4) break;
+        const uint4 u = *reinterpret_cast<const uint4*>(raw + r * DBK + qd * 16);
+        float f[16];
+        i8x4_to_f32(u.x, f);
+        i8x4_to_f32(u.y, f + 4);
+        i8x4_to_f32(u.z, f + 8);
+        i8x4_to_f32(u.w, f + 12);
+        uint32_t w[8];
+        if (qa.apply) {
+          const float sc = scl[r * kQ8Groups + gi];
+#pragma unroll
+          for (int j = 0; j < 16; j++) f[j] *= sc;
+#pragma unroll
+          for (int j = 0; j < 8; j++) w[j] = pack2_16<F16>(f[2 * j], f[2 * j + 1]);
+        } else if (F16) {
+#pragma unroll
+          for (int j = 0; j < 8; j++) w[j] = pack2_16<true>(f[2 * j], f[2 * j + 1]);
+        } else {
+          // an int8 value has at most 8 significant bits: the upper half of its f32 pattern is its bf16 value
+#pragma unroll
+          for (int j = 0; j < 8; j++) w[j] = __byte_perm(__float_as_uint(f[2 * j]), __float_as_uint(f[2 * j + 1]), 0x7632);
+        }
+        uint8_t* row = dst + r * 128;
+        *reinterpret_cast<uint4*>(row + (((2 * qd) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(row + (((2 * qd + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      tc::fence_proxy_async();  // the generic-proxy stores become visible to the tensor core's reads
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&cfull[c]);
+    }
   }
 
   // Drain: warp w holds TMEM lane quarter q = w % 4 (weight rows nl = 32 q + lane) and accumulator columns
@@ -210,6 +332,12 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     __syncthreads();
   }
   auto rr = [&](int c) { return ep.row_part ? rrs[c] : 1.f; };  // factor of accumulator column (row) c
+  // colscale entry of SwiGLU weight row p (interleaved order), or of the int8 matrix's row behind it (cs_inter > 0)
+  auto cs_row = [&](int p) {
+    if (ep.cs_inter <= 0) return p;
+    const int j = p & 127;
+    return j < 64 ? (p >> 7) * 64 + j : ep.cs_inter + (p >> 7) * 64 + j - 64;
+  };
 
   if (direct) {
     // no K split, store or SwiGLU: the output tile is assembled in shared memory and leaves by one TMA store
@@ -217,7 +345,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       // weight rows 0..63 of the block are gate rows, 64..127 the matching up rows (interleave_gate_up order): the
       // scaled accumulators go to part[c][nl], then a rolled sweep (small code: each CTA runs it once, from a cold
       // instruction cache) forms 4 outputs per step into the [NB][64] 16-bit tile that follows the partial
-      const float cs = ep.colscale ? ep.colscale[n0 + nl] : 1.f;
+      const float cs = ep.colscale ? ep.colscale[cs_row(n0 + nl)] : 1.f;
 #pragma unroll
       for (int c = 0; c < CW; c++) part[(c_lo + c) * DP + nl] = acc(c) * cs * rr(c_lo + c);
       __syncthreads();
@@ -324,8 +452,8 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       float cg_[4] = {1.f, 1.f, 1.f, 1.f}, cu_[4] = {1.f, 1.f, 1.f, 1.f};
       if (ep.colscale) {
         for (int i = 0; i < 4; i++) {
-          cg_[i] = ep.colscale[n0 + j4 + i];
-          cu_[i] = ep.colscale[n0 + 64 + j4 + i];
+          cg_[i] = ep.colscale[cs_row(n0 + j4 + i)];
+          cu_[i] = ep.colscale[cs_row(n0 + 64 + j4 + i)];
         }
       }
       for (int cb = r_lo + warp * 2 + (lane >> 4); cb < r_hi; cb += 16 * RB) {
@@ -435,11 +563,11 @@ __global__ void __launch_bounds__(DTHREADS, 1)
   }
 }
 
-template <int NB, int EPI, bool F16>
+template <int NB, int EPI, bool F16, bool Q8>
 int run_dec(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tcm, int m, int n, int k, int groups,
-            int ks, int kper, int direct, const GemmEpiArgs& ep, cudaStream_t st) {
-  using C = DCfg<NB>;
-  auto kern = gemm_dec_kernel<NB, EPI, F16>;
+            int ks, int kper, int direct, const GemmEpiArgs& ep, const Q8Args& qa, cudaStream_t st) {
+  using C = DCfg<NB, Q8>;
+  auto kern = gemm_dec_kernel<NB, EPI, F16, Q8>;
   DUO_TRY(ensure_smem_attr(kern, C::SMEM));
   unsigned* fault = tc_fault_ptr();
   if (!fault) return fail(DUO_ECUDA, "tensor-core fault word is not addressable");
@@ -464,19 +592,19 @@ int run_dec(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tcm
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  DUO_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tw, tx, tcm, m, n, k, kper, direct, ep, fault));
+  DUO_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tw, tx, tcm, m, n, k, kper, direct, ep, qa, fault));
   DUO_LAUNCH_CHECK("gemm_dec_kernel");
   return DUO_OK;
 }
 
-template <int NB, bool F16>
+template <int NB, bool F16, bool Q8>
 int dispatch_dec(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tcm, int m, int n, int k,
-                 int groups, int ks, int kper, int direct, const GemmEpiArgs& ep, cudaStream_t st) {
+                 int groups, int ks, int kper, int direct, const GemmEpiArgs& ep, const Q8Args& qa, cudaStream_t st) {
   if (ep.epi == EPI_SWIGLU)
-    return run_dec<NB, EPI_SWIGLU, F16>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, st);
+    return run_dec<NB, EPI_SWIGLU, F16, Q8>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, qa, st);
   if (ep.epi == EPI_ADD_F32)
-    return run_dec<NB, EPI_ADD_F32, F16>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, st);
-  return run_dec<NB, EPI_STORE, F16>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, st);
+    return run_dec<NB, EPI_ADD_F32, F16, Q8>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, qa, st);
+  return run_dec<NB, EPI_STORE, F16, Q8>(tw, tx, tcm, m, n, k, groups, ks, kper, direct, ep, qa, st);
 }
 
 // Clusters of ks CTAs of the kernel that can be resident at once (one CTA per SM; a cluster must fit in one GPC).
@@ -485,13 +613,13 @@ template <int NB> int max_clusters(int ks) {
   static int cache[9] = {};
   if (ks <= 1) return sm_count();
   if (cache[ks]) return cache[ks];
-  auto kern = gemm_dec_kernel<NB, EPI_STORE, false>;
+  auto kern = gemm_dec_kernel<NB, EPI_STORE, false, false>;
   int n = 0;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DCfg<NB>::SMEM) == cudaSuccess) {
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DCfg<NB, false>::SMEM) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1, 1, ks);
     cfg.blockDim = dim3(DTHREADS);
-    cfg.dynamicSmemBytes = DCfg<NB>::SMEM;
+    cfg.dynamicSmemBytes = DCfg<NB, false>::SMEM;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = 1;
@@ -516,17 +644,17 @@ struct DecPlan {
   int nb = 0, groups = 0, ks = 1, kper = 0;
   double cost = 0.0;
 };
-template <int NB> void plan_dec(int m, int n, int num_k, DecPlan& best) {
+template <int NB> void plan_dec(int m, int n, int num_k, bool q8, int max_kper, DecPlan& best) {
   const long sms = sm_count();
   const int groups = cdiv(m, NB);
   const long base = (long)cdiv(n, DBM) * groups;
   for (int want = 1; want <= std::min(8, num_k); want++) {
     const int kper = cdiv(num_k, want);
     const int ks = cdiv(num_k, kper);
-    if (ks != want) continue;  // the same split as a smaller want
+    if (ks != want || kper > max_kper) continue;  // the same split as a smaller want, or too long a slice
     const long slots = ks > 1 ? (long)max_clusters<NB>(ks) : sms;
     const long waves = (base + slots - 1) / slots;
-    const double ingest = (double)(DBM + NB) * kper * DBK * 2;
+    const double ingest = (double)(DBM * (q8 ? 1 : 2) + NB * 2) * kper * DBK;
     const double reduce = ks > 1 ? (double)NB * DBM * 4 * (ks - 1) / ks : 0.0;
     const double cost = (double)waves * (kWaveBytes + ingest + reduce);
     if (best.nb == 0 || cost < best.cost) {
@@ -535,10 +663,35 @@ template <int NB> void plan_dec(int m, int n, int num_k, DecPlan& best) {
   }
 }
 
-}  // namespace
+int make_tmap_u8(CUtensorMap* map, const int8_t* base, long rows, long cols, int box_rows, int box_cols) {
+  typedef CUresult (*Enc)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                          const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                          CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Enc enc = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (Enc) nullptr;
+    return reinterpret_cast<Enc>(p);
+  }();
+  if (!enc) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || cols % 16)
+    return fail(DUO_EINVAL, "tensor map: int8 base 16-byte aligned and rows a multiple of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DUO_ECUDA, "cuTensorMapEncodeTiled (int8) failed with code " + std::to_string((int)r));
+  return DUO_OK;
+}
 
-int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dtype, const GemmEpiArgs& ep,
-                    cudaStream_t st) {
+// shared host path: w is the 16-bit weight matrix, or (q8 != nullptr) the int8 matrix with its scales
+int launch_dec(const void* x, int m, int k, const void* w, const Q8Args* q8, int n, int ab_dtype,
+               const GemmEpiArgs& ep, cudaStream_t st) {
   if (m == 0 || n == 0) return DUO_OK;
   DUO_CHECK_ARG(m <= 256, "gemm_dec: at most 256 rows");
   DUO_CHECK_ARG(k % DBK == 0, "gemm_dec: k must be a multiple of 64");
@@ -560,10 +713,26 @@ int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dt
   if (ep.row_part)
     DUO_CHECK_ARG((ep.epi == EPI_STORE || ep.epi == EPI_SWIGLU) && ep.row_blocks > 0 && ep.row_d > 0,
                   "gemm_dec: row factors apply to the store and SwiGLU epilogues");
+  Q8Args qa;
+  int max_kper = 1 << 30;
+  if (q8) {
+    qa = *q8;
+    DUO_CHECK_ARG(qa.s && qa.group > 0 && k % qa.group == 0 && qa.group % DBK == 0,
+                  "q8 gemm: the group size must divide k and be a multiple of 64");
+    qa.ngroups = k / qa.group;
+    qa.apply = qa.group < k;
+    if (qa.apply) max_kper = (kQ8Groups - 1) * qa.group / DBK;  // a slice spans at most kQ8Groups groups
+    if (qa.inter > 0)
+      DUO_CHECK_ARG(ep.epi == EPI_SWIGLU && n == 2 * qa.inter && qa.inter % 64 == 0,
+                    "q8 gemm: the gate / up interleave is the SwiGLU epilogue's, n = 2 inter");
+    else
+      DUO_CHECK_ARG(ep.epi != EPI_SWIGLU, "q8 gemm: SwiGLU reads gate and up rows through the interleave");
+  }
   const int num_k = k / DBK;
   DecPlan p;
-  if (m > 64) plan_dec<128>(m, n, num_k, p);
-  plan_dec<64>(m, n, num_k, p);
+  if (m > 64) plan_dec<128>(m, n, num_k, q8 != nullptr, max_kper, p);
+  plan_dec<64>(m, n, num_k, q8 != nullptr, max_kper, p);
+  if (p.nb == 0) return fail(DUO_EINVAL, "q8 gemm: k too long for the group scales of one K split");
   // direct epilogue (TMA store of the finished tile): no K split, a store or SwiGLU, an output whose base and rows
   // are 16-byte aligned, and at least one row group of rows (the store box is never taller than the whole output)
   const int es = ep.c_dtype == DUO_F32 ? 4 : 2;
@@ -571,18 +740,41 @@ int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dt
   const int direct = p.ks == 1 && ep.epi != EPI_ADD_F32 && c_aligned && m >= p.nb;
   CUtensorMap tw, tx, tcm;
   std::memset(&tcm, 0, sizeof(tcm));
-  DUO_TRY(make_tmap_16(&tw, w, ab_dtype, n, k, k, DBM, DBK));
+  if (q8) DUO_TRY(make_tmap_u8(&tw, static_cast<const int8_t*>(w), n, k, qa.inter > 0 ? 64 : DBM, DBK));
+  else DUO_TRY(make_tmap_16(&tw, w, ab_dtype, n, k, k, DBM, DBK));
   DUO_TRY(make_tmap_16(&tx, x, ab_dtype, m, k, k, p.nb, DBK));
   if (direct) {
     const bool sw = ep.epi == EPI_SWIGLU;
     DUO_TRY(make_tmap_plain(&tcm, ep.c, ep.c_dtype, m, sw ? n / 2 : n, ep.ldc, p.nb, sw ? 64 : DBM));
   }
-  if (ab_dtype == DUO_F16) {
-    if (p.nb == 64) return dispatch_dec<64, true>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, st);
-    return dispatch_dec<128, true>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, st);
+  const bool f16 = ab_dtype == DUO_F16;
+#define DUO_DEC_DISPATCH(NB_, F16_, Q8_) \
+  return dispatch_dec<NB_, F16_, Q8_>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, qa, st)
+  if (q8) {
+    if (p.nb == 64) { if (f16) DUO_DEC_DISPATCH(64, true, true); DUO_DEC_DISPATCH(64, false, true); }
+    if (f16) DUO_DEC_DISPATCH(128, true, true);
+    DUO_DEC_DISPATCH(128, false, true);
   }
-  if (p.nb == 64) return dispatch_dec<64, false>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, st);
-  return dispatch_dec<128, false>(tw, tx, tcm, m, n, k, p.groups, p.ks, p.kper, direct, ep, st);
+  if (p.nb == 64) { if (f16) DUO_DEC_DISPATCH(64, true, false); DUO_DEC_DISPATCH(64, false, false); }
+  if (f16) DUO_DEC_DISPATCH(128, true, false);
+  DUO_DEC_DISPATCH(128, false, false);
+#undef DUO_DEC_DISPATCH
+}
+
+}  // namespace
+
+int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dtype, const GemmEpiArgs& ep,
+                    cudaStream_t st) {
+  return launch_dec(x, m, k, w, nullptr, n, ab_dtype, ep, st);
+}
+
+int launch_gemm_dec_q8(const void* x, int m, int k, const int8_t* wq, const float* ws, int group, int inter, int n,
+                       int ab_dtype, const GemmEpiArgs& ep, cudaStream_t st) {
+  Q8Args qa;
+  qa.s = ws;
+  qa.group = group;
+  qa.inter = inter;
+  return launch_dec(x, m, k, wq, &qa, n, ab_dtype, ep, st);
 }
 
 }  // namespace duo

@@ -61,12 +61,20 @@ struct GemmEpiArgs {
   const float* row_part = nullptr;
   int row_blocks = 0, row_d = 0;
   float row_eps = 0.f;
+  // SwiGLU on int8 weights in their own order [gate | up] (launch_gemm_dec_q8, inter = cs_inter): colscale holds one
+  // entry per int8 row, not per interleaved row
+  int cs_inter = 0;
 };
 
 // decode-sized tcgen05 GEMM (m <= 256 rows; weights on the MMA's M side, grid = weight blocks x row groups x K
 // slices, K split over a cluster where the SMs need it): y = x . w^T
 int launch_gemm_dec(const void* x, int m, int k, const void* w, int n, int ab_dtype, const GemmEpiArgs& ep,
                     cudaStream_t st);
+// the same kernel reading the int8 weights wq [n, k] (scales ws [n, k / group]; group a multiple of 64 dividing k,
+// = k for one scale per row, which the caller passes as ep.colscale) and converting them on chip; inter > 0: SwiGLU
+// with wq = [gate (inter rows) | up (inter rows)], n = 2 inter
+int launch_gemm_dec_q8(const void* x, int m, int k, const int8_t* wq, const float* ws, int group, int inter, int n,
+                       int ab_dtype, const GemmEpiArgs& ep, cudaStream_t st);
 
 // persistent tcgen05 GEMM over prepared tensor maps (A box 128 x 64, B box bn x 64; bn = 256)
 int launch_gemm_persist(const CUtensorMap& ta, const CUtensorMap& tb, int bn, int m, int n, int k, int ab_dtype,

@@ -48,6 +48,7 @@ SIGNATURES = {
     "duo_q8_gemv": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp]),
     "duo_q8_gather": (_i, [_vp, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "duo_gemm_bf16": (_i, [_vp, _i, _i, _vp, _i, _vp, _vp, _i, _i, _i, _vp]),
+    "duo_q8_gemm": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _i, _i, _i, _vp]),
     "duo_gemm_swiglu": (_i, [_vp, _i, _i, _vp, _i, _i, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "duo_rmsnorm": (_i, [_vp, _i, _i, _vp, _f, _i, _vp, _i, _vp]),
     "duo_gdn_conv_fwd": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),

@@ -69,6 +69,21 @@ def gemm_bf16(a, b, col_scale=None, out=None, out_dtype=torch.bfloat16, accumula
     return out
 
 
+def q8_gemm(x, q, s, y=None, out_dtype=None, accumulate=False, swiglu=False, stream=None):
+    """y[m, n] (+)= x[m, k] . dequant(q, s)^T for m <= 256 on the tensor cores, the int8 weights converted on chip
+    (engine/kernels.js:97-151); swiglu: q = [gate | up] rows, y = silu(gate) * up [m, n / 2] in x's dtype."""
+    _dev(x, q, s, y)
+    m, k = x.shape
+    n = q.shape[0]
+    g = k // s.shape[1]
+    if y is None:
+        y = torch.zeros(m, n // 2 if swiglu else n, dtype=x.dtype if swiglu else (out_dtype or x.dtype),
+                        device=x.device)
+    call("duo_q8_gemm", ptr(x), dtype_code(x.dtype), m, k, ptr(q), ptr(s), g, n, int(swiglu), ptr(y),
+         dtype_code(y.dtype), y.stride(0), int(accumulate), stream_ptr(stream))
+    return y
+
+
 def interleave_gate_up(gate, up):
     """[inter, k] gate and up weights -> the [2 inter, k] row order duo_gemm_swiglu reads (blocks of 64 rows:
     64 gate rows, then the matching 64 up rows)."""

@@ -101,6 +101,16 @@ int duo_gemm_swiglu(const void* a, int m, int k, const void* b, int inter, int a
                     void* out, int ldo, const int32_t* push_neurons, const int32_t* push_modes, const float* push_vals,
                     int push_count, int push_rows, int t, int row_base, duo_stream stream);
 
+/* y[m, n] (+)= x[m, k] . dequant(W)[n, k]^T for 1 <= m <= 256 rows on the tensor cores, streaming the int8 weights
+ * q [n, k] (scales s [n, k / group]) and converting them on chip: x bf16 or f16; y f32 (accumulate != 0 adds into
+ * it), bf16 or f16 with leading dim ldy.  group is a multiple of 64 that divides k (128: the reference format; k: one
+ * scale per row).  The operand the tensor core sees is dequant(W) rounded to x's dtype (exact for one scale per row,
+ * whose scale multiplies the f32 sum).  swiglu != 0: q holds [gate (n / 2 rows) | up (n / 2 rows)] and
+ * y[m, n / 2] = silu(gate) * up in x's dtype.  The decode path of `matmul(add)` on the int8 format,
+ * engine/kernels.js:97-151 (dispatched by model.js:382-392). */
+int duo_q8_gemm(const void* x, int x_dtype, int m, int k, const int8_t* q, const float* s, int group, int n,
+                int swiglu, void* y, int y_dtype, int ldy, int accumulate, duo_stream stream);
+
 /* y[m, :] = x[m, :] * rsqrt(mean(x^2) + eps) * (1 + w) (offset != 0) or * w.  x f32, y f32 / bf16.
  * Replaces `rmsnorm(offset)`, engine/kernels.js:226-246. */
 int duo_rmsnorm(const float* x, int m, int d, const float* w, float eps, int offset, void* y, int y_dtype,

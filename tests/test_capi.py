@@ -74,6 +74,19 @@ def test_projection_and_scan_arguments_are_checked_first(L):
     st = lib.duo_gemm_swiglu(sentinel, 4, 64, sentinel, 128, L.DUO_BF16, None, sentinel, 128, sentinel, sentinel,
                              sentinel, 1, 2, 1, 0, None)  # 4 rows of A, 2 rows in the push table
     assert st == L.DUO_EINVAL and b"push table" in lib.duo_last_error()
+    # int8 decode GEMM: at most 256 rows, the group a multiple of 64 dividing k, x 16-bit, SwiGLU n a multiple of 128
+    st = lib.duo_q8_gemm(sentinel, L.DUO_BF16, 300, 128, sentinel, sentinel, 128, 128, 0, sentinel, L.DUO_F32, 128, 0,
+                         None)
+    assert st == L.DUO_EINVAL and b"256" in lib.duo_last_error()
+    st = lib.duo_q8_gemm(sentinel, L.DUO_BF16, 4, 128, sentinel, sentinel, 32, 128, 0, sentinel, L.DUO_F32, 128, 0,
+                         None)
+    assert st == L.DUO_EINVAL and b"group" in lib.duo_last_error()
+    st = lib.duo_q8_gemm(sentinel, L.DUO_F32, 4, 128, sentinel, sentinel, 128, 128, 0, sentinel, L.DUO_F32, 128, 0,
+                         None)
+    assert st == L.DUO_EINVAL and b"bf16 or f16" in lib.duo_last_error()
+    st = lib.duo_q8_gemm(sentinel, L.DUO_BF16, 4, 128, sentinel, sentinel, 128, 192, 1, sentinel, L.DUO_BF16, 96, 0,
+                         None)
+    assert st == L.DUO_EINVAL and b"SwiGLU" in lib.duo_last_error()
     # the residual-add GEMM accumulates into f32 only
     st = lib.duo_gemm_bf16(sentinel, 4, 64, sentinel, 4, None, sentinel, L.DUO_BF16, 4, 1, None)
     assert st == L.DUO_EINVAL and b"f32" in lib.duo_last_error()

@@ -163,6 +163,58 @@ def test_gemm_swiglu(ops, m, inter, k, dt):
     assert ops.fault_status() == 0
 
 
+def _q8_operand(q, s, group, dt):
+    """The weight operand the tensor core sees and the factor on the f32 sum: 16-bit(f32(q) s) for group scales (the
+    16-bit pack's value), q itself with the row scale on the sum for one scale per row."""
+    k = q.shape[1]
+    if group == k:
+        return q.double(), s[:, 0].double()
+    return (q.float() * s.repeat_interleave(group, 1)).to(dt).double(), torch.ones(q.shape[0], dtype=torch.float64)
+
+
+@pytest.mark.parametrize("m,n,k,group,dt", [(9, 1000, 1024, 1024, torch.bfloat16), (40, 8224, 1024, 1024, torch.bfloat16),
+                                            (130, 1024, 3584, 128, torch.bfloat16), (256, 8224, 1024, 128, torch.bfloat16),
+                                            (256, 1024, 3584, 3584, torch.float16), (64, 384, 512, 64, torch.bfloat16)])
+def test_q8_gemm(ops, m, n, k, group, dt):
+    """int8 weights streamed into the decode GEMM and converted on chip (engine/kernels.js:97-151): store (f32 and
+    16-bit) and residual add, against a float64 product of the same operands (f32 accumulation bounds the error)."""
+    q = torch.randint(-127, 128, (n, k), generator=_seed(n), dtype=torch.int8)
+    s = torch.rand(n, k // group, generator=_seed(k)) * 1e-2 + 1e-3
+    x = torch.randn(m, k, generator=_seed(m)).to(dt)
+    wop, post = _q8_operand(q, s, group, dt)
+    ref = (x.double() @ wop.T) * post
+    qd, sd, xd = q.cuda(), s.cuda(), x.cuda()
+    y = ops.q8_gemm(xd, qd, sd, out_dtype=torch.float32)
+    assert rel_max(y, ref) < 1e-5 * max(1.0, k / 1024)
+    y16 = ops.q8_gemm(xd, qd, sd, out_dtype=dt)
+    assert rel_max(y16.float(), ref) < 8e-3
+    x0 = torch.randn(m, n, generator=_seed(2))
+    acc = ops.q8_gemm(xd, qd, sd, y=x0.clone().cuda(), accumulate=True)
+    assert rel_max(acc, x0.double() + ref) < 1e-5 * max(1.0, k / 1024)
+    if dt == torch.bfloat16 and group == k:  # the 16-bit pack of the same weights through the bf16 GEMM
+        yp = ops.gemm_bf16(xd, qd.to(torch.bfloat16), col_scale=sd[:, 0].contiguous(), out_dtype=torch.float32)
+        assert rel_max(y, yp) < 1e-5 * max(1.0, k / 1024)
+    assert ops.fault_status() == 0
+
+
+@pytest.mark.parametrize("m,inter,k,group,dt", [(37, 128, 256, 128, torch.bfloat16), (256, 3584, 1024, 1024, torch.bfloat16),
+                                                (100, 3584, 1024, 128, torch.float16), (200, 512, 256, 256, torch.bfloat16)])
+def test_q8_gemm_swiglu(ops, m, inter, k, group, dt):
+    """gate|up on int8 weights in their own row order [gate | up], read through the 16-bit pack's interleave, with
+    SwiGLU fused (kernels_qwen35.js:250-280): against float64 on the same operands (16-bit output rounding)."""
+    q = torch.randint(-127, 128, (2 * inter, k), generator=_seed(inter), dtype=torch.int8)
+    s = torch.rand(2 * inter, k // group, generator=_seed(k + 1)) * 1e-2 + 1e-3
+    x = torch.randn(m, k, generator=_seed(m + 3)).to(dt)
+    wop, post = _q8_operand(q, s, group, dt)
+    gu = (x.double() @ wop.T) * post
+    g, u = gu[:, :inter], gu[:, inter:]
+    ref = g / (1 + torch.exp(-g)) * u
+    out = ops.q8_gemm(x.cuda(), q.cuda(), s.cuda(), swiglu=True)
+    assert out.shape == (m, inter) and out.dtype == dt
+    assert rel_max(out.float(), ref) < 1e-2
+    assert ops.fault_status() == 0
+
+
 def test_rmsnorm(ops):
     x = torch.randn(7, 1024, generator=_seed(9)) * 3
     w = torch.randn(1024, generator=_seed(10)) * 0.1
