@@ -197,6 +197,45 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       }
     }
   }
+  // colscale entry of SwiGLU weight row p (interleaved order), or of the int8 matrix's row behind it (cs_inter > 0)
+  auto cs_row = [&](int p) {
+    if (ep.cs_inter <= 0) return p;
+    const int j = p & 127;
+    return j < 64 ? (p >> 7) * 64 + j : ep.cs_inter + (p >> 7) * 64 + j - 64;
+  };
+  // The column scales of this thread's epilogue columns, loaded now so that their latency hides under the mainloop:
+  // direct path weight row n0 + (warp % 4) 32 + lane; reduce path rows n4 .. n4 + 3, or for SwiGLU the gate and up
+  // rows of output columns 4 (lane % 16) .. + 3.
+  float cs_d = 1.f;
+  float csv[4] = {1.f, 1.f, 1.f, 1.f}, cu_[4] = {1.f, 1.f, 1.f, 1.f};
+  if (ep.colscale) {
+    if (direct) {
+      const int nd = n0 + (warp & 3) * 32 + lane;
+      cs_d = EPI == EPI_SWIGLU ? ep.colscale[cs_row(nd)] : (nd < N ? ep.colscale[nd] : 0.f);
+    } else if (EPI == EPI_SWIGLU) {
+      const int j4 = (lane & 15) * 4;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        csv[i] = ep.colscale[cs_row(n0 + j4 + i)];
+        cu_[i] = ep.colscale[cs_row(n0 + 64 + j4 + i)];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; i++) csv[i] = (n4 + i < N) ? ep.colscale[n4 + i] : 0.f;
+    }
+  }
+  // fused RMSNorm of the activation rows (consumer side): rrs[c] = rsqrt(mean x^2 + eps) of row m0 + c, from the
+  // producer's per-block partials, by warps 2-7 while the mainloop runs (published by the barrier after the drain)
+  __shared__ float rrs[NB];
+  if (ep.row_part && threadIdx.x >= 64) {
+    for (int c = threadIdx.x - 64; c < NB; c += DTHREADS - 64) {
+      const int m = m0 + c;
+      float sum = 0.f;
+      if (m < M)
+        for (int b = 0; b < ep.row_blocks; b++) sum += ep.row_part[(long)m * ep.row_blocks + b];
+      rrs[c] = rsqrtf(sum / (float)ep.row_d + ep.row_eps);
+    }
+  }
 
   bool ok = true;
   if (warp == 0 && lane == 0) {
@@ -319,25 +358,8 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       for (int i = 0; i < 32; i++) r[j][i] = 0u;
   }
   auto acc = [&](int c) { return __uint_as_float(r[c >> 5][c & 31]); };  // accumulator column c_lo + c
-  // fused RMSNorm of the activation rows (consumer side): rrs[c] = rsqrt(mean x^2 + eps) of row m0 + c
-  __shared__ float rrs[NB];
-  if (ep.row_part) {
-    for (int c = threadIdx.x; c < NB; c += DTHREADS) {
-      const int m = m0 + c;
-      float sum = 0.f;
-      if (m < M)
-        for (int b = 0; b < ep.row_blocks; b++) sum += ep.row_part[(long)m * ep.row_blocks + b];
-      rrs[c] = rsqrtf(sum / (float)ep.row_d + ep.row_eps);
-    }
-    __syncthreads();
-  }
+  if (ep.row_part) __syncthreads();  // rrs complete
   auto rr = [&](int c) { return ep.row_part ? rrs[c] : 1.f; };  // factor of accumulator column (row) c
-  // colscale entry of SwiGLU weight row p (interleaved order), or of the int8 matrix's row behind it (cs_inter > 0)
-  auto cs_row = [&](int p) {
-    if (ep.cs_inter <= 0) return p;
-    const int j = p & 127;
-    return j < 64 ? (p >> 7) * 64 + j : ep.cs_inter + (p >> 7) * 64 + j - 64;
-  };
 
   if (direct) {
     // no K split, store or SwiGLU: the output tile is assembled in shared memory and leaves by one TMA store
@@ -345,7 +367,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       // weight rows 0..63 of the block are gate rows, 64..127 the matching up rows (interleave_gate_up order): the
       // scaled accumulators go to part[c][nl], then a rolled sweep (small code: each CTA runs it once, from a cold
       // instruction cache) forms 4 outputs per step into the [NB][64] 16-bit tile that follows the partial
-      const float cs = ep.colscale ? ep.colscale[cs_row(n0 + nl)] : 1.f;
+      const float cs = cs_d;
 #pragma unroll
       for (int c = 0; c < CW; c++) part[(c_lo + c) * DP + nl] = acc(c) * cs * rr(c_lo + c);
       __syncthreads();
@@ -372,8 +394,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         *reinterpret_cast<uint2*>(tile + (c * 64 + j4) * 2) = pk;
       }
     } else {
-      const int n = n0 + nl;
-      const float cs = ep.colscale ? (n < N ? ep.colscale[n] : 0.f) : 1.f;
+      const float cs = cs_d;
       if (ep.c_dtype == DUO_F32) {
         float* o = reinterpret_cast<float*>(smem);
 #pragma unroll
@@ -449,13 +470,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       // half-warp per row: lane & 15 -> output columns 4 (lane & 15) .. + 3 of the block's 64 neurons
       const int j4 = (lane & 15) * 4;
       const int nout = n0 / 2 + j4;  // first output column
-      float cg_[4] = {1.f, 1.f, 1.f, 1.f}, cu_[4] = {1.f, 1.f, 1.f, 1.f};
-      if (ep.colscale) {
-        for (int i = 0; i < 4; i++) {
-          cg_[i] = ep.colscale[cs_row(n0 + j4 + i)];
-          cu_[i] = ep.colscale[cs_row(n0 + 64 + j4 + i)];
-        }
-      }
+      const float* cg_ = csv;  // gate column scales (preloaded)
       for (int cb = r_lo + warp * 2 + (lane >> 4); cb < r_hi; cb += 16 * RB) {
         int cr[RB];
 #pragma unroll
@@ -483,10 +498,6 @@ __global__ void __launch_bounds__(DTHREADS, 1)
     } else {
       // one row per warp step: lane -> weight rows n0 + 4 lane .. + 3
       const int n = n4;
-      float csv[4] = {1.f, 1.f, 1.f, 1.f};
-      if (ep.colscale) {
-        for (int i = 0; i < 4; i++) csv[i] = (n + i < N) ? ep.colscale[n + i] : 0.f;
-      }
       for (int cb = r_lo + warp; cb < r_hi && n < N; cb += 8 * RB) {
         int cr[RB];
 #pragma unroll
