@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <string>
+#include <type_traits>
 #include <utility>
 
 #include "../../include/duo_mixer.h"
@@ -207,6 +208,18 @@ __device__ __forceinline__ float silu16_(float x) { return __fdividef(x, 1.f + _
 template <typename T> __device__ __forceinline__ float silu_t(float x) {
   if constexpr (sizeof(T) == 2) return silu16_(x);
   else return siluf_(x);
+}
+// SiLU as x sigmoid(x) = x (1 + tanh(x / 2)) / 2 on one hardware tanh (tanh.approx.f32, about 2^-11 relative error,
+// one special-function op where silu16_ takes two): for values rounded to bf16 right after
+__device__ __forceinline__ float silu_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return 0.5f * x * (1.f + t);
+}
+// the bf16 engine's SiLU where the special-function pipe bounds the kernel; f16 and f32 keep silu_t
+template <typename T> __device__ __forceinline__ float silu_bf(float x) {
+  if constexpr (sizeof(T) == 2 && !std::is_same<T, __half>::value) return silu_tanh(x);
+  else return silu_t<T>(x);
 }
 // torch's softplus (beta 1, threshold 20) and the reference WGSL's (kernels_qwen35.js:11)
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }

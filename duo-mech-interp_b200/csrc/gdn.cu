@@ -249,9 +249,20 @@ __global__ void __launch_bounds__(256) gdn_conv_tma_kernel(const __grid_constant
     w[j][0] = ww.x; w[j][1] = ww.y; w[j][2] = ww.z; w[j][3] = ww.w;
   }
   T* out = static_cast<T*>(a.qkv_out);
+  const int hv_idx = cgp - 2 * a.hk;  // v-head blocks: the head whose gates they compute
+  const float neg_ea = norm ? 0.f : -expf(a.a_log[hv_idx]), dtb = norm ? 0.f : a.dt_bias[hv_idx];
   for (int j = j0; j < j1; j++) {
     const int s2 = (j - j0) % CONV_NS;
     const uint32_t ph = (uint32_t)(((j - j0) / CONV_NS) & 1);
+    const int t0 = j * CONV_TT, tn = min(CONV_TT, a.t - t0);
+    // v-head blocks: this tile's b and a inputs (one per token, 16 KB apart) requested before the wait, so that
+    // their latency overlaps it rather than the tile's tail
+    float yb = 0.f, ya = 0.f;
+    if (!norm && tid < tn) {
+      const long base = (m0 + t0 + tid) * a.w + conv_dim + a.hv * a.dv + hv_idx;
+      yb = to_f(y[base]);
+      ya = to_f(y[base + a.hv]);
+    }
     const bool ok = tc::mbar_wait(&full[s2], ph);
     if (__syncthreads_or(!ok)) {  // a load that never landed: give up (the fault word says so)
       if (tid == 0) {
@@ -265,7 +276,6 @@ __global__ void __launch_bounds__(256) gdn_conv_tma_kernel(const __grid_constant
       return;
     }
     const T* tile = ring + s2 * CONV_TT * 128;
-    const int t0 = j * CONV_TT, tn = min(CONV_TT, a.t - t0);
     for (int i = hw; i < tn; i += 16) {
       float v[8];
 #pragma unroll
@@ -288,7 +298,7 @@ __global__ void __launch_bounds__(256) gdn_conv_tma_kernel(const __grid_constant
 #pragma unroll
         for (int e = 0; e < 4; e++) {
           const float* wj = w[half * 4 + e];
-          v[half * 4 + e] = silu_t<T>(wj[0] * x[0][e] + wj[1] * x[1][e] + wj[2] * x[2][e] + wj[3] * x[3][e]);
+          v[half * 4 + e] = silu_bf<T>(wj[0] * x[0][e] + wj[1] * x[1][e] + wj[2] * x[2][e] + wj[3] * x[3][e]);
         }
       }
       if (norm) {
@@ -308,11 +318,9 @@ __global__ void __launch_bounds__(256) gdn_conv_tma_kernel(const __grid_constant
       store4<T>(o + 64 + 4 * c, v + 4);
     }
     if (!norm && tid < tn) {
-      const int hh = cgp - 2 * a.hk;
       const long m = m0 + t0 + tid;
-      const long base = m * a.w + conv_dim + a.hv * a.dv;
-      a.beta_out[m * a.hv + hh] = sigmoidf_(to_f(y[base + hh]));
-      a.g_out[m * a.hv + hh] = -expf(a.a_log[hh]) * softplusf_(to_f(y[base + a.hv + hh]) + a.dt_bias[hh]);
+      a.beta_out[m * a.hv + hv_idx] = sigmoidf_(yb);
+      a.g_out[m * a.hv + hv_idx] = neg_ea * softplusf_(ya + dtb);
     }
     __syncthreads();  // every read of this slot and of the halo is done
     if (j + 1 < j1 && tid < 128) {

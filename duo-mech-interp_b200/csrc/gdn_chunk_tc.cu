@@ -56,14 +56,6 @@ constexpr float QSCALE = 0.08838834764831845f;  // 1 / sqrt(128)
 // byte offset of 16-byte chunk c (0..7) of row r of a K-major 128-byte-swizzled tile
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-// SiLU as x sigmoid(x) = x (1 + tanh(x / 2)) / 2 on one hardware tanh (tanh.approx.f32, about 2^-11 relative):
-// the gate of an output that is rounded to 16 bits right after
-__device__ __forceinline__ float silu_tanh(float x) {
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
-  return 0.5f * x * (1.f + t);
-}
-
 __device__ __forceinline__ uint4 pack8h(const float* v) {
   uint4 u;
   u.x = wm::pack_f16(v[0], v[1]);
