@@ -4,6 +4,7 @@
 // Activation layout is token-major [M = rows * T, width] as in the reference (kernels_qwen35.js:5-6).  The residual
 // stream is f32; GEMM inputs, projections, caches and mixer outputs use the engine's activation dtype (f32 = the
 // reference's precision, bf16 = the tensor-core path).  The Gated DeltaNet state and the conv state are f32 always.
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -57,7 +58,7 @@ struct duo_engine {
   int rows = 0, max_len = 0, max_tokens = 0;
   float* x = nullptr;
   void* xn = nullptr;
-  float* nrm_part[2] = {nullptr, nullptr};  // fused-norm row partials: [256 rows][hidden / 128] each
+  float* nrm_part[2] = {nullptr, nullptr};  // fused-norm row partials: [rows][hidden / 128 (decode) or / 256]
   void* y = nullptr;
   void* qkv = nullptr;
   float* g = nullptr;
@@ -250,10 +251,11 @@ void set_norm_out(GemmEpiArgs& ep, const float* w, void* xn, float* part) {
   ep.nrm_part = part;
 }
 
-// the GEMM consumes xn written by set_norm_out: its accumulator rows are scaled by rsqrt(mean x^2 + eps)
-void set_row_norm(GemmEpiArgs& ep, const float* part, int d, float eps) {
+// the GEMM consumes xn written by set_norm_out: its accumulator rows are scaled by rsqrt(mean x^2 + eps); the
+// producer wrote one partial per 128 columns (decode GEMM, m <= 256) or per 256 (persistent GEMM)
+void set_row_norm(GemmEpiArgs& ep, const float* part, int m, int d, float eps) {
   ep.row_part = part;
-  ep.row_blocks = d / 128;
+  ep.row_blocks = d / (m <= 256 ? 128 : 256);
   ep.row_d = d;
   ep.row_eps = eps;
 }
@@ -264,11 +266,11 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
   const int M = rows * T;
   const int H = c.hidden;
   const int act = e->act;
-  // RMSNorm fused into the decode GEMMs (bf16, 8 < M <= 256 rows): the residual-add epilogue writes the next norm's
+  // RMSNorm fused into the tensor-core GEMMs (bf16, M > 8 rows): the residual-add epilogue writes the next norm's
   // weighted input and per-block sums of squares; the consuming GEMM scales its accumulator rows by the rsqrt.  The
   // norm before layer 0's input projection stays a launch.  f16 keeps the launch: the weighted input before the
   // rsqrt could leave the f16 range.
-  const bool fuse_norm = act == DUO_BF16 && M > kGemvMax && M <= 256 && H % 128 == 0 && fused_norm_enabled();
+  const bool fuse_norm = act == DUO_BF16 && M > kGemvMax && H % 256 == 0 && fused_norm_enabled();
   PROF_TRY(DUO_PROF_GATHER, launch_gather(ids_dev, M, e->w.embed.q, e->w.embed.s, e->gsize(H), H, c.vocab, e->x, st));
   for (int l = 0; l < c.layers; l++) {
     const duo_layer_view& L = e->lw[l];
@@ -284,7 +286,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.c = e->y;
       ep.c_dtype = act;
       ep.ldc = wproj;
-      if (in_fused) set_row_norm(ep, e->nrm_part[1], H, c.eps);
+      if (in_fused) set_row_norm(ep, e->nrm_part[1], M, H, c.eps);
       PROF_TRY(M <= kGemvMax ? DUO_PROF_GEMV : DUO_PROF_GEMM, project(e, xin, M, H, L.proj, e->p_proj[l], wproj, ep, st));
     }
     int out_k;
@@ -363,7 +365,7 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
       ep.row_base = row_base;
       ep.push = pt;
       ep.b_const = true;  // weight packs are written once, at creation
-      if (fuse_norm) set_row_norm(ep, e->nrm_part[0], H, c.eps);
+      if (fuse_norm) set_row_norm(ep, e->nrm_part[0], M, H, c.eps);
       if (M <= 256 && dec_q8_enabled()) {
         // int8 gate / up rows in their own order: the kernel reads them through the pack's interleave
         const int grp = e->gsize(H);
@@ -549,7 +551,7 @@ extern "C" int duo_engine_alloc(duo_engine* e, int rows, int max_len, int max_to
   DUO_TRY(A(&p, Mx * c.hidden * 4)); e->x = (float*)p;
   DUO_TRY(A(&e->xn, Mx * c.hidden * as));
   for (auto& np : e->nrm_part) {
-    DUO_TRY(A(&p, (size_t)256 * (c.hidden / 128 + 1) * 4));
+    DUO_TRY(A(&p, (size_t)std::max<long>(256L * (c.hidden / 128 + 1), Mx * (c.hidden / 256 + 1)) * 4));
     np = (float*)p;
   }
   DUO_TRY(A(&e->y, Mx * e->wmax * as));

@@ -442,14 +442,25 @@ int launch_gemm_tc(const void* a, int m, int k, const void* b, int n, int ab_dty
   DUO_CHECK_ARG(ab_dtype == DUO_BF16 || ab_dtype == DUO_F16, "gemm_tc: operands must be bf16 or f16");
   // decode-sized row counts: the weights-on-M kernel (row groups x weight blocks x K slices)
   if (m <= 256 && ep.epi != EPI_ARGMAX) return launch_gemm_dec(a, m, k, b, n, ab_dtype, ep, st);
-  DUO_CHECK_ARG(!ep.nrm_out && !ep.row_part, "gemm_tc: the fused norm is a decode-GEMM epilogue (m <= 256)");
+  // the fused RMSNorm (producer partials per 256 columns, consumer row factors) is an epilogue of the persistent
+  // kernel with 256-wide tiles, whatever the grid
+  const bool fused_norm = ep.nrm_out || ep.row_part;
+  if (ep.nrm_out) {
+    const bool al = ((reinterpret_cast<uintptr_t>(ep.nrm_out) | reinterpret_cast<uintptr_t>(ep.c) |
+                      reinterpret_cast<uintptr_t>(ep.nrm_w)) & 15) == 0 && ep.ldc % 8 == 0;
+    DUO_CHECK_ARG(ep.epi == EPI_ADD_F32 && n % 256 == 0 && al && ep.nrm_w && ep.nrm_part,
+                  "gemm_tc: the fused norm needs the residual add, n a multiple of 256 and 16-byte aligned rows");
+  }
+  if (ep.row_part)
+    DUO_CHECK_ARG((ep.epi == EPI_STORE || ep.epi == EPI_SWIGLU) && ep.row_blocks > 0 && ep.row_d > 0,
+                  "gemm_tc: row factors apply to the store and SwiGLU epilogues");
   const int sms = sm_count();
   const long tiles_m = cdiv(m, TC_BM);
   // the widest N tile that still gives every SM work (SwiGLU: gate / up interleaved per 64 rows, tiles >= 128)
   if (ep.epi == EPI_SWIGLU) DUO_CHECK_ARG(n % 128 == 0, "gemm_tc: SwiGLU epilogue needs n a multiple of 128");
   int bn = 256;
-  if (tiles_m * cdiv(n, 256) < sms) bn = 128;
-  if (ep.epi != EPI_SWIGLU && tiles_m * cdiv(n, 128) < sms) bn = 64;
+  if (!fused_norm && tiles_m * cdiv(n, 256) < sms) bn = 128;
+  if (!fused_norm && ep.epi != EPI_SWIGLU && tiles_m * cdiv(n, 128) < sms) bn = 64;
   const long tiles = tiles_m * cdiv(n, bn);
   // small grid: per-tile kernel, two CTAs per SM; otherwise the persistent kernel
   const bool small = bn == 64 || (bn == 128 && tiles < 2L * sms);

@@ -197,15 +197,23 @@ __global__ void __launch_bounds__(PTHREADS, 1)
     int it = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
       const int b = it & 1;
+      int tile_m, tile_n;
+      tile_mn(t, tile_m, tile_n);
+      const int row0 = tile_m + quad * 32;
+      // fused RMSNorm (consumer): the factor rsqrt(mean x^2 + eps) of this thread's accumulator row, from the
+      // producer's per-block partials, requested before the accumulator wait
+      float rrow = 1.f;
+      if (EPI != EPI_ADD_F32 && EPI != EPI_ARGMAX && ep.row_part && row0 + lane < M) {
+        float sum = 0.f;
+        for (int q = 0; q < ep.row_blocks; q++) sum += ep.row_part[(long)(row0 + lane) * ep.row_blocks + q];
+        rrow = rsqrtf(sum / (float)ep.row_d + ep.row_eps);
+      }
       if (!pwait(&acc_full[b], (uint32_t)((it >> 1) & 1), abort)) {
         if (lane == 0) atomicOr(fault, 4u);
         break;
       }
       tc::fence_after_sync();
-      int tile_m, tile_n;
-        tile_mn(t, tile_m, tile_n);
       const uint32_t trow = tmem + b * BN + ((uint32_t)(quad * 32) << 16);
-      const int row0 = tile_m + quad * 32;
       const int n0 = (EPI == EPI_SWIGLU) ? tile_n / 2 : tile_n;
       if (EPI == EPI_ARGMAX) {
         // thread = row: scan its BN columns in ascending order, keeping the first maximum
@@ -239,6 +247,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
         }
         continue;
       }
+      float rowss[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // fused RMSNorm (producer): rows s8 * 4 + lane / 8
 #pragma unroll 1
       for (int c0 = 0; c0 < NC; c0 += 32) {
         // (1) 32 accumulator columns of this thread's row -> scaled (SwiGLU: combined) values -> the transpose buffer
@@ -277,12 +286,13 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             tc::tmem_ld_wait(r0);
             tc::tmem_ld_wait(r1);
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = silu16_(__uint_as_float(r0[j]) * cg[j]) * (__uint_as_float(r1[j]) * cu[j]);
+            for (int j = 0; j < 32; j++)
+              v[j] = silu16_(__uint_as_float(r0[j]) * cg[j] * rrow) * (__uint_as_float(r1[j]) * cu[j] * rrow);
           } else {
             tc::tmem_ld32_issue(trow + c0, r0);
             tc::tmem_ld_wait(r0);
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r0[j]);  // scaled after the transpose
+            for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r0[j]) * rrow;  // column scales after the transpose
           }
         }
         if (c0 + 32 >= NC) {  // every TMEM read of this tile is done: hand the accumulator back to the MMA warp
@@ -305,7 +315,8 @@ __global__ void __launch_bounds__(PTHREADS, 1)
 #pragma unroll
             for (int i = 0; i < 4; i++) cs4[i] = n + i < ncols ? ep.colscale[n + i] : 0.f;
           }
-          float4 old[8], add[8];
+          float4 old[8], add[8], nw4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (EPI == EPI_ADD_F32 && ep.nrm_out) nw4 = *reinterpret_cast<const float4*>(ep.nrm_w + n);
 #pragma unroll
           for (int s8 = 0; s8 < 8; s8++) {
             const int m = row0 + s8 * 4 + (lane >> 3);
@@ -344,6 +355,23 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             float* X = static_cast<float*>(ep.c) + (long)m * ep.ldc + n;
             if (v16 && n + 4 <= ncols) *reinterpret_cast<float4*>(X) = make_float4(o[0], o[1], o[2], o[3]);
             else for (int i = 0; i < 4 && n + i < ncols; i++) X[i] = o[i];
+            if (EPI == EPI_ADD_F32 && ep.nrm_out) {  // the next norm's weighted input (host: N % 256 == 0, aligned)
+              const float y[4] = {o[0] * (1.f + nw4.x), o[1] * (1.f + nw4.y), o[2] * (1.f + nw4.z), o[3] * (1.f + nw4.w)};
+              uint32_t w2[2];
+#pragma unroll
+              for (int i = 0; i < 2; i++) {
+                if (F16) {
+                  const __half2 h = __floats2half2_rn(y[2 * i], y[2 * i + 1]);
+                  w2[i] = *reinterpret_cast<const uint32_t*>(&h);
+                } else {
+                  const __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+                  w2[i] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+              }
+              *reinterpret_cast<uint2*>(static_cast<uint8_t*>(ep.nrm_out) + ((long)m * ep.ldc + n) * 2) =
+                  make_uint2(w2[0], w2[1]);
+              rowss[s8] += o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3];
+            }
           }
         } else {
           // 16-bit output: 4 lanes x 8 columns (16 bytes) per row, 8 rows per step
@@ -387,6 +415,18 @@ __global__ void __launch_bounds__(PTHREADS, 1)
           }
         }
         __syncwarp();  // wb is rewritten by the next chunk
+      }
+      if (EPI == EPI_ADD_F32 && ep.nrm_out) {
+        // the 8 lanes of a row hold its 4-column pieces: sum them, then one lane per row writes the tile's partial
+#pragma unroll
+        for (int s8 = 0; s8 < 8; s8++) {
+          float v = rowss[s8];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          const int m = row0 + s8 * 4 + (lane >> 3);
+          if ((lane & 7) == 0 && m < M) ep.nrm_part[(long)m * (N / BN) + tile_n / BN] = v;
+        }
       }
     }
   }

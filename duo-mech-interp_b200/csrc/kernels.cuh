@@ -50,9 +50,10 @@ struct GemmEpiArgs {
   int32_t* idx = nullptr;       // ARGMAX: column of each partial maximum (c holds the f32 maxima)
   bool b_const = false;         // B is not written by the kernel launched just before (weight packs): its first
                                 // tiles may be fetched before the programmatic-launch wait
-  // RMSNorm fused across two decode GEMMs (launch_gemm_dec only; n a multiple of 128).  The residual add also
-  // writes the next norm's input scaled by its weight, nrm_out[m, n] = x_new[m, n] * (1 + nrm_w[n]) in the operand
-  // dtype (row stride ldc), and each CTA's sum of x_new^2 over its 128 columns to nrm_part[m * (n / 128) + block];
+  // RMSNorm fused across two tensor-core GEMMs (decode GEMM: blocks of 128 columns, n a multiple of 128; m > 256:
+  // the persistent kernel's 256-wide tiles, n a multiple of 256).  The residual add also writes the next norm's input
+  // scaled by its weight, nrm_out[m, n] = x_new[m, n] * (1 + nrm_w[n]) in the operand dtype (row stride ldc), and
+  // the sum of x_new^2 over each block of columns to nrm_part[m * (n / block) + block index];
   // the consuming GEMM multiplies the accumulator of activation row m by
   // rsqrt(sum_b row_part[m * row_blocks + b] / row_d + row_eps), summed in block order (deterministic).
   const float* nrm_w = nullptr;
