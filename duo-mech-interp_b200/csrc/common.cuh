@@ -43,6 +43,9 @@ int fail(int code, const std::string& msg);
   } while (0)
 
 void count_launch();
+// launches executed by graph replays: the capture counted one step's kernels, each replay runs them again
+void count_launches(long long delta);
+unsigned long long launch_count();
 
 // ---------------------------------------------------------------------------------------------------------------
 // Programmatic dependent launch.  Kernels are launched with programmatic stream serialisation, so the CTAs of a kernel

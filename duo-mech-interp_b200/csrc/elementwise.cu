@@ -195,19 +195,25 @@ int launch_finish_rows(const float* x, int h, int t, int row_base, int rows, flo
 }
 
 // ids for the next decode step from the argmax of the previous one, and the token log
+// One block: the step index is the host's `step`, or (step_ctr != nullptr, a graph-replayed step) read from the
+// device counter, which the block advances once every thread has read it.
 __global__ void feed_tokens_kernel(const int32_t* __restrict__ am, int rows, int32_t* __restrict__ ids,
-                                   int32_t* __restrict__ log, int n_steps, int step) {
+                                   int32_t* __restrict__ log, int n_steps, int step, int32_t* step_ctr) {
   pdl_enter();
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= rows) return;
-  const int tok = am[r];
-  ids[r] = tok;
-  log[(long)r * n_steps + step] = tok;
+  if (step_ctr) step = *step_ctr;
+  __syncthreads();
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    const int tok = am[r];
+    ids[r] = tok;
+    if (step < n_steps) log[(long)r * n_steps + step] = tok;
+  }
+  __syncthreads();
+  if (step_ctr && threadIdx.x == 0) *step_ctr = step + 1;
 }
 
 int launch_feed_tokens(const int32_t* am, int rows, int32_t* ids, int32_t* log, int n_steps, int step,
-                       cudaStream_t st) {
-  DUO_CUDA_TRY(::duo::launch_kernel(feed_tokens_kernel, cdiv(rows, 128), 128, 0, st, am, rows, ids, log, n_steps, step));
+                       int32_t* step_ctr, cudaStream_t st) {
+  DUO_CUDA_TRY(::duo::launch_kernel(feed_tokens_kernel, 1, 256, 0, st, am, rows, ids, log, n_steps, step, step_ctr));
   DUO_LAUNCH_CHECK("feed_tokens_kernel");
   return DUO_OK;
 }

@@ -115,8 +115,10 @@ int launch_push_stats(const float* logits, int n, int vocab, long ld, const int3
                       const float* tlw, int nt, float* stats, float* d, long ldd, cudaStream_t st);
 int launch_finish_rows(const float* x, int h, int t, int row_base, int rows, float* last, int32_t* len,
                        cudaStream_t st);
+// the greedy tokens am[rows] -> the next forward's ids and column `step` of log[rows][n_steps] (step_ctr != nullptr:
+// the step index is read from, and advanced in, that device counter)
 int launch_feed_tokens(const int32_t* am, int rows, int32_t* ids, int32_t* log, int n_steps, int step,
-                       cudaStream_t st);
+                       int32_t* step_ctr, cudaStream_t st);
 
 // ---- Gated DeltaNet
 struct GdnConvArgs {

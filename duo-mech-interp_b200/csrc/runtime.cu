@@ -23,6 +23,10 @@ int fail(int code, const std::string& msg) {
 static std::atomic<unsigned long long> g_launches{0};
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void count_launches(long long delta) {
+  g_launches.fetch_add(static_cast<unsigned long long>(delta), std::memory_order_relaxed);
+}
+unsigned long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 bool pdl_enabled() {
   static const bool on = [] {

@@ -230,6 +230,41 @@ def test_generate_matches_step_loop(tiny):
     assert torch.equal(toks.long(), torch.stack(ref_toks, 1))
 
 
+@pytest.mark.parametrize("act,rows", [("f32", 3), ("bf16", 12), ("bf16", 3)])
+def test_generate_graph_replay_equals_direct(tiny, act, rows):
+    """generate on a non-default stream replays a CUDA graph of one decode step (the step index in a device
+    counter); on the default stream it launches each step.  Same tokens, same final logits, bit for bit, across two
+    generate calls (the second one captures again)."""
+    import torch
+    from duo import Model
+    types, packs = tiny
+    W, _ = packs[128]
+    T = 9
+    ids = torch.randint(0, TINY["vocab"], (rows, T), generator=torch.Generator().manual_seed(11))
+    vecs = [torch.randn(TINY["hidden"], generator=torch.Generator().manual_seed(12 + r)) for r in range(rows)]
+    cfg = duo_cfg_from_tiny(types, act)
+    out = {}
+    import contextlib
+    from duo import lib as L
+    for name, stream in (("direct", None), ("graph", torch.cuda.Stream())):
+        with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
+            m = Model(cfg, W, stream=stream).alloc(rows=rows, max_len=32, max_t=T, max_tokens=rows * T)
+            m.set_vectors(vecs)
+            m.forward(ids.reshape(-1), 0, rows, T, {"vec": 1})
+            c0 = L.lib().duo_launch_count()
+            g1 = m.generate(5, vec=1).cpu()
+            g2 = m.generate(3, vec=1).cpu()
+            launches = L.lib().duo_launch_count() - c0  # replays count the kernels they run
+            out[name] = (g1, g2, m.logits_all().cpu(), m.row_len(0), launches)
+    d, g = out["direct"], out["graph"]
+    assert d[4] == g[4] > 0
+    assert torch.equal(d[0], g[0]) and torch.equal(d[1], g[1])
+    assert torch.equal(d[2], g[2])
+    assert d[3] == g[3] == T + 8
+    from duo import ops
+    assert ops.fault_status() == 0
+
+
 @pytest.mark.parametrize("act", ["f16", "bf16"])
 def test_greedy_from_lm_head_epilogue(tiny, act):
     """More than 8 rows on the tensor-core engine: argmax_all and generate take the LM head's argmax epilogue (no
