@@ -190,8 +190,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const long off = (long)m * ep.ldc + n;
           const bool vec4 = al && n + 4 <= ncols;
           if (EPI == EPI_SWIGLU && ep.push.count) {
+            const unsigned pm = push_mask(ep.push, n, 4);
+            if (pm) {
 #pragma unroll
-            for (int i = 0; i < 4; i++) x[i] = push_apply(ep.push, r, n + i, x[i]);
+              for (int i = 0; i < 4; i++) x[i] = push_apply_masked(ep.push, pm, r, n + i, x[i]);
+            }
           }
           if (EPI == EPI_ADD_F32) {
             float* X = static_cast<float*>(ep.c) + off;
@@ -597,6 +600,7 @@ extern "C" int duo_gemm_swiglu(const void* a, int m, int k, const void* b, int i
   DUO_CHECK_ARG(ldo >= inter, "gemm_swiglu: ldo < inter");
   DUO_CHECK_ARG(push_count >= 0 && (push_count == 0 || (push_neurons && push_modes && push_vals)),
                 "gemm_swiglu: null push table");
+  DUO_CHECK_ARG(push_count <= 32, "gemm_swiglu: at most 32 push records");
   DUO_CHECK_ARG(push_count == 0 || row_base + (m > 0 ? (m - 1) / t : 0) < push_rows,
                 "gemm_swiglu: rows beyond the push table");
   GemmEpiArgs ep;

@@ -372,16 +372,18 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       for (int c = 0; c < CW; c++) part[(c_lo + c) * DP + nl] = acc(c) * cs * rr(c_lo + c);
       __syncthreads();
       uint8_t* tile = smem + C::OUT_OFF;
+      // this thread's 4 output columns are the same in every iteration (DTHREADS is a multiple of 16)
+      const unsigned pm = ep.push.count ? push_mask(ep.push, n0 / 2 + (threadIdx.x & 15) * 4, 4) : 0u;
 #pragma unroll 1
       for (int idx = threadIdx.x; idx < NB * 16; idx += DTHREADS) {
         const int c = idx >> 4, j4 = (idx & 15) * 4, m = m0 + c;
         const float4 g = *reinterpret_cast<const float4*>(part + c * DP + j4);
         const float4 u = *reinterpret_cast<const float4*>(part + c * DP + 64 + j4);
         float o[4] = {silu16_(g.x) * u.x, silu16_(g.y) * u.y, silu16_(g.z) * u.z, silu16_(g.w) * u.w};
-        if (ep.push.count && m < M) {
+        if (pm && m < M) {
           const int rw = ep.row_base + m / ep.t;
 #pragma unroll
-          for (int i = 0; i < 4; i++) o[i] = push_apply(ep.push, rw, n0 / 2 + j4 + i, o[i]);
+          for (int i = 0; i < 4; i++) o[i] = push_apply_masked(ep.push, pm, rw, n0 / 2 + j4 + i, o[i]);
         }
         uint2 pk;
         if (F16) {
@@ -471,6 +473,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       const int j4 = (lane & 15) * 4;
       const int nout = n0 / 2 + j4;  // first output column
       const float* cg_ = csv;  // gate column scales (preloaded)
+      const unsigned pm = ep.push.count ? push_mask(ep.push, nout, 4) : 0u;
       for (int cb = r_lo + warp * 2 + (lane >> 4); cb < r_hi; cb += 16 * RB) {
         int cr[RB];
 #pragma unroll
@@ -490,7 +493,7 @@ __global__ void __launch_bounds__(DTHREADS, 1)
 #pragma unroll
           for (int c = 0; c < 4; c++) {
             o[c] = silu16_(gv[c] * cg_[c]) * (uv[c] * cu_[c]);
-            if (ep.push.count) o[c] = push_apply(ep.push, rw, nout + c, o[c]);
+            if (pm) o[c] = push_apply_masked(ep.push, pm, rw, nout + c, o[c]);
           }
           store4_16((long)m * ep.ldc + nout, o);
         }

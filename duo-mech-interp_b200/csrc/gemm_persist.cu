@@ -316,6 +316,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             for (int i = 0; i < 4; i++) cs4[i] = n + i < ncols ? ep.colscale[n + i] : 0.f;
           }
           float4 old[8], add[8], nw4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          const unsigned pm = (EPI == EPI_SWIGLU && ep.push.count) ? push_mask(ep.push, n, 4) : 0u;
           if (EPI == EPI_ADD_F32 && ep.nrm_out) nw4 = *reinterpret_cast<const float4*>(ep.nrm_w + n);
 #pragma unroll
           for (int s8 = 0; s8 < 8; s8++) {
@@ -348,9 +349,9 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             x.x *= cs4[0]; x.y *= cs4[1]; x.z *= cs4[2]; x.w *= cs4[3];
             float o[4] = {old[s8].x + x.x + add[s8].x, old[s8].y + x.y + add[s8].y, old[s8].z + x.z + add[s8].z,
                           old[s8].w + x.w + add[s8].w};
-            if (EPI == EPI_SWIGLU && ep.push.count) {
+            if (EPI == EPI_SWIGLU && pm) {
               const int r = ep.row_base + m / ep.t;
-              for (int i = 0; i < 4; i++) o[i] = push_apply(ep.push, r, n + i, o[i]);
+              for (int i = 0; i < 4; i++) o[i] = push_apply_masked(ep.push, pm, r, n + i, o[i]);
             }
             float* X = static_cast<float*>(ep.c) + (long)m * ep.ldc + n;
             if (v16 && n + 4 <= ncols) *reinterpret_cast<float4*>(X) = make_float4(o[0], o[1], o[2], o[3]);
@@ -378,6 +379,7 @@ __global__ void __launch_bounds__(PTHREADS, 1)
           const int c8 = (lane & 3) * 8, n = nb + c8;
           // this lane's 8 column scales (store; SwiGLU values are scaled already)
           float cs8[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+          const unsigned pm = (EPI == EPI_SWIGLU && ep.push.count) ? push_mask(ep.push, n, 8) : 0u;
           if (EPI != EPI_SWIGLU && ep.colscale) {
 #pragma unroll
             for (int i = 0; i < 8; i++) cs8[i] = n + i < ncols ? ep.colscale[n + i] : 0.f;
@@ -391,9 +393,9 @@ __global__ void __launch_bounds__(PTHREADS, 1)
             const float4 hi = *reinterpret_cast<const float4*>(wb + row * PEPI_PITCH + c8 + 4);
             float x[8] = {lo.x * cs8[0], lo.y * cs8[1], lo.z * cs8[2], lo.w * cs8[3],
                           hi.x * cs8[4], hi.y * cs8[5], hi.z * cs8[6], hi.w * cs8[7]};
-            if (EPI == EPI_SWIGLU && ep.push.count) {
+            if (EPI == EPI_SWIGLU && pm) {
               const int r = ep.row_base + m / ep.t;
-              for (int i = 0; i < 8 && n + i < ncols; i++) x[i] = push_apply(ep.push, r, n + i, x[i]);
+              for (int i = 0; i < 8 && n + i < ncols; i++) x[i] = push_apply_masked(ep.push, pm, r, n + i, x[i]);
             }
             const long off = (long)m * ep.ldc + n;
             if (v16 && n + 8 <= ncols) {

@@ -29,6 +29,29 @@ __device__ __forceinline__ float push_apply(const PushTable& pt, int r, int n, f
   }
   return v;
 }
+// The entries that can touch columns [n, n + w) (bit i: entry i; the table holds at most 32): computed once for a
+// thread's columns, so the per-element loop visits only them (usually none) instead of the whole table.
+__device__ __forceinline__ unsigned push_mask(const PushTable& pt, int n, int w) {
+  unsigned mask = 0u;
+  for (int i = 0; i < pt.count; i++) {
+    const int pn = pt.neuron[i];
+    if (pn == DUO_ALL_NEURONS || (pn >= n && pn < n + w)) mask |= 1u << i;
+  }
+  return mask;
+}
+// push_apply over the entries of `mask` (a push_mask covering n), in list order
+__device__ __forceinline__ float push_apply_masked(const PushTable& pt, unsigned mask, int r, int n, float v) {
+  while (mask) {
+    const int i = __ffs(mask) - 1;
+    mask &= mask - 1u;
+    const int pn = pt.neuron[i];
+    if (pn == DUO_ALL_NEURONS || pn == n) {
+      const float val = pt.vals[(long)i * pt.rows + r];
+      v = pt.mode[i] == DUO_PUSH_MUL ? v * val : v + val;
+    }
+  }
+  return v;
+}
 
 // Epilogues of the tensor-core GEMM.
 enum GemmEpi {

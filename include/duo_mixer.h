@@ -95,7 +95,8 @@ int duo_gemm_bf16(const void* a, int m, int k, const void* b, int n, const float
  * push_rows + r] to neuron push_neurons[p] (DUO_PUSH_ADD) or multiplies it in (DUO_PUSH_MUL); neuron -1 is every
  * neuron.  B holds gate and up rows interleaved in blocks of 64: B rows [128 b, 128 b + 64) are gate rows 64 b ..
  * 64 b + 63 and B rows [128 b + 64, 128 b + 128) the matching up rows (col_scale in the same order, may be NULL).
- * A and B are bf16 or f16 (ab_dtype); out has the same dtype, leading dim ldo.  k and inter multiples of 64.
+ * A and B are bf16 or f16 (ab_dtype); out has the same dtype, leading dim ldo.  k and inter multiples of 64; at most
+ * 32 push records.
  * Replaces `_mm(xn, gu)` + `swiglu`, engine/model.js:448-457 and engine/kernels_qwen35.js:250-280. */
 int duo_gemm_swiglu(const void* a, int m, int k, const void* b, int inter, int ab_dtype, const float* col_scale,
                     void* out, int ldo, const int32_t* push_neurons, const int32_t* push_modes, const float* push_vals,
