@@ -472,6 +472,123 @@ static int run_recurrent(const GdnScanArgs& a, cudaStream_t st) {
   return DUO_OK;
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// short prefill (2 <= t <= SHORT_T tokens per row, 16-bit engines): the delta rule token by token with the (row,
+// head) state held in registers across the call's tokens.  The chunked kernel computes a whole 64-token chunk
+// whatever t, and its one CTA per (row, head) owns an SM (its shared memory) for its fixed costs; here a persistent
+// grid of 2 CTAs per SM walks the (row, head) items, stages the item's q (times 1 / sqrt(dk)), k, v, e^g and beta in
+// shared memory, reads and writes the 64 KB state once, and per token runs S *= e^g; u = S^T k;
+// S += k (beta (v - u))^T; o = S^T q.  Lane l of warp w owns state column 16 w + l % 16, rows 64 (l / 16) ..
+// + 63, so both column sums close with one shuffle and a token needs no block barrier.  q and k arrive l2-normalised
+// from the conv prologue (l2norm_qk == 0).  Then the gated RMSNorm per token.
+constexpr int SHORT_T = 16, SHORT_THREADS = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(SHORT_THREADS, 2) gdn_short_kernel(GdnScanArgs a) {
+  pdl_enter();
+  __shared__ __align__(16) float qs[SHORT_T][128], ks[SHORT_T][128], vs[SHORT_T][128], os[SHORT_T][128];
+  __shared__ float gs[SHORT_T], bs[SHORT_T];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = warp * 16 + (lane & 15), r0 = (lane >> 4) * 64;  // this lane's state column and first row
+  const int H = a.h, TT = a.t;
+  const int items = a.b * H;
+  const T* q = static_cast<const T*>(a.q);
+  const T* k = static_cast<const T*>(a.k);
+  const T* v = static_cast<const T*>(a.v);
+  const float qscale = rsqrtf(128.f);
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int b = item / H, h = item % H, kh = h / (H / a.hq);
+    float* S = a.state + (((long)(a.state_row0 + b) * H + h) * 128) * 128;  // [dk][dv]
+    for (int idx = tid; idx < TT * 128; idx += SHORT_THREADS) {
+      const int t = idx >> 7, cc = idx & 127;
+      const long m = (long)b * TT + t;
+      qs[t][cc] = to_f(q[m * a.q_stride + kh * 128 + cc]) * qscale;
+      ks[t][cc] = to_f(k[m * a.k_stride + kh * 128 + cc]);
+      vs[t][cc] = to_f(v[m * a.v_stride + h * 128 + cc]);
+    }
+    if (tid < TT) {
+      const long m = (long)b * TT + tid;
+      gs[tid] = expf(a.g[m * H + h]);
+      bs[tid] = a.beta[m * H + h];
+    }
+    float st[64];
+#pragma unroll
+    for (int r = 0; r < 64; r++) st[r] = S[(long)(r0 + r) * 128 + c];
+    __syncthreads();
+#pragma unroll 1
+    for (int t = 0; t < TT; t++) {
+      const float gd = gs[t];
+      const float4* k4 = reinterpret_cast<const float4*>(&ks[t][r0]);
+      const float4* q4 = reinterpret_cast<const float4*>(&qs[t][r0]);
+      float ua = 0.f, ub = 0.f, uc = 0.f, ud = 0.f;  // four independent chains
+#pragma unroll
+      for (int r = 0; r < 16; r++) {
+        const float4 kk = k4[r];
+        st[4 * r] *= gd; st[4 * r + 1] *= gd; st[4 * r + 2] *= gd; st[4 * r + 3] *= gd;
+        ua = fmaf(st[4 * r], kk.x, ua); ub = fmaf(st[4 * r + 1], kk.y, ub);
+        uc = fmaf(st[4 * r + 2], kk.z, uc); ud = fmaf(st[4 * r + 3], kk.w, ud);
+      }
+      float u = (ua + ub) + (uc + ud);
+      u += __shfl_xor_sync(0xffffffffu, u, 16);
+      const float d = bs[t] * (vs[t][c] - u);
+      float oa = 0.f, ob = 0.f, oc = 0.f, od = 0.f;
+#pragma unroll
+      for (int r = 0; r < 16; r++) {
+        const float4 kk = k4[r], qq = q4[r];
+        st[4 * r] = fmaf(kk.x, d, st[4 * r]); st[4 * r + 1] = fmaf(kk.y, d, st[4 * r + 1]);
+        st[4 * r + 2] = fmaf(kk.z, d, st[4 * r + 2]); st[4 * r + 3] = fmaf(kk.w, d, st[4 * r + 3]);
+        oa = fmaf(st[4 * r], qq.x, oa); ob = fmaf(st[4 * r + 1], qq.y, ob);
+        oc = fmaf(st[4 * r + 2], qq.z, oc); od = fmaf(st[4 * r + 3], qq.w, od);
+      }
+      float o = (oa + ob) + (oc + od);
+      o += __shfl_xor_sync(0xffffffffu, o, 16);
+      if (lane < 16) os[t][c] = o;
+    }
+#pragma unroll
+    for (int r = 0; r < 64; r++) S[(long)(r0 + r) * 128 + c] = st[r];
+    __syncthreads();  // os complete
+    // per token: gated RMSNorm over the head's 128 outputs (warp w takes tokens w, w + 8; lane: columns 4 lane ..)
+    const float hs = a.head_scale ? a.head_scale[h] : 1.f;
+    for (int t = warp; t < TT; t += SHORT_THREADS / 32) {
+      const long m = (long)b * TT + t;
+      float ov[4], ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        ov[i] = os[t][lane * 4 + i];
+        ss += ov[i] * ov[i];
+      }
+      ss = warp_sum(ss);
+      const float rms = a.norm_w ? rsqrtf(ss / 128.f + a.eps) : 1.f;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int cc = lane * 4 + i;
+        float y = ov[i];
+        if (a.norm_w)
+          y = y * rms * a.norm_w[cc] * silu_bf<T>(to_f(static_cast<const T*>(a.z)[m * a.z_stride + h * 128 + cc])) * hs;
+        static_cast<T*>(a.o)[m * a.o_stride + h * 128 + cc] = from_f<T>(y);
+      }
+    }
+    __syncthreads();  // the staged inputs and os are rewritten by the next item
+  }
+}
+
+int launch_gdn_short(const GdnScanArgs& a, int dtype, cudaStream_t st) {
+  if (a.b == 0 || a.t == 0) return DUO_OK;
+  if (a.t > SHORT_T || a.dk != 128 || a.dv != 128 || a.l2norm_qk || a.hq < 1 || a.h % a.hq ||
+      (dtype != DUO_BF16 && dtype != DUO_F16))
+    return fail(DUO_EINVAL, "gdn_short: 16-bit inputs, t <= 16, dk = dv = 128, q and k already normalised");
+  const int items = a.b * a.h;
+  const int grid = std::min(items, 2 * sm_count());
+  return with_act(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    if constexpr (sizeof(T) == 2) {
+      DUO_CUDA_TRY(::duo::launch_kernel(gdn_short_kernel<T>, grid, SHORT_THREADS, 0, st, a));
+      DUO_LAUNCH_CHECK("gdn_short_kernel");
+    }
+    return DUO_OK;
+  });
+}
+
 int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st) {
   if (a.b == 0 || a.t == 0) return DUO_OK;
   if (a.dk != 128 || a.dv != 128) return fail(DUO_EINVAL, "gdn: needs dk = dv = 128");

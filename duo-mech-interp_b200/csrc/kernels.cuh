@@ -176,6 +176,8 @@ struct GdnScanArgs {
 };
 long gdn_chunk_ws_bytes(int b, int t, int h);
 int launch_gdn_recurrent(const GdnScanArgs& a, int dtype, cudaStream_t st);
+// short prefill of the 16-bit engines (2 <= t <= 16): token by token with the state held in registers per item
+int launch_gdn_short(const GdnScanArgs& a, int dtype, cudaStream_t st);
 // decode step (t = 1): conv + gates + l2norm + delta rule + gated norm in one kernel (needs hk == hv)
 int launch_gdn_decode(const GdnConvArgs& ca, const GdnScanArgs& a, int dtype, cudaStream_t st);
 int launch_gdn_chunk(const GdnScanArgs& a, int dtype, cudaStream_t st);
