@@ -236,14 +236,6 @@ int capture_rows(duo_engine* e, int kind, int l, const void* src, int dtype, int
   return DUO_OK;
 }
 
-bool short_scan_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("DUO_SHORT_SCAN");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 bool fused_norm_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("DUO_FUSED_NORM");
@@ -323,11 +315,9 @@ int forward_impl(duo_engine* e, const int32_t* ids_dev, int row_base, int rows, 
         PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_decode(ca, sa, act, st));
       } else {
         PROF_TRY(DUO_PROF_GDN_CONV, launch_gdn_conv(ca, act, st));
-        // prefill of the 16-bit engines: up to 16 tokens per row token by token (gdn_short_kernel), longer calls the
-        // chunked tensor-core scan; the f32 engine: the recurrent form
-        if (act != DUO_F32 && T > 1 && T <= 16 && short_scan_enabled())
-          PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_short(sa, act, st));  // a few tokens per row: token by token
-        else if (act != DUO_F32 && T > 1) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
+        // prefill of the 16-bit engines: launch_gdn_chunk (up to 16 tokens per row token by token in registers,
+        // longer calls the chunked tensor-core scan); the f32 engine: the recurrent form
+        if (act != DUO_F32 && T > 1) PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_chunk(sa, act, st));
         else PROF_TRY(DUO_PROF_GDN_SCAN, launch_gdn_recurrent(sa, act, st));
       }
       out_k = e->vd;

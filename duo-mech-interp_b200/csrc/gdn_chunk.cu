@@ -613,10 +613,22 @@ static bool chunk_tc_enabled() {
   return on;
 }
 
+static bool short_scan_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("DUO_SHORT_SCAN");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int launch_gdn_chunk(const GdnScanArgs& a, int dtype, cudaStream_t st) {
   if (a.b == 0 || a.t == 0) return DUO_OK;
   if (a.dk != 128 || a.dv != 128) return fail(DUO_EINVAL, "gdn_chunk: needs dk = dv = 128");
   if (a.hq <= 0 || a.h % a.hq) return fail(DUO_EINVAL, "gdn_chunk: value heads must be a multiple of q/k heads");
+  // up to 16 tokens per row (16-bit, no l2norm option): token by token with the state in registers, which beats a
+  // mostly empty 64-token chunk (DUO_SHORT_SCAN=0 keeps the chunk kernels)
+  if (a.t <= 16 && !a.l2norm_qk && (dtype == DUO_BF16 || dtype == DUO_F16) && short_scan_enabled())
+    return launch_gdn_short(a, dtype, st);
   // 16-bit inputs without the l2norm option: the tcgen05 kernel (no workspace); DUO_CHUNK_TC=0 keeps the warp-level
   // two-kernel form, which also serves f32 inputs and l2norm_qk
   if (chunk_tc_enabled() && gdn_chunk_tc_eligible(a, dtype)) return launch_gdn_chunk_tc(a, dtype, st);
