@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(256) gdn_conv_kernel(GdnConvArgs a) {
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         const float* wj = w[half * 4 + j];
-        v[half * 4 + j] = silu_t<T>(wj[0] * xv[0][j] + wj[1] * xv[1][j] + wj[2] * xv[2][j] + wj[3] * xv[3][j]);
+        v[half * 4 + j] = silu_bf<T>(wj[0] * xv[0][j] + wj[1] * xv[1][j] + wj[2] * xv[2][j] + wj[3] * xv[3][j]);
       }
     }
     if (norm) {
@@ -340,8 +340,9 @@ int launch_gdn_conv(const GdnConvArgs& a, int dtype, cudaStream_t st) {
   if (a.rows == 0 || a.t == 0) return DUO_OK;
   if (a.dk != 128 || a.dv != 128 || a.ks != CONV_KS) return fail(DUO_EINVAL, "gdn_conv: needs dk = dv = 128, ks = 4");
   const int conv_dim = 2 * a.hk * a.dk + a.hv * a.dv;
-  // the TMA-fed form for 16-bit projections whose rows are 16-byte aligned and at least one box (64 token rows) tall
-  if (dtype != DUO_F32 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.w % 8 == 0 && (long)a.rows * a.t >= CONV_TT) {
+  // the TMA-fed form for 16-bit projections whose rows are 16-byte aligned, with at least one box (64 tokens) per row:
+  // shorter rows would stream a mostly unused box per tile (the register-staged kernel loads only their tokens)
+  if (dtype != DUO_F32 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.w % 8 == 0 && a.t >= CONV_TT) {
     CUtensorMap tmy;
     DUO_TRY(make_tmap_plain(&tmy, a.y, dtype, (long)a.rows * a.t, a.w, a.w, CONV_TT, 128));
     unsigned* fault = tc_fault_ptr();

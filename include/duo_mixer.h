@@ -124,8 +124,8 @@ int duo_rmsnorm(const float* x, int m, int d, const float* w, float eps, int off
  * place), then SiLU and the l2norm (eps 1e-6) of every q and k head -> qkv [b * t, conv_dim] (same dtype as y);
  * beta = sigmoid(b), g = -exp(a_log) * softplus(a + dt_bias) -> beta, g [b * t, hv] f32.  dk = dv = 128.
  * Replaces `conv` + `convState` (engine/kernels_qwen35.js:129-178) and the gate and l2norm prep of `delta`
- * (kernels_qwen35.js:208-229).  16-bit projections whose rows are 16-byte aligned and that span at least 64 token
- * rows take the TMA-fed kernel, the rest the register-staged one. */
+ * (kernels_qwen35.js:208-229).  16-bit projections whose rows are 16-byte aligned, called with at least 64 tokens
+ * per row, take the TMA-fed kernel, the rest the register-staged one. */
 int duo_gdn_conv_fwd(const void* y, int dtype, int w, const float* conv_w, float* conv_state, const float* a_log,
                      const float* dt_bias, void* qkv, float* g, float* beta, int b, int t, int hk, int hv, int dk,
                      int dv, duo_stream stream);
