@@ -265,6 +265,54 @@ def test_generate_graph_replay_equals_direct(tiny, act, rows):
     assert ops.fault_status() == 0
 
 
+_FUSED_NORM_SCRIPT = """
+import sys
+import numpy as np
+import torch
+sys.path[:0] = sys.argv[2:]
+from tiny import TINY, tiny_state_dict
+from test_gpu_model import duo_cfg_from_tiny
+from duo import Model, from_state_dict
+sd, types = tiny_state_dict()
+W = from_state_dict({k: torch.from_numpy(v) for k, v in sd.items()}, duo_cfg_from_tiny(types, "f32"))
+rows, T = 4, 4800
+ids = torch.randint(0, TINY["vocab"], (rows * T,), generator=torch.Generator().manual_seed(21))
+m = Model(duo_cfg_from_tiny(types, "bf16"), W).alloc(rows=rows, max_len=T + 4, max_t=T, max_tokens=rows * T)
+m.forward(ids, 0, rows, T)
+first = m.logits_all().cpu().numpy()
+m.step([1, 2, 3, 4])
+np.save(sys.argv[1], np.stack([first, m.logits_all().cpu().numpy()]))
+"""
+
+
+def test_fused_prefill_norm_equals_separate_norm(tmp_path):
+    """A bf16 prefill large enough for the persistent GEMMs to carry the RMSNorms (4 rows x 4800 tokens of the tiny
+    model: 150 tiles of 128 x 256 per H-wide projection) against the same forward with every norm its own launch
+    (DUO_FUSED_NORM=0, a second process): both round the norm's input to bf16 once, at different points, so their
+    logits agree within the bf16 bound."""
+    import os
+    import subprocess
+    import sys as _sys
+    import numpy as np
+    from conftest import GOLDEN, PKG, ROOT
+    script = tmp_path / "run.py"
+    script.write_text(_FUSED_NORM_SCRIPT)
+    tests_dir = os.path.dirname(os.path.abspath(__file__))
+    out = {}
+    for name, env_val in (("fused", None), ("separate", "0")):
+        env = dict(os.environ)
+        env.pop("DUO_FUSED_NORM", None)
+        if env_val is not None:
+            env["DUO_FUSED_NORM"] = env_val
+        dst = tmp_path / f"{name}.npy"
+        r = subprocess.run([_sys.executable, str(script), str(dst), tests_dir, GOLDEN, PKG, ROOT], env=env,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        out[name] = torch.from_numpy(np.load(dst))
+    for step in range(2):
+        assert rel_max(out["fused"][step], out["separate"][step]) < TOL16, step
+
+
 @pytest.mark.parametrize("act", ["f16", "bf16"])
 def test_greedy_from_lm_head_epilogue(tiny, act):
     """More than 8 rows on the tensor-core engine: argmax_all and generate take the LM head's argmax epilogue (no
